@@ -66,3 +66,391 @@ def synth_case(B, Hq, Hk, S, D, rho, seed=0, *, device="cpu", dtype=torch.float3
     v = synth_stream(B, Hk, S, D, rho, 3 * seed + 1, device=device, dtype=dtype)
     q = synth_query(B, Hq, D, 3 * seed + 2, device=device, dtype=dtype)
     return k, v, q
+
+
+# --------------------------------------------------------------------------
+# Benchmark driver.
+#
+# Workload (config 2 of the spec, the one the metric is quoted on): a
+# Qwen3-8B-shaped decode step -- 36 layers, batch 16 per GPU, Hq=32, Hkv=8,
+# D=128, context 32768 archived tokens + a raw tail of 5, bf16 K/V archived
+# with the jpeg codec r=8, K=4, int8 codes + fp32 scales.  One step = one
+# split-K decode-attention launch per layer over the whole archive; tokens/s
+# = sequences in the batch / step time.  The archive (about 20 GB per GPU) is
+# far larger than L2, so no L2 flush is needed between steps.
+#
+# N GPUs: one process per GPU; every GPU owns its own batch of 16 sequences
+# (weak scaling: the (batch, KV head) units are independent, there is no
+# data-path collective).
+# --------------------------------------------------------------------------
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = ("decode-attn tokens/s & achieved HBM GB/s (% of peak) on int8 DCT KV, "
+          "1/2/4/8 B200")
+CFG2 = dict(layers=36, B=16, Hq=32, Hk=8, D=128, S=32768, tail=5, r=8, K=4, rho=0.95)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def attn_bytes(B, Hq, Hk, D, n, K, tail, code_b=1, scale_b=4, io_b=2):
+    """Algorithmic bytes of one decode-attention launch: K and V codes and
+    scales, the raw tail, q and the output (each read or written once)."""
+    return (2 * B * Hk * n * K * D * code_b + 2 * B * Hk * n * K * scale_b
+            + 2 * B * Hk * tail * D * io_b + 2 * B * Hq * D * io_b)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the attention kernel from the committed ncu
+    summary (profiles/attn_decode_cfg2.json), or None."""
+    p = ROOT / "profiles" / "attn_decode_cfg2.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms on the given GPUs (read-only query)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.t0 = None
+
+    def start(self):
+        try:
+            self.t0 = time.time()
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ",".join(map(str, self.gpus)),
+                 f"--query-gpu=timestamp,{self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self, t_begin, t_end):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        rows = []
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                ts = time.mktime(time.strptime(f[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                rows.append((ts, float(f[2]), float(f[3]), f[6:10]))
+            except Exception:
+                continue
+        if not rows:
+            return None
+        inside = [x for x in rows if t_begin - 1.0 <= x[0] <= t_end + 1.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for x in inside for n, v in zip(names, x[3]) if v == "Active"})
+        return {"sm_mhz": statistics.median(x[1] for x in inside),
+                "sm_max_mhz": max(x[2] for x in inside), "reasons": reasons,
+                "samples": len(inside)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif n_gpus > 1:
+        raise SystemExit("--gpus N > 1 runs under torchrun (one process per GPU)")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_layers(cfg, rank, device):
+    """Archive every layer's synthetic K/V through the product's append path
+    (the jpeg int8 archive kernel); returns [(k_stream, v_stream, q)]."""
+    import flashcodec_b200 as fc
+    layers = []
+    for L in range(cfg["layers"]):
+        seed = 1000 * rank + L
+        k, v, q = synth_case(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"],
+                             cfg["rho"], seed, device=device, dtype=torch.bfloat16)
+        c = fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"], quant_bits=8)
+        ks, vs = fc._CodecStream(c), fc._CodecStream(c)
+        ks.append(k)
+        del k
+        vs.append(v)
+        del v
+        layers.append((ks, vs, q))
+    torch.cuda.synchronize()
+    return layers
+
+
+def cpu_sample_from(layers, cfg, b_sample=1):
+    """Host copy of one layer's archive for b_sample sequences (oracle input)."""
+    ks, vs, q = layers[0]
+    n = ks.n_blocks
+    out = {}
+    for nm, st in (("k", ks), ("v", vs)):
+        out[nm] = st._coeffs[:b_sample, :, :n].cpu().numpy()
+        out[nm + "s"] = st._scales[:b_sample, :, :n].cpu().numpy()
+        out[nm + "raw"] = st.raw[:b_sample].float().cpu().numpy()
+    out["q"] = q[:b_sample].float().cpu().numpy()
+    return out
+
+
+def time_cpu_baseline(sample, cfg, reps, threads):
+    """Time the oracle's fp32 restatement of the reference's torch attention
+    path on host cores; tokens/s scaled from the sample (b_sample sequences,
+    one layer) to the 36-layer step."""
+    import numpy as np
+    from oracle import oracle as orc
+    import flashcodec_b200 as fc
+    A = fc.block_basis(fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"]),
+                       cfg["r"]).numpy()
+    args = (sample["q"], sample["k"], sample["ks"], sample["v"], sample["vs"], sample["kraw"],
+            sample["vraw"], A)
+    orc.reference_attention_int8(*args)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        orc.reference_attention_int8(*args)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    b = sample["q"].shape[0]
+    nbytes = attn_bytes(b, cfg["Hq"], cfg["Hk"], cfg["D"], sample["k"].shape[2], cfg["K"],
+                        cfg["tail"])
+    return {"value": b / (cfg["layers"] * t), "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": (f"one layer, batch {b} of {cfg['B']}, all {cfg['Hk']} KV heads, full "
+                       f"context; median of {reps} calls of "
+                       f"oracle.reference_attention_int8 (numpy: fp32 dequantize + fp32 BLAS) "
+                       f"= {t * 1e3:.1f} ms ({nbytes / t / 1e9:.2f} GB/s of compressed "
+                       f"bytes); tokens/s = batch / (36 layers x time)")}
+
+
+def run_reference(args, cfg):
+    """--impl reference: the reference algorithm's CPU implementation (the
+    oracle port) on the host cores, same metric/config/unit."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    b = 1
+    k, v, q = synth_case(b, cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"], cfg["rho"],
+                         0, dtype=torch.bfloat16)
+    import flashcodec_b200 as fc
+    basis = fc.dct_basis(cfg["r"], cfg["K"]).numpy()
+    n = cfg["S"] // cfg["r"]
+    rows = {}
+    for nm, x in (("k", k), ("v", v)):
+        xn = x.float().numpy()
+        coef = orc.jpeg_encode(xn[:, :, :n * cfg["r"]], cfg["r"], cfg["K"], basis, "bf16")
+        rows[nm], rows[nm + "s"] = orc.jpeg_quantize(coef, "bf16")
+        rows[nm + "raw"] = xn[:, :, n * cfg["r"]:]
+    A = basis[:cfg["K"], :cfg["r"]].T.copy()
+    call = (q.float().numpy(), rows["k"], rows["ks"], rows["v"], rows["vs"], rows["kraw"],
+            rows["vraw"], A)
+    for _ in range(args.warmup):
+        orc.reference_attention_int8(*call)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.reference_attention_int8(*call)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = b / (cfg["layers"] * dt)
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt * cfg["layers"] * cfg["B"] / b * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic",
+            "config": workload_config(cfg, world),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                             "kind": "port",
+                             "sample": (f"each step: one layer, batch {b} of {cfg['B']}, all "
+                                        f"{cfg['Hk']} KV heads, full context, "
+                                        "oracle.reference_attention_int8 (numpy: fp32 dequantize + fp32 BLAS); "
+                                        "tokens/s = batch / (36 layers x step time); "
+                                        "ms_per_step scaled to the full 36-layer batch-16 step")},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(cfg, world):
+    return {"workload": ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K "
+                         "decode-attention launch per layer over the int8 DCT archive"),
+            "layers": cfg["layers"], "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
+            "Hq": cfg["Hq"], "Hkv": cfg["Hk"], "head_dim": cfg["D"], "context": cfg["S"],
+            "raw_tail": cfg["tail"], "codec": f"jpeg r={cfg['r']} K={cfg['K']} int8, fp32 scales",
+            "kv_dtype": "bf16", "parallelism": f"batch-sharded x{world} (no collective)",
+            "l2": "no flush: the archive read each step (~20 GB per GPU) is >100x L2"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="flashcodec_b200", choices=["flashcodec_b200", "reference"])
+    ap.add_argument("--layers", type=int, default=CFG2["layers"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = dict(CFG2, layers=args.layers)
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as K
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layers = build_layers(cfg, rank, dev)
+    n = layers[0][0].n_blocks
+    per_launch = attn_bytes(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"], n, cfg["K"], cfg["tail"])
+    outs = [torch.empty_like(q) for _, _, q in layers]
+
+    def step():
+        for i, (ks, vs, q) in enumerate(layers):
+            outs[i] = fc.codec_decode_attention(q, ks, vs)
+
+    for _ in range(args.warmup):
+        step()
+    sampler = ClockSampler(list(range(max(world, 1)))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    stream = torch.cuda.current_stream(dev)
+    # one event pair around every attention launch of the timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps * len(layers))]
+    barrier(world)
+    t_wall0 = time.time()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    j = 0
+    for _ in range(args.steps):
+        for i, (ks, vs, q) in enumerate(layers):
+            ev[j][0].record(stream)
+            outs[i] = fc.codec_decode_attention(q, ks, vs)
+            ev[j][1].record(stream)
+            j += 1
+    end.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    barrier(world)
+    ms = start.elapsed_time(end) / args.steps
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    ms_max = max_over_ranks(ms, world)
+    kern_max = max_over_ranks(kern_ms, world)
+    clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
+    assert K.attn_status(dev) == 0, "a bounded wait in the attention kernel gave up"
+
+    # end to end through the public API with host buffers: H2D of every
+    # layer's query from pinned memory, the attention calls, D2H of outputs
+    qh = torch.stack([q for _, _, q in layers]).cpu().pin_memory()
+    oh = torch.empty_like(qh).pin_memory()
+    qd = torch.empty_like(qh, device=dev)
+    for _ in range(2):
+        qd.copy_(qh, non_blocking=True)
+        for i, (ks, vs, _) in enumerate(layers):
+            outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
+        oh.copy_(torch.stack(outs), non_blocking=True)
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, args.steps // 3)
+    e_start.record(stream)
+    for _ in range(e_steps):
+        qd.copy_(qh, non_blocking=True)
+        for i, (ks, vs, _) in enumerate(layers):
+            outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
+        oh.copy_(torch.stack(outs), non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e_steps, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        cpu = time_cpu_baseline(cpu_sample_from(layers, cfg), cfg, reps=5, threads=threads)
+
+    if rank == 0:
+        peak, kind = measured_peaks()
+        achieved = per_launch / (kern_max * 1e-3) / 1e9
+        traffic = ncu_traffic()
+        line = {
+            "metric": METRIC, "value": world * cfg["B"] / (ms_max * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": workload_config(cfg, world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": kind,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": per_launch,
+                         "kernel_ms": kern_max},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * cfg["B"] / (e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": qh.numel() * qh.element_size(),
+                    "d2h_bytes_per_step": oh.numel() * oh.element_size(),
+                    "ms_per_step": e_ms},
+            "gpu_launches": args.steps * len(layers),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.path.insert(0, str(ROOT))
+    main()

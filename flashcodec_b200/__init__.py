@@ -1,0 +1,29 @@
+"""flashcodec_b200 -- B200-native (sm_100a) implementation of flashcodec's
+compressed-KV hot path, with flashcodec's Python API.
+
+KV layout (B, H, S, D), compression along the sequence axis (dim=-2):
+- mode="jpeg": blockwise orthonormal DCT-II, keep K of r coefficients,
+  optionally int8 with a per-(block, frequency) scale;
+- mode="png": per-block anchor + fp32 first-order deltas, Top-M pruning.
+Decode attention runs directly on the compressed archive.
+
+All arithmetic runs in hand-written CUDA kernels (libflashcodec_sm100.so,
+C ABI in include/flashcodec_b200.h).  CUDA tensors only: there is no CPU
+implementation in this package.
+"""
+
+from .attention import block_basis, codec_decode_attention
+from .cache import CodecKVCache, _CodecStream, make_codec
+from .codecs import (JPEGCodec, PNGCodec, dct_basis, dct_compress, dct_decompress,
+                     dequantize_coeffs, png_filter, png_reconstruct, quantize_coeffs)
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "CodecKVCache", "make_codec", "JPEGCodec", "PNGCodec",
+    "codec_decode_attention", "block_basis",
+    "dct_basis", "dct_compress", "dct_decompress",
+    "quantize_coeffs", "dequantize_coeffs",
+    "png_filter", "png_reconstruct",
+    "__version__",
+]

@@ -1,0 +1,193 @@
+"""Tensor-level wrappers around the C ABI (one function per entry point).
+
+Every wrapper checks that its tensors live on a CUDA device, passes data
+pointers, element strides and the current CUDA stream of that device, and maps
+a nonzero status to an exception.  No wrapper computes anything itself.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+
+DTYPE_CODE = {torch.float32: _lib.FC_F32, torch.bfloat16: _lib.FC_BF16,
+              torch.float16: _lib.FC_F16, torch.int8: _lib.FC_I8}
+
+
+def require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "flashcodec_b200 runs on CUDA devices only (got a tensor on "
+                f"{t.device}); there is no CPU implementation")
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def as_bhsd(x: torch.Tensor) -> torch.Tensor:
+    """View (..., S, D) as (B, H, S, D) with unit stride on D (copying only
+    when the layout cannot be expressed)."""
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if x.dim() == 4:
+        return x
+    if x.dim() == 2:
+        return x[None, None]
+    if x.dim() == 3:
+        return x[None]
+    lead = math.prod(x.shape[:-2])
+    return x.reshape(1, lead, x.shape[-2], x.shape[-1])
+
+
+def _s(t, *dims):
+    return [t.stride(d) for d in dims]
+
+
+# ----------------------------------------------------------------- jpeg codec
+def jpeg_encode(x: torch.Tensor, basis: torch.Tensor, r: int, k: int, out: torch.Tensor,
+                scales: torch.Tensor | None = None, err: torch.Tensor | None = None) -> None:
+    """x (B,H,S,D) -> out (B,H,n,k,D) [int8 codes with scales (B,H,n,k,1) | coefficients]."""
+    require_cuda(x, basis, out, scales)
+    B, H, S, D = x.shape
+    if (scales is None) != (out.dtype != torch.int8):
+        raise ValueError("int8 output needs scales; float output takes none")
+    st = _stream(x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().fc_jpeg_encode(
+            _p(x), dtype_code(x), B, H, S, D, *_s(x, 0, 1, 2),
+            _p(basis), r, k,
+            _p(out), *_s(out, 0, 1, 2, 3),
+            _p(scales), dtype_code(scales) if scales is not None else 0,
+            *(_s(scales, 0, 1, 2) if scales is not None else (0, 0, 0)),
+            _p(err), st)
+    _lib.check(rc, "jpeg_encode")
+
+
+def jpeg_decode(coef: torch.Tensor, scales: torch.Tensor | None, basis: torch.Tensor, r: int,
+                out: torch.Tensor, out_len: int) -> None:
+    """coef (B,H,n,k,D) [+ scales (B,H,n,k,1)] -> out (B,H,>=out_len,D)."""
+    require_cuda(coef, scales, basis, out)
+    B, H, n, k, D = coef.shape
+    st = _stream(coef.device)
+    with torch.cuda.device(coef.device):
+        rc = _lib.load().fc_jpeg_decode(
+            _p(coef), dtype_code(coef), B, H, n, D, k, *_s(coef, 0, 1, 2, 3),
+            _p(scales), dtype_code(scales) if scales is not None else 0,
+            *(_s(scales, 0, 1, 2) if scales is not None else (0, 0, 0)),
+            _p(basis), r, _p(out), dtype_code(out), out_len, *_s(out, 0, 1, 2), st)
+    _lib.check(rc, "jpeg_decode")
+
+
+# ------------------------------------------------------------------ png codec
+def png_encode(x: torch.Tensor, r: int, keep_m: int, deltas: torch.Tensor,
+               anchors: torch.Tensor) -> None:
+    """x (B,H,S,D) -> deltas (B,H,n,r-1,D) fp32, anchors (B,H,n,D) in x.dtype."""
+    require_cuda(x, deltas, anchors)
+    B, H, S, D = x.shape
+    st = _stream(x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().fc_png_encode(
+            _p(x), dtype_code(x), B, H, S, D, *_s(x, 0, 1, 2), r, keep_m,
+            _p(deltas), *_s(deltas, 0, 1, 2, 3), _p(anchors), *_s(anchors, 0, 1, 2), st)
+    _lib.check(rc, "png_encode")
+
+
+def png_decode(deltas: torch.Tensor, anchors: torch.Tensor, out: torch.Tensor,
+               out_len: int) -> None:
+    """deltas (B,H,n,r-1,D) fp32 + anchors (B,H,n,D) -> out (B,H,>=out_len,D)."""
+    require_cuda(deltas, anchors, out)
+    B, H, n, rm1, D = deltas.shape
+    st = _stream(deltas.device)
+    with torch.cuda.device(deltas.device):
+        rc = _lib.load().fc_png_decode(
+            _p(deltas), *_s(deltas, 0, 1, 2, 3), _p(anchors), dtype_code(anchors),
+            *_s(anchors, 0, 1, 2), B, H, n, rm1 + 1, D, _p(out), out_len, *_s(out, 0, 1, 2), st)
+    _lib.check(rc, "png_decode")
+
+
+# ------------------------------------------------------------------ attention
+_workspaces: dict = {}
+
+
+def attn_workspace_bytes(B, Hq, Hk, D, n_blocks, s, r, n_raw) -> int:
+    return int(_lib.load().fc_decode_attn_workspace_size(B, Hq, Hk, D, n_blocks, s, r, n_raw))
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised workspace cached per (device, stream).  The kernel
+    leaves its counters at zero, so the buffer is reused across calls issued
+    on the same stream."""
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def reset_workspace(device: torch.device) -> None:
+    """Zero the cached workspace of the current stream (after a failed call)."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    if key in _workspaces:
+        _workspaces[key].zero_()
+
+
+def attn_status(device: torch.device) -> int:
+    """The workspace status word of the current stream (synchronises)."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _workspaces.get(key)
+    return 0 if ws is None else int(ws[:4].view(torch.int32).item())
+
+
+def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
+                ws: torch.Tensor | None = None) -> None:
+    """q (B,Hq,1,D); krows/vrows (B,Hk,n,s,D) or None; k/vscales (B,Hk,n,s,1)
+    or None; kraw/vraw (B,Hk,t,D) or None; A (r,s) fp32; out (B,Hq,1,D)."""
+    require_cuda(q, krows, vrows, kscales, vscales, kraw, vraw, A, out)
+    B, Hq, _, D = q.shape
+    n = krows.shape[2] if krows is not None else 0
+    s = krows.shape[3] if krows is not None else 1
+    r = A.shape[0] if A is not None else 1
+    Hk = (krows if krows is not None else kraw).shape[1]
+    t = kraw.shape[2] if kraw is not None else 0
+    need = attn_workspace_bytes(B, Hq, Hk, D, n, s, r, t)
+    if ws is None:
+        ws = workspace(q.device, need)
+    z = (0, 0, 0, 0)
+    st = _stream(q.device)
+    with torch.cuda.device(q.device):
+        rc = _lib.load().fc_decode_attn(
+            _p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1),
+            Hk, n, s, r, dtype_code(krows) if krows is not None else 0,
+            _p(krows), *(_s(krows, 0, 1, 2, 3) if krows is not None else z),
+            _p(vrows), *(_s(vrows, 0, 1, 2, 3) if vrows is not None else z),
+            _p(kscales), *(_s(kscales, 0, 1, 2) if kscales is not None else z[:3]),
+            _p(vscales), *(_s(vscales, 0, 1, 2) if vscales is not None else z[:3]),
+            dtype_code(kscales) if kscales is not None else 0,
+            _p(kraw), *(_s(kraw, 0, 1, 2) if kraw is not None else z[:3]),
+            _p(vraw), *(_s(vraw, 0, 1, 2) if vraw is not None else z[:3]),
+            dtype_code(kraw) if kraw is not None else 0, t,
+            _p(A), float(scale),
+            _p(out), dtype_code(out), out.stride(0), out.stride(1),
+            _p(ws), ws.numel(), st)
+    if rc != _lib.FC_OK:
+        reset_workspace(q.device)
+    _lib.check(rc, "decode_attn")

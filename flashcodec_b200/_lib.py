@@ -1,0 +1,101 @@
+"""ctypes binding of libflashcodec_sm100.so (include/flashcodec_b200.h).
+
+The shared library is built in-tree by ``python -m flashcodec_b200.build``.
+There is no fallback: if the library is missing or cannot be loaded every
+kernel call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libflashcodec_sm100.so"
+
+FC_OK, FC_EINVAL, FC_ECUDA, FC_ERANGE, FC_ENOTSUP = 0, 1, 2, 3, 4
+FC_F32, FC_BF16, FC_F16, FC_I8 = 0, 1, 2, 3
+
+# exported symbols, in header order (tests check the library exports them all)
+SYMBOLS = ("fc_version", "fc_last_error_string", "fc_jpeg_encode", "fc_jpeg_decode",
+           "fc_png_encode", "fc_png_decode", "fc_decode_attn_workspace_size",
+           "fc_decode_attn")
+
+_I64, _I32, _P, _F32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float
+_SIGS = {
+    "fc_version": ([], ctypes.c_char_p),
+    "fc_last_error_string": ([], ctypes.c_char_p),
+    "fc_jpeg_encode": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32, _I32,
+                        _P, _I64, _I64, _I64, _I64, _P, _I32, _I64, _I64, _I64, _P, _P], _I32),
+    "fc_jpeg_decode": ([_P, _I32, _I64, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _I64,
+                        _P, _I32, _I64, _I64, _I64, _P, _I32, _P, _I32, _I64, _I64, _I64,
+                        _I64, _P], _I32),
+    "fc_png_encode": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
+                       _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P], _I32),
+    "fc_png_decode": ([_P, _I64, _I64, _I64, _I64, _P, _I32, _I64, _I64, _I64,
+                       _I64, _I64, _I64, _I32, _I64, _P, _I64, _I64, _I64, _I64, _P], _I32),
+    "fc_decode_attn_workspace_size": ([_I64, _I64, _I64, _I64, _I64, _I32, _I32, _I64],
+                                      ctypes.c_size_t),
+    "fc_decode_attn": ([_P, _I32, _I64, _I64, _I64, _I64, _I64,
+                        _I64, _I64, _I32, _I32, _I32,
+                        _P, _I64, _I64, _I64, _I64,
+                        _P, _I64, _I64, _I64, _I64,
+                        _P, _I64, _I64, _I64,
+                        _P, _I64, _I64, _I64,
+                        _I32,
+                        _P, _I64, _I64, _I64,
+                        _P, _I64, _I64, _I64,
+                        _I32, _I64,
+                        _P, _F32,
+                        _P, _I32, _I64, _I64,
+                        _P, ctypes.c_size_t, _P], _I32),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class FlashCodecError(RuntimeError):
+    """A kernel call returned a nonzero status (see include/flashcodec_b200.h)."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(msg)
+        self.status = status
+
+
+def load(path: Path | str | None = None) -> ctypes.CDLL:
+    """Load the kernel library (once).  Raises RuntimeError if it is absent."""
+    global _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p.name} is not built; run `python -m flashcodec_b200.build` "
+                "(flashcodec_b200 has no non-CUDA implementation)")
+        lib = ctypes.CDLL(str(p))
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    """Map a C status to the exception types the reference raises."""
+    if status == FC_OK:
+        return
+    msg = load().fc_last_error_string().decode(errors="replace") or what
+    if status == FC_EINVAL:
+        raise ValueError(msg)
+    if status == FC_ENOTSUP:
+        raise NotImplementedError(msg)
+    raise FlashCodecError(status, msg)
+
+
+def version() -> str:
+    return load().fc_version().decode()

@@ -1,0 +1,808 @@
+// Coefficient-domain split-K decode attention (one query token) over a
+// flashcodec archive: int8 DCT codes + per-(block, frequency) scales, plain
+// coefficients, or png [anchor; deltas] rows, plus a raw tail.
+//
+// Work decomposition: one CTA per (batch, KV head, query-head group, split).
+// A split owns a contiguous range ("chunk") of archived blocks of one
+// (batch, KV head) stream and serves every query head of the GQA group from
+// the same bytes, so each code byte leaves HBM exactly once per step.
+//
+// Per CTA, two passes over the chunk (no online rescaling in the inner loop):
+//   1. K rows:  s[row][g] = scale_row * (q_g . code_row)       (fp32, warp
+//      lanes span D, a shuffle reduction closes each row)
+//      logits[pos][g] = log2(e) * softmax_scale * sum_j A[p][j] s[blk*s+j][g]
+//   2. chunk max m_g, p = 2^(logit - m_g), l_g = sum p,
+//      w[row][g] = vscale_row * sum_p p[blk*r+p][g] A[p][j]
+//   3. V rows:  acc[g][d] += w[row][g] * code_row[d]
+// The raw tail (< r tokens at full precision) joins the last split.
+// Partial (m, l, acc) of every split go to the caller's workspace; the split
+// that finishes last (atomic ticket) merges them with a log-sum-exp reduction
+// and writes the output, so one launch does the whole attention and no CTA
+// ever waits for another.
+//
+// When the archive rows of a stream are contiguous (the cache layout
+// (B, H, capacity, s, D)), tiles of TB blocks are staged into a ring of
+// shared-memory buffers with 1D bulk async copies (cp.async.bulk, completion
+// on an mbarrier) issued NST tiles ahead; V tiles stream in while the softmax
+// runs.  Every mbarrier wait is bounded: on timeout the CTA records an error
+// code in the workspace header and exits.
+#include <math.h>
+
+#include <algorithm>
+#include <atomic>
+
+#include "fc_common.cuh"
+
+namespace fc {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kStages = 4;            // bulk-copy ring depth
+constexpr int kStageBytes = 8192;     // bytes per ring buffer
+constexpr int kMaxRS = 64;            // r, s <= 64
+constexpr int kMaxD = 256;
+constexpr int kTargetChunk = 128;     // blocks per split (upper target)
+constexpr int kMinChunk = 16;
+constexpr uint64_t kWaitNs = 100000000ull;  // 100 ms bound on any mbarrier wait
+constexpr int kWsHeader = 256;        // workspace bytes before the counters
+constexpr size_t kSmemBudget = 96 * 1024;  // per-CTA shared-memory plan budget
+
+struct AttnArgs {
+    const void *q;
+    int q_dtype;
+    int64_t q_sb, q_sh;
+    int64_t B, Hq, Hk, D, n;
+    int s, r, G, GT, n_groups;
+    const void *krows, *vrows;
+    int64_t k_sb, k_sh, k_sn, k_sj;
+    int64_t v_sb, v_sh, v_sn, v_sj;
+    const void *ksc, *vsc;
+    int sc_dtype;
+    int64_t ks_sb, ks_sh, ks_sn, vs_sb, vs_sh, vs_sn;
+    const void *kraw, *vraw;
+    int raw_dtype;
+    int64_t kr_sb, kr_sh, kr_st, vr_sb, vr_sh, vr_st;
+    int n_raw;
+    const float *A;
+    float scale_log2;  // softmax_scale * log2(e)
+    void *out;
+    int out_dtype;
+    int64_t o_sb, o_sh;
+    int n_split;
+    int chunk;       // blocks per split
+    int tb;          // blocks per bulk tile
+    int lprl;        // log2(lanes per row)
+    int *status;     // workspace header: epoch of the last launch whose wait gave up
+    int epoch;       // this launch's epoch (> 0, increasing)
+    int *cnt;        // per (unit, group) arrival counters
+    float *pm, *pl, *pacc;
+    // shared-memory carve-up (byte offsets)
+    int off_A, off_ksc, off_vsc, off_sc, off_lg, off_red, off_stat, off_ring, off_bar;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// 1D bulk async copy global -> shared, completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait on an mbarrier phase.  Gives up after kWaitNs of wall time,
+// recording this launch's epoch in *status (atomicMax), or as soon as another
+// CTA of the same launch has recorded it.  Returns false when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity, int *status,
+                                                  int epoch) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*reinterpret_cast<volatile int *>(status) == epoch) return false;
+        if (global_ns() - t0 > kWaitNs) {
+            atomicMax(status, epoch);
+            return false;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ kernel
+template <typename RT, int VEC, int NCH, int GT, bool BULK>
+__global__ void __launch_bounds__(kThreads)
+attn_kernel(AttnArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *sA = reinterpret_cast<float *>(smem + a.off_A);
+    float *sks = reinterpret_cast<float *>(smem + a.off_ksc);
+    float *svs = reinterpret_cast<float *>(smem + a.off_vsc);
+    float *ssc = reinterpret_cast<float *>(smem + a.off_sc);
+    float *slg = reinterpret_cast<float *>(smem + a.off_lg);
+    float *sred = reinterpret_cast<float *>(smem + a.off_red);
+    float *sstat = reinterpret_cast<float *>(smem + a.off_stat);
+    unsigned char *ring = smem + a.off_ring;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lpr = 1 << a.lprl, rpw = 32 >> a.lprl;
+    const int li = lane & (lpr - 1), lr = lane >> a.lprl;
+    const int rows_per_pass = kWarps * rpw;
+
+    const int split = blockIdx.x % a.n_split;
+    const int64_t unit = blockIdx.x / a.n_split;  // b * Hk + hk
+    const int gg = blockIdx.y;
+    const int64_t b = unit / a.Hk, hk = unit % a.Hk;
+    const int s = a.s, r = a.r;
+    const int64_t n0 = (int64_t)split * a.chunk;
+    const int nb = (int)max((int64_t)0, min((int64_t)a.chunk, a.n - n0));  // blocks here
+    const int nraw = (split == a.n_split - 1) ? a.n_raw : 0;
+    const int grun = min(GT, a.G - gg * GT);  // live heads in this group
+    const int64_t hq0 = hk * a.G + (int64_t)gg * GT;
+
+    const RT *kbase = static_cast<const RT *>(a.krows) + b * a.k_sb + hk * a.k_sh + n0 * a.k_sn;
+    const RT *vbase = static_cast<const RT *>(a.vrows) + b * a.v_sb + hk * a.v_sh + n0 * a.v_sn;
+    const int64_t row_elems = a.D;  // contiguous row length in the bulk layout
+    const unsigned blk_bytes = (unsigned)(s * a.D * sizeof(RT));
+    const int ntiles = BULK ? (nb + a.tb - 1) / a.tb : 0;
+    const int ttot = 2 * ntiles;
+
+    auto issue = [&](int t) {
+        // tile t < ntiles: K blocks [t*tb, ...); else V blocks
+        const int tt = t < ntiles ? t : t - ntiles;
+        const int blocks = min(a.tb, nb - tt * a.tb);
+        const RT *src = (t < ntiles ? kbase : vbase) + (int64_t)tt * a.tb * s * row_elems;
+        uint64_t *bar = bars + (t % kStages);
+        mbar_expect_tx(bar, blocks * blk_bytes);
+        bulk_g2s(ring + (t % kStages) * kStageBytes, src, blocks * blk_bytes, bar);
+    };
+    // Tiles [0, issued) have been requested (only thread 0 tracks this).  On
+    // an abort, thread 0 waits -- bounded again -- for the copies still in
+    // flight to land before the CTA releases its shared memory.
+    int issued = 0;
+    auto drain = [&](int from) {
+        if (tid != 0) return;
+        for (int u = from; u < issued; u++) {
+            uint64_t *bar = bars + (u % kStages);
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(bar, (u / kStages) & 1) && global_ns() - t0 < kWaitNs) {
+            }
+        }
+    };
+
+    if (BULK && tid == 0) {
+        for (int i = 0; i < kStages; i++) mbar_init(bars + i, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (BULK && tid == 0)
+        for (; issued < min(kStages, ttot); issued++) issue(issued);
+
+    // small per-CTA operands: A, the chunk's scales
+    for (int i = tid; i < r * s; i += kThreads) sA[i] = a.A ? a.A[i] : 0.0f;
+    for (int i = tid; i < nb * s; i += kThreads) {
+        const int blk = i / s, j = i % s;
+        sks[i] = a.ksc ? load_as_f32(a.ksc, b * a.ks_sb + hk * a.ks_sh + (n0 + blk) * a.ks_sn + j,
+                                     a.sc_dtype) : 1.0f;
+        svs[i] = a.vsc ? load_as_f32(a.vsc, b * a.vs_sb + hk * a.vs_sh + (n0 + blk) * a.vs_sn + j,
+                                     a.sc_dtype) : 1.0f;
+    }
+
+    // q for this lane's channels, fp32 registers
+    float qr[GT][NCH][VEC];
+#pragma unroll
+    for (int g = 0; g < GT; g++)
+#pragma unroll
+        for (int c = 0; c < NCH; c++)
+#pragma unroll
+            for (int v = 0; v < VEC; v++) {
+                const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
+                qr[g][c][v] = (g < grun && d < a.D)
+                                  ? load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype)
+                                  : 0.0f;
+            }
+    __syncthreads();
+
+    // ---- dot products of one row with every head's q, reduced over the row's lanes
+    auto row_dot_typed = [&](const RT *p, bool valid, float part[GT]) {
+#pragma unroll
+        for (int g = 0; g < GT; g++) part[g] = 0.0f;
+        if (valid) {
+#pragma unroll
+            for (int c = 0; c < NCH; c++) {
+                const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
+                if (d0 < a.D) {
+                    float x[VEC];
+                    load_vec_f32<RT, VEC>(p + d0, x);
+#pragma unroll
+                    for (int g = 0; g < GT; g++)
+#pragma unroll
+                        for (int v = 0; v < VEC; v++) part[g] = fmaf(qr[g][c][v], x[v], part[g]);
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < GT; g++)
+            for (int off = lpr >> 1; off > 0; off >>= 1)
+                part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+    };
+    auto row_dot_raw = [&](const void *base, int64_t off, bool valid, float part[GT]) {
+#pragma unroll
+        for (int g = 0; g < GT; g++) part[g] = 0.0f;
+        if (valid) {
+#pragma unroll
+            for (int c = 0; c < NCH; c++)
+#pragma unroll
+                for (int v = 0; v < VEC; v++) {
+                    const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
+                    if (d < a.D) {
+                        const float x = load_as_f32(base, off + d, a.raw_dtype);
+#pragma unroll
+                        for (int g = 0; g < GT; g++) part[g] = fmaf(qr[g][c][v], x, part[g]);
+                    }
+                }
+        }
+#pragma unroll
+        for (int g = 0; g < GT; g++)
+            for (int o = lpr >> 1; o > 0; o >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], o);
+    };
+
+    // ------------------------------------------------ pass 1: K rows -> scores
+    const int krows_total = nb * s;
+    int t_cur = 0;  // next ring tile to consume
+    if (BULK) {
+        for (int t = 0; t < ntiles; t++, t_cur++) {
+            const bool ok = mbar_wait_bounded(bars + (t % kStages), (t / kStages) & 1, a.status,
+                                              a.epoch);
+            if (__syncthreads_or(!ok)) { drain(t); return; }
+            const RT *tile = reinterpret_cast<const RT *>(ring + (t % kStages) * kStageBytes);
+            const int trows = min(a.tb, nb - t * a.tb) * s;
+            for (int base = 0; base < trows; base += rows_per_pass) {
+                const int row = base + warp * rpw + lr;
+                const bool valid = row < trows;
+                float part[GT];
+                row_dot_typed(tile + (int64_t)row * row_elems, valid, part);
+                if (valid && li == 0) {
+                    const int grow = t * a.tb * s + row;
+                    const float ks = sks[grow];
+#pragma unroll
+                    for (int g = 0; g < GT; g++) ssc[grow * GT + g] = part[g] * ks;
+                }
+            }
+            __syncthreads();
+            if (tid == 0 && t + kStages < ttot) issue(issued++);
+        }
+    } else {
+        for (int base = 0; base < krows_total; base += rows_per_pass) {
+            const int row = base + warp * rpw + lr;
+            const bool valid = row < krows_total;
+            const int blk = valid ? row / s : 0, j = valid ? row % s : 0;
+            float part[GT];
+            row_dot_typed(kbase + (int64_t)blk * a.k_sn + (int64_t)j * a.k_sj, valid, part);
+            if (valid && li == 0) {
+                const float ks = sks[row];
+#pragma unroll
+                for (int g = 0; g < GT; g++) ssc[row * GT + g] = part[g] * ks;
+            }
+        }
+    }
+    // raw tail rows
+    for (int base = 0; base < nraw; base += rows_per_pass) {
+        const int t = base + warp * rpw + lr;
+        const bool valid = t < nraw;
+        float part[GT];
+        row_dot_raw(a.kraw, b * a.kr_sb + hk * a.kr_sh + (int64_t)t * a.kr_st, valid, part);
+        if (valid && li == 0) {
+#pragma unroll
+            for (int g = 0; g < GT; g++) ssc[(krows_total + t) * GT + g] = part[g];
+        }
+    }
+    __syncthreads();
+
+    // --------------------------------------- logits, chunk max, weights
+    const int npos = nb * r + nraw;
+    const int my_g = tid % GT;  // kThreads is a multiple of GT
+    float tmax = -INFINITY;
+    for (int idx = tid; idx < npos * GT; idx += kThreads) {
+        const int pos = idx / GT;
+        float lg;
+        if (pos < nb * r) {
+            const int blk = pos / r, p = pos % r;
+            lg = 0.0f;
+            for (int j = 0; j < s; j++) lg = fmaf(sA[p * s + j], ssc[(blk * s + j) * GT + my_g], lg);
+        } else {
+            lg = ssc[(krows_total + pos - nb * r) * GT + my_g];
+        }
+        lg *= a.scale_log2;
+        slg[idx] = lg;
+        tmax = fmaxf(tmax, lg);
+    }
+    for (int off = 16; off >= GT; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+    if (lane < GT) sstat[warp * GT + lane] = tmax;
+    __syncthreads();
+    float m_g = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) m_g = fmaxf(m_g, sstat[w * GT + my_g]);
+    float tsum = 0.0f;
+    for (int idx = tid; idx < npos * GT; idx += kThreads) {
+        const float p = exp2f(slg[idx] - m_g);
+        slg[idx] = p;
+        tsum += p;
+    }
+    for (int off = 16; off >= GT; off >>= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
+    __syncthreads();  // everyone has read sstat (max) and written slg
+    if (lane < GT) sstat[kWarps * GT + warp * GT + lane] = tsum;
+    // weights folded back through A and the V scales
+    for (int idx = tid; idx < krows_total * GT; idx += kThreads) {
+        const int row = idx / GT, blk = row / s, j = row % s;
+        float w = 0.0f;
+        for (int p = 0; p < r; p++) w = fmaf(slg[(blk * r + p) * GT + my_g], sA[p * s + j], w);
+        ssc[idx] = w * svs[row];
+    }
+    for (int idx = tid; idx < nraw * GT; idx += kThreads)
+        ssc[krows_total * GT + idx] = slg[nb * r * GT + idx];
+    __syncthreads();
+
+    // ------------------------------------------------ pass 2: V rows -> acc
+    float acc[GT][NCH][VEC];
+#pragma unroll
+    for (int g = 0; g < GT; g++)
+#pragma unroll
+        for (int c = 0; c < NCH; c++)
+#pragma unroll
+            for (int v = 0; v < VEC; v++) acc[g][c][v] = 0.0f;
+
+    auto accum_typed = [&](const RT *p, int wrow) {
+        float w[GT];
+#pragma unroll
+        for (int g = 0; g < GT; g++) w[g] = ssc[wrow * GT + g];
+#pragma unroll
+        for (int c = 0; c < NCH; c++) {
+            const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
+            if (d0 < a.D) {
+                float x[VEC];
+                load_vec_f32<RT, VEC>(p + d0, x);
+#pragma unroll
+                for (int g = 0; g < GT; g++)
+#pragma unroll
+                    for (int v = 0; v < VEC; v++) acc[g][c][v] = fmaf(w[g], x[v], acc[g][c][v]);
+            }
+        }
+    };
+
+    if (BULK) {
+        for (int t = ntiles; t < ttot; t++) {
+            const bool ok = mbar_wait_bounded(bars + (t % kStages), (t / kStages) & 1, a.status,
+                                              a.epoch);
+            if (__syncthreads_or(!ok)) { drain(t); return; }
+            const RT *tile = reinterpret_cast<const RT *>(ring + (t % kStages) * kStageBytes);
+            const int tv = t - ntiles;
+            const int trows = min(a.tb, nb - tv * a.tb) * s;
+            for (int base = 0; base < trows; base += rows_per_pass) {
+                const int row = base + warp * rpw + lr;
+                if (row < trows) accum_typed(tile + (int64_t)row * row_elems, tv * a.tb * s + row);
+            }
+            __syncthreads();
+            if (tid == 0 && t + kStages < ttot) issue(issued++);
+        }
+    } else {
+        for (int base = 0; base < krows_total; base += rows_per_pass) {
+            const int row = base + warp * rpw + lr;
+            if (row < krows_total) {
+                const int blk = row / s, j = row % s;
+                accum_typed(vbase + (int64_t)blk * a.v_sn + (int64_t)j * a.v_sj, row);
+            }
+        }
+    }
+    for (int base = 0; base < nraw; base += rows_per_pass) {
+        const int t = base + warp * rpw + lr;
+        if (t < nraw) {
+            float w[GT];
+#pragma unroll
+            for (int g = 0; g < GT; g++) w[g] = ssc[(krows_total + t) * GT + g];
+            const int64_t off = b * a.vr_sb + hk * a.vr_sh + (int64_t)t * a.vr_st;
+#pragma unroll
+            for (int c = 0; c < NCH; c++)
+#pragma unroll
+                for (int v = 0; v < VEC; v++) {
+                    const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
+                    if (d < a.D) {
+                        const float x = load_as_f32(a.vraw, off + d, a.raw_dtype);
+#pragma unroll
+                        for (int g = 0; g < GT; g++) acc[g][c][v] = fmaf(w[g], x, acc[g][c][v]);
+                    }
+                }
+        }
+    }
+
+    // reduce acc over the row groups of each warp, then over warps
+#pragma unroll
+    for (int g = 0; g < GT; g++)
+#pragma unroll
+        for (int c = 0; c < NCH; c++)
+#pragma unroll
+            for (int v = 0; v < VEC; v++)
+                for (int off = lpr; off < 32; off <<= 1)
+                    acc[g][c][v] += __shfl_xor_sync(0xffffffffu, acc[g][c][v], off);
+    if (lr == 0) {
+#pragma unroll
+        for (int g = 0; g < GT; g++)
+#pragma unroll
+            for (int c = 0; c < NCH; c++)
+#pragma unroll
+                for (int v = 0; v < VEC; v++) {
+                    const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
+                    if (d < a.D) sred[(warp * GT + g) * a.D + d] = acc[g][c][v];
+                }
+    }
+    __syncthreads();
+
+    // per-head (m, l) of this chunk
+    float *s_m = sstat + 2 * kWarps * GT;
+    float *s_l = s_m + GT;
+    if (tid < GT) {
+        float l = 0.0f, m = -INFINITY;
+        for (int w = 0; w < kWarps; w++) {
+            l += sstat[kWarps * GT + w * GT + tid];
+            m = fmaxf(m, sstat[w * GT + tid]);
+        }
+        s_m[tid] = m;
+        s_l[tid] = l;
+    }
+    __syncthreads();
+
+    if (a.n_split == 1) {
+        for (int idx = tid; idx < GT * a.D; idx += kThreads) {
+            const int g = idx / (int)a.D;
+            const int64_t d = idx % a.D;
+            if (g >= grun) continue;
+            float o = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; w++) o += sred[(w * GT + g) * a.D + d];
+            store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, o / s_l[g]);
+        }
+        return;
+    }
+
+    // ---------------------------------------------- partials + last-arriver merge
+    const int64_t grp = unit * a.n_groups + gg;
+    const int64_t slot = grp * a.n_split + split;
+    for (int idx = tid; idx < GT * a.D; idx += kThreads) {
+        const int g = idx / (int)a.D;
+        const int64_t d = idx % a.D;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) o += sred[(w * GT + g) * a.D + d];
+        a.pacc[slot * GT * a.D + idx] = o;
+    }
+    if (tid < GT) {
+        a.pm[slot * GT + tid] = s_m[tid];
+        a.pl[slot * GT + tid] = s_l[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = (atomicAdd(a.cnt + grp, 1) == a.n_split - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // merge: M = max m_i, L = sum l_i 2^(m_i - M), O = sum acc_i 2^(m_i - M) / L
+    float *s_fac = sred;  // reuse: n_split x GT factors
+    if (tid < GT) {
+        float M = -INFINITY;
+        for (int i = 0; i < a.n_split; i++) M = fmaxf(M, __ldcg(a.pm + (grp * a.n_split + i) * GT + tid));
+        float L = 0.0f;
+        for (int i = 0; i < a.n_split; i++) {
+            const int64_t si = (grp * a.n_split + i) * GT + tid;
+            const float f = exp2f(__ldcg(a.pm + si) - M);
+            s_fac[i * GT + tid] = f;
+            L += __ldcg(a.pl + si) * f;
+        }
+        s_l[tid] = L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < GT * a.D; idx += kThreads) {
+        const int g = idx / (int)a.D;
+        const int64_t d = idx % a.D;
+        if (g >= grun) continue;
+        float o = 0.0f;
+        for (int i = 0; i < a.n_split; i++)
+            o = fmaf(__ldcg(a.pacc + ((grp * a.n_split + i) * GT + g) * a.D + d), s_fac[i * GT + g], o);
+        store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, o / s_l[g]);
+    }
+    if (tid == 0) a.cnt[grp] = 0;  // ready for the next launch
+}
+
+// ---------------------------------------------------------------- planning
+// Launch epochs: a positive, increasing tag per call (wraps after 2^31 - 1).
+int next_epoch() {
+    static std::atomic<int> e{0};
+    int v = e.fetch_add(1) + 1;
+    if (v <= 0) {
+        e.store(1);
+        v = 1;
+    }
+    return v;
+}
+
+struct Plan {
+    int GT = 1, n_groups = 1, n_split = 1, chunk = 0, tb = 1, lprl = 5;
+    int vec_mode = 0;  // 0 = generic scalar, 1 = 16-byte vectors, direct; 2 = bulk ring
+    size_t smem = 0, ws = 0;
+    int off_A, off_ksc, off_vsc, off_sc, off_lg, off_red, off_stat, off_ring, off_bar;
+};
+
+inline int pick_gt(int64_t G) {
+    if (G <= 1) return 1;
+    if (G <= 2) return 2;
+    if (G <= 4) return 4;
+    return 8;
+}
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Shared by fc_decode_attn_workspace_size and fc_decode_attn so both agree.
+Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, int r,
+               int64_t n_raw, int es, int vec_mode) {
+    Plan p;
+    const int64_t G = Hq / Hk;
+    p.GT = pick_gt(G);
+    p.n_groups = (int)((G + p.GT - 1) / p.GT);
+    p.vec_mode = vec_mode;
+    if (vec_mode > 0) {
+        const int vec = 16 / es;
+        int lpr = (int)(D / vec);
+        int l = 0;
+        while ((1 << l) < lpr) l++;
+        p.lprl = l;
+    } else {
+        p.lprl = 5;
+    }
+    const int64_t units = B * Hk * p.n_groups;
+    // chunk: enough splits to fill the GPU several times over, each split at
+    // least kMinChunk blocks, at most kTargetChunk (shared-memory bound)
+    if (n == 0) {
+        p.n_split = 1;
+        p.chunk = 0;
+    } else {
+        const int64_t want_ctas = (int64_t)num_sms() * 8;
+        int64_t ns = (want_ctas + units - 1) / units;
+        ns = std::max<int64_t>(1, std::min<int64_t>(ns, (n + kMinChunk - 1) / kMinChunk));
+        int64_t chunk = (n + ns - 1) / ns;
+        chunk = std::min<int64_t>(chunk, kTargetChunk);
+        ns = (n + chunk - 1) / chunk;
+        chunk = (n + ns - 1) / ns;
+        p.n_split = (int)ns;
+        p.chunk = (int)chunk;
+    }
+    // cap the chunk so the per-block shared-memory arrays fit the budget
+    {
+        const size_t fixed = (size_t)r * s * 4 + (size_t)kWarps * p.GT * D * 4 +
+                             (size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4 +
+                             (vec_mode == 2 ? (size_t)kStages * (kStageBytes + 8) : 0) +
+                             (size_t)2 * (n_raw + 1) * p.GT * 4 + 8 * 128;
+        const size_t per_block = ((size_t)2 * s + (size_t)(s + r) * p.GT) * 4;
+        const size_t cap = fixed < kSmemBudget ? (kSmemBudget - fixed) / per_block : 1;
+        if (n > 0 && (size_t)p.chunk > cap) {
+            const int64_t chunk = std::max<int64_t>(1, (int64_t)cap);
+            p.n_split = (int)((n + chunk - 1) / chunk);
+            p.chunk = (int)((n + p.n_split - 1) / p.n_split);
+        }
+    }
+    const int64_t blk_bytes = (int64_t)s * D * es;
+    p.tb = (int)std::max<int64_t>(1, std::min<int64_t>(kStageBytes / blk_bytes, p.chunk > 0 ? p.chunk : 1));
+    // shared memory carve-up
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 128); return (int)o; };
+    const int64_t raw_max = std::max<int64_t>(n_raw, 1);
+    p.off_A = take((size_t)r * s * 4);
+    p.off_ksc = take((size_t)std::max(p.chunk, 1) * s * 4);
+    p.off_vsc = take((size_t)std::max(p.chunk, 1) * s * 4);
+    p.off_sc = take(((size_t)std::max(p.chunk, 1) * s + raw_max) * p.GT * 4);
+    p.off_lg = take(((size_t)std::max(p.chunk, 1) * r + raw_max) * p.GT * 4);
+    p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4, (size_t)p.n_split * p.GT * 4));
+    p.off_stat = take((size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4);
+    p.off_ring = take(vec_mode == 2 ? (size_t)kStages * kStageBytes : 0);
+    p.off_bar = take(vec_mode == 2 ? (size_t)kStages * 8 : 0);
+    p.smem = off;
+    // workspace: header | counters | pm | pl | pacc
+    if (p.n_split > 1) {
+        const size_t slots = (size_t)units * p.n_split;
+        size_t w = kWsHeader;
+        w = align_up(w + (size_t)units * 4, 256);
+        w = align_up(w + slots * p.GT * 4, 256);
+        w = align_up(w + slots * p.GT * 4, 256);
+        w = align_up(w + slots * p.GT * D * 4, 256);
+        p.ws = w;
+    } else {
+        p.ws = kWsHeader;
+    }
+    return p;
+}
+
+int pick_vec_mode(int64_t D, int es, const void *k, const void *v, int64_t k_sb, int64_t k_sh,
+                  int64_t k_sn, int64_t k_sj, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                  int64_t v_sj, int s) {
+    const int vec = 16 / es;
+    if (D % vec != 0) return 0;
+    const int64_t lpr = D / vec;
+    if (lpr > 32 || (lpr & (lpr - 1)) != 0) return 0;
+    auto ok16 = [&](int64_t stride) { return (stride * es) % 16 == 0; };
+    if (k && !aligned(k, 16)) return 0;
+    if (v && !aligned(v, 16)) return 0;
+    if (!(ok16(k_sb) && ok16(k_sh) && ok16(k_sn) && ok16(k_sj) && ok16(v_sb) && ok16(v_sh) &&
+          ok16(v_sn) && ok16(v_sj)))
+        return 0;
+    const bool contig = k_sj == D && k_sn == (int64_t)s * D && v_sj == D && v_sn == (int64_t)s * D;
+    // the bulk ring needs every block's rows to fit one stage buffer
+    const bool fits = (int64_t)s * D * es <= kStageBytes;
+    return (contig && fits) ? 2 : 1;
+}
+
+template <typename RT, int GT>
+int launch_gt(const Plan &p, AttnArgs &args, dim3 grid, cudaStream_t st) {
+    auto setup = [&](auto kern) {
+        if (p.smem > 48 * 1024)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+        kern<<<grid, kThreads, p.smem, st>>>(args);
+    };
+    constexpr int V16 = 16 / (int)sizeof(RT);
+    if (p.vec_mode == 2) setup(attn_kernel<RT, V16, 1, GT, true>);
+    else if (p.vec_mode == 1) setup(attn_kernel<RT, V16, 1, GT, false>);
+    else setup(attn_kernel<RT, 1, kMaxD / 32, GT, false>);
+    return check_launch("decode_attn");
+}
+
+template <typename RT>
+int launch_rt(const Plan &p, AttnArgs &args, dim3 grid, cudaStream_t st) {
+    switch (p.GT) {
+        case 1: return launch_gt<RT, 1>(p, args, grid, st);
+        case 2: return launch_gt<RT, 2>(p, args, grid, st);
+        case 4: return launch_gt<RT, 4>(p, args, grid, st);
+        default: return launch_gt<RT, 8>(p, args, grid, st);
+    }
+}
+
+}  // namespace
+}  // namespace fc
+
+using namespace fc;
+
+extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t Hk, int64_t D,
+                                                int64_t n_blocks, int s, int r, int64_t n_raw) {
+    if (B <= 0 || Hk <= 0 || Hq <= 0 || Hq % Hk != 0 || D <= 0 || s <= 0 || r <= 0) return 0;
+    // the workspace depends on the split plan only, which is the same for
+    // every row dtype with the same vector mode; take the largest
+    size_t w = 0;
+    for (int es : {1, 2, 4})
+        for (int vm : {0, 1, 2})
+            w = std::max(w, make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm).ws);
+    return w;
+}
+
+extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                              int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int s,
+                              int r, int rows_dtype, const void *k_rows, int64_t k_sb,
+                              int64_t k_sh, int64_t k_sn, int64_t k_sj, const void *v_rows,
+                              int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t v_sj,
+                              const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                              const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                              int scale_dtype, const void *k_raw, int64_t kr_sb, int64_t kr_sh,
+                              int64_t kr_st, const void *v_raw, int64_t vr_sb, int64_t vr_sh,
+                              int64_t vr_st, int raw_dtype, int64_t n_raw, const float *A,
+                              float softmax_scale, void *out, int out_dtype, int64_t o_sb,
+                              int64_t o_sh, void *workspace, size_t workspace_bytes,
+                              void *stream) {
+    clear_error();
+    if (B < 0 || Hq <= 0 || Hk <= 0 || D <= 0) { set_error("decode_attn: bad shape"); return FC_EINVAL; }
+    if (Hq % Hk != 0) { set_error("decode_attn: Hq (%lld) must be a multiple of Hk (%lld)", (long long)Hq, (long long)Hk); return FC_EINVAL; }
+    if (D > kMaxD) { set_error("decode_attn: head dim %lld > %d", (long long)D, kMaxD); return FC_ENOTSUP; }
+    if (n_blocks < 0 || n_raw < 0) { set_error("decode_attn: negative length"); return FC_EINVAL; }
+    if (n_blocks > 0 && (s < 1 || s > kMaxRS || r < 1 || r > kMaxRS)) { set_error("decode_attn: need 1 <= s, r <= %d", kMaxRS); return FC_EINVAL; }
+    if (n_raw >= (n_blocks > 0 ? r : kMaxRS + 1)) { set_error("decode_attn: raw tail longer than a block"); return FC_EINVAL; }
+    if (!is_float_dtype(q_dtype) || !is_float_dtype(out_dtype)) { set_error("decode_attn: q/out dtype must be f32/bf16/f16"); return FC_EINVAL; }
+    if (n_blocks > 0 && dtype_size(rows_dtype) == 0) { set_error("decode_attn: bad rows dtype"); return FC_EINVAL; }
+    if (n_blocks > 0 && rows_dtype == FC_I8 && (!k_scales || !v_scales)) { set_error("decode_attn: int8 rows need scales"); return FC_EINVAL; }
+    if ((k_scales || v_scales) && scale_dtype != FC_F32 && scale_dtype != FC_F16) { set_error("decode_attn: scale dtype must be f32 or f16"); return FC_EINVAL; }
+    if (n_raw > 0 && (!k_raw || !v_raw || !is_float_dtype(raw_dtype))) { set_error("decode_attn: raw tail pointers/dtype"); return FC_EINVAL; }
+    if (B == 0) return FC_OK;
+    if (n_blocks == 0 && n_raw == 0) { set_error("decode_attn: empty cache (caller returns zeros)"); return FC_EINVAL; }
+    if (!q || !out || (n_blocks > 0 && (!k_rows || !v_rows || !A))) { set_error("decode_attn: null pointer"); return FC_EINVAL; }
+    if (n_blocks == 0) { s = 1; r = std::max<int>(r, 1); rows_dtype = FC_F32; }
+
+    const int es = dtype_size(rows_dtype);
+    const int vm = n_blocks > 0 ? pick_vec_mode(D, es, k_rows, v_rows, k_sb, k_sh, k_sn, k_sj,
+                                                v_sb, v_sh, v_sn, v_sj, s)
+                                : 0;
+    Plan p = make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm);
+    if (p.smem > 200 * 1024) { set_error("decode_attn: shared memory plan too large"); return FC_ENOTSUP; }
+    if (!workspace || workspace_bytes < p.ws) {
+        set_error("decode_attn: workspace of %zu bytes needed, %zu given", p.ws, workspace_bytes);
+        return FC_ERANGE;
+    }
+    if (!aligned(workspace, 256)) { set_error("decode_attn: workspace must be 256-byte aligned"); return FC_EINVAL; }
+
+    AttnArgs a{};
+    a.q = q; a.q_dtype = q_dtype; a.q_sb = q_sb; a.q_sh = q_sh;
+    a.B = B; a.Hq = Hq; a.Hk = Hk; a.D = D; a.n = n_blocks;
+    a.s = s; a.r = r; a.G = (int)(Hq / Hk); a.GT = p.GT; a.n_groups = p.n_groups;
+    a.krows = k_rows; a.vrows = v_rows;
+    a.k_sb = k_sb; a.k_sh = k_sh; a.k_sn = k_sn; a.k_sj = k_sj;
+    a.v_sb = v_sb; a.v_sh = v_sh; a.v_sn = v_sn; a.v_sj = v_sj;
+    a.ksc = k_scales; a.vsc = v_scales; a.sc_dtype = scale_dtype;
+    a.ks_sb = ks_sb; a.ks_sh = ks_sh; a.ks_sn = ks_sn;
+    a.vs_sb = vs_sb; a.vs_sh = vs_sh; a.vs_sn = vs_sn;
+    a.kraw = k_raw; a.vraw = v_raw; a.raw_dtype = raw_dtype;
+    a.kr_sb = kr_sb; a.kr_sh = kr_sh; a.kr_st = kr_st;
+    a.vr_sb = vr_sb; a.vr_sh = vr_sh; a.vr_st = vr_st;
+    a.n_raw = (int)n_raw;
+    a.A = A;
+    a.scale_log2 = softmax_scale * 1.4426950408889634f;
+    a.out = out; a.out_dtype = out_dtype; a.o_sb = o_sb; a.o_sh = o_sh;
+    a.n_split = p.n_split; a.chunk = p.chunk; a.tb = p.tb; a.lprl = p.lprl;
+    unsigned char *ws = static_cast<unsigned char *>(workspace);
+    a.status = reinterpret_cast<int *>(ws);
+    a.epoch = next_epoch();
+    const int64_t units = B * Hk * p.n_groups;
+    size_t off = kWsHeader;
+    a.cnt = reinterpret_cast<int *>(ws + off);
+    off = align_up(off + (size_t)units * 4, 256);
+    const size_t slots = (size_t)units * p.n_split;
+    a.pm = reinterpret_cast<float *>(ws + off);
+    off = align_up(off + slots * p.GT * 4, 256);
+    a.pl = reinterpret_cast<float *>(ws + off);
+    off = align_up(off + slots * p.GT * 4, 256);
+    a.pacc = reinterpret_cast<float *>(ws + off);
+    a.off_A = p.off_A; a.off_ksc = p.off_ksc; a.off_vsc = p.off_vsc; a.off_sc = p.off_sc;
+    a.off_lg = p.off_lg; a.off_red = p.off_red; a.off_stat = p.off_stat;
+    a.off_ring = p.off_ring; a.off_bar = p.off_bar;
+
+    const int64_t nctas = units / p.n_groups * p.n_split;
+    if (nctas > 0x7fffffffLL) { set_error("decode_attn: grid too large"); return FC_ENOTSUP; }
+    dim3 grid((unsigned)nctas, (unsigned)p.n_groups);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (rows_dtype) {
+        case FC_I8: return launch_rt<int8_t>(p, a, grid, st);
+        case FC_BF16: return launch_rt<__nv_bfloat16>(p, a, grid, st);
+        case FC_F16: return launch_rt<__half>(p, a, grid, st);
+        default: return launch_rt<float>(p, a, grid, st);
+    }
+}

@@ -1,0 +1,447 @@
+// Codec kernels: jpeg archive (DCT-II projection + int8 quantizer), jpeg read
+// path (dequantize + synthesis), png archive (anchor + deltas, Top-M) and png
+// read path (segmented fp64 prefix sum).
+//
+// All four are HBM-bound streaming kernels.  One warp owns one r-token block
+// of one (batch, head) row; lanes span the head dimension with vector loads so
+// each warp touches whole contiguous rows.  Arithmetic follows the reference's
+// CPU PyTorch order exactly (explicit __fmaf_rn / __fmul_rn / __fdiv_rn so the
+// compiler cannot re-associate or contract), which makes every output
+// bit-identical to the reference.
+#include <math.h>
+
+#include "fc_common.cuh"
+
+namespace fc {
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kMaxR = 64;       // largest block_size the kernels take
+constexpr int kEncTile = 4;     // frequencies computed per pass in the encoder
+
+struct EncArgs {
+    const void *x;
+    int64_t B, H, S, D, nblk;
+    int64_t x_sb, x_sh, x_ss;
+    const float *basis;
+    int r, k;
+    void *out;
+    int64_t o_sb, o_sh, o_sn, o_sj;
+    void *scales;
+    int scale_dtype;
+    int64_t s_sb, s_sh, s_sn;
+    int *err;
+};
+
+__device__ __forceinline__ float nan_max(float m, float a) {
+    // torch.amax propagates NaN; fmaxf would drop it
+    return (a > m || a != a) ? a : m;
+}
+
+// x (B,H,S,D) of T -> coefficients (quantized to int8 + scales when
+// `scales` != nullptr).  Dynamic shared memory: per warp kEncTile x D floats.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+jpeg_encode_kernel(EncArgs a) {
+    extern __shared__ float smem[];
+    __shared__ float s_basis[kMaxR * kMaxR];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < a.k * a.r; i += blockDim.x) s_basis[i] = a.basis[i];
+    __syncthreads();
+
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    const int64_t total = a.B * a.H * a.nblk;
+    if (gw >= total) return;
+    const int64_t blk = gw % a.nblk;
+    const int64_t bh = gw / a.nblk;
+    const int64_t b = bh / a.H, h = bh % a.H;
+    const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * a.r * a.x_ss;
+    const int rows = (int)min((int64_t)a.r, a.S - blk * a.r);  // rows past S are zero padding
+    float *tile = smem + warp * kEncTile * a.D;
+    constexpr int dt = Elem<T>::code;
+    const bool quant = a.scales != nullptr;
+
+    for (int j0 = 0; j0 < a.k; j0 += kEncTile) {
+        const int nj = min(kEncTile, a.k - j0);
+        float amax[kEncTile];
+#pragma unroll
+        for (int jj = 0; jj < kEncTile; jj++) amax[jj] = 0.0f;
+        for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+            float acc[kEncTile][VEC];
+#pragma unroll
+            for (int jj = 0; jj < kEncTile; jj++)
+#pragma unroll
+                for (int v = 0; v < VEC; v++) acc[jj][v] = 0.0f;
+            for (int i = 0; i < a.r; i++) {
+                float xv[VEC];
+                if (i < rows) {
+                    load_vec_f32<T, VEC>(xb + i * a.x_ss + d0, xv);
+                } else {
+#pragma unroll
+                    for (int v = 0; v < VEC; v++) xv[v] = 0.0f;
+                }
+#pragma unroll
+                for (int jj = 0; jj < kEncTile; jj++) {
+                    if (jj < nj) {
+                        const float m = s_basis[(j0 + jj) * a.r + i];
+#pragma unroll
+                        for (int v = 0; v < VEC; v++) acc[jj][v] = __fmaf_rn(xv[v], m, acc[jj][v]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int jj = 0; jj < kEncTile; jj++) {
+                if (jj >= nj) continue;
+                const int64_t orow = b * a.o_sb + h * a.o_sh + blk * a.o_sn + (j0 + jj) * a.o_sj;
+#pragma unroll
+                for (int v = 0; v < VEC; v++) {
+                    const float c = round_to_dtype(acc[jj][v], dt);  // .to(x.dtype), jpeg.py:67
+                    if (quant) {
+                        tile[jj * a.D + d0 + v] = c;
+                        amax[jj] = nan_max(amax[jj], fabsf(c));
+                    } else {
+                        store_from_f32(a.out, orow + d0 + v, dt, c);
+                    }
+                }
+            }
+        }
+        if (!quant) continue;
+#pragma unroll
+        for (int jj = 0; jj < kEncTile; jj++)
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                amax[jj] = nan_max(amax[jj], __shfl_xor_sync(0xffffffffu, amax[jj], off));
+        __syncwarp();
+#pragma unroll
+        for (int jj = 0; jj < kEncTile; jj++) {
+            if (jj >= nj) continue;
+            // scale = amax / 127 in the coefficient dtype; 1 where it is 0
+            float s = round_to_dtype(__fdiv_rn(amax[jj], 127.0f), dt);
+            if (!(s > 0.0f)) s = 1.0f;
+            int8_t *orow = static_cast<int8_t *>(a.out) + b * a.o_sb + h * a.o_sh +
+                           blk * a.o_sn + (j0 + jj) * a.o_sj;
+            for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+                uint32_t packed[(VEC + 3) / 4];
+#pragma unroll
+                for (int w = 0; w < (VEC + 3) / 4; w++) packed[w] = 0u;
+#pragma unroll
+                for (int v = 0; v < VEC; v++) {
+                    float q = rintf(__fdiv_rn(tile[jj * a.D + d0 + v], s));
+                    q = fminf(fmaxf(q, -127.0f), 127.0f);
+                    const int qi = (int)q;
+                    if constexpr (VEC % 4 == 0) {
+                        packed[v / 4] |= ((uint32_t)(qi & 0xFF)) << (8 * (v % 4));
+                    } else {
+                        orow[d0 + v] = (int8_t)qi;
+                    }
+                }
+                if constexpr (VEC % 4 == 0) {
+#pragma unroll
+                    for (int w = 0; w < VEC / 4; w++)
+                        reinterpret_cast<uint32_t *>(orow + d0)[w] = packed[w];
+                }
+            }
+            if (lane == 0) {
+                const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + (j0 + jj);
+                if (a.scale_dtype == FC_F16) {
+                    const __half hs = __float2half_rn(s);
+                    static_cast<__half *>(a.scales)[si] = hs;
+                    if (__half2float(hs) != s && a.err) atomicOr(a.err, 1);
+                } else {
+                    static_cast<float *>(a.scales)[si] = s;
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+struct DecArgs {
+    const void *coef;
+    int64_t B, H, n, D;
+    int k;
+    int64_t c_sb, c_sh, c_sn, c_sj;
+    const void *scales;
+    int scale_dtype;
+    int64_t s_sb, s_sh, s_sn;
+    const float *basis;
+    int r;
+    void *out;
+    int out_dtype;
+    int64_t out_len, o_sb, o_sh, o_ss;
+};
+
+// coefficients (B,H,n,k,D) -> (B,H,out_len,D); KM >= k coefficient registers.
+template <typename CT, int VEC, int KM>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+jpeg_decode_kernel(DecArgs a) {
+    __shared__ float s_basis[kMaxR * kMaxR];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < a.k * a.r; i += blockDim.x) s_basis[i] = a.basis[i];
+    __syncthreads();
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= a.B * a.H * a.n) return;
+    const int64_t blk = gw % a.n, bh = gw / a.n;
+    const int64_t b = bh / a.H, h = bh % a.H;
+    const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh + blk * a.c_sn;
+    float sc[KM];
+#pragma unroll
+    for (int j = 0; j < KM; j++) {
+        sc[j] = 1.0f;
+        if (j < a.k && a.scales)
+            sc[j] = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
+    }
+    const int64_t obase = b * a.o_sb + h * a.o_sh;
+    for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+        float c[KM][VEC];
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
+            if (j < a.k) {
+                load_vec_f32<CT, VEC>(cb + j * a.c_sj + d0, c[j]);
+                if (a.scales) {
+                    // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
+#pragma unroll
+                    for (int v = 0; v < VEC; v++) c[j][v] = __fmul_rn(c[j][v], sc[j]);
+                }
+            }
+        }
+        for (int i = 0; i < a.r; i++) {
+            const int64_t pos = blk * a.r + i;
+            if (pos >= a.out_len) break;
+#pragma unroll
+            for (int v = 0; v < VEC; v++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int j = 0; j < KM; j++)
+                    if (j < a.k) acc = __fmaf_rn(c[j][v], s_basis[j * a.r + i], acc);
+                store_from_f32(a.out, obase + pos * a.o_ss + d0 + v, a.out_dtype, acc);
+            }
+        }
+    }
+}
+
+struct PngEncArgs {
+    const void *x;
+    int64_t B, H, S, D, nblk;
+    int64_t x_sb, x_sh, x_ss;
+    int r, keep_m;
+    float *deltas;
+    int64_t d_sb, d_sh, d_sn, d_si;
+    void *anchors;
+    int64_t a_sb, a_sh, a_sn;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+png_encode_kernel(PngEncArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= a.B * a.H * a.nblk) return;
+    const int64_t blk = gw % a.nblk, bh = gw / a.nblk;
+    const int64_t b = bh / a.H, h = bh % a.H;
+    const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * a.r * a.x_ss;
+    const int rows = (int)min((int64_t)a.r, a.S - blk * a.r);
+    float *db = a.deltas + b * a.d_sb + h * a.d_sh + blk * a.d_sn;
+    T *ab = static_cast<T *>(a.anchors) + b * a.a_sb + h * a.a_sh + blk * a.a_sn;
+    for (int64_t d = lane; d < a.D; d += 32) {
+        float prev = Elem<T>::to_f32(xb[d]);
+        ab[d] = xb[d];                                   // anchor, input dtype (png.py:51)
+        for (int i = 1; i < a.r; i++) {
+            const float cur = i < rows ? Elem<T>::to_f32(xb[i * a.x_ss + d]) : 0.0f;
+            db[(i - 1) * a.d_si + d] = __fsub_rn(cur, prev);  // fp32 deltas (png.py:52-53)
+            prev = cur;
+        }
+        if (a.keep_m < a.r - 1) {
+            // Top-M by |delta| per (block, channel); the rest times 0 (png.py:54-59)
+            float dl[kMaxR];
+            for (int i = 0; i < a.r - 1; i++) dl[i] = db[i * a.d_si + d];
+            for (int i = 0; i < a.r - 1; i++) {
+                const float ai = fabsf(dl[i]);
+                int rank = 0;
+                for (int t = 0; t < a.r - 1; t++) {
+                    const float at = fabsf(dl[t]);
+                    rank += (at > ai || (at == ai && t < i)) ? 1 : 0;
+                }
+                if (rank >= a.keep_m) db[i * a.d_si + d] = __fmul_rn(dl[i], 0.0f);
+            }
+        }
+    }
+}
+
+struct PngDecArgs {
+    const float *deltas;
+    int64_t d_sb, d_sh, d_sn, d_si;
+    const void *anchors;
+    int a_dtype;
+    int64_t a_sb, a_sh, a_sn;
+    int64_t B, H, n;
+    int r;
+    int64_t D;
+    void *out;
+    int64_t out_len, o_sb, o_sh, o_ss;
+};
+
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+png_decode_kernel(PngDecArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= a.B * a.H * a.n) return;
+    const int64_t blk = gw % a.n, bh = gw / a.n;
+    const int64_t b = bh / a.H, h = bh % a.H;
+    const float *db = a.deltas + b * a.d_sb + h * a.d_sh + blk * a.d_sn;
+    const int64_t abase = b * a.a_sb + h * a.a_sh + blk * a.a_sn;
+    const int64_t obase = b * a.o_sb + h * a.o_sh;
+    for (int64_t d = lane; d < a.D; d += 32) {
+        const float an = load_as_f32(a.anchors, abase + d, a.a_dtype);
+        int64_t pos = blk * a.r;
+        if (pos < a.out_len) store_from_f32(a.out, obase + pos * a.o_ss + d, a.a_dtype, an);
+        double pre = 0.0;  // torch's CPU cumsum accumulates fp32 in fp64 (png.py:71)
+        for (int i = 1; i < a.r; i++) {
+            pre += (double)__ldg(db + (i - 1) * a.d_si + d);
+            if (++pos >= a.out_len) break;
+            const float v = __fadd_rn(an, __double2float_rn(pre));
+            store_from_f32(a.out, obase + pos * a.o_ss + d, a.a_dtype, v);
+        }
+    }
+}
+
+inline unsigned grid_for(int64_t warps) {
+    return (unsigned)((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+}
+
+template <typename F>
+int launch_typed(int dt, F &&f) {
+    switch (dt) {
+        case FC_F32: return f((float *)nullptr);
+        case FC_BF16: return f((__nv_bfloat16 *)nullptr);
+        case FC_F16: return f((__half *)nullptr);
+        case FC_I8: return f((int8_t *)nullptr);
+        default: set_error("unknown dtype code %d", dt); return FC_EINVAL;
+    }
+}
+
+}  // namespace
+}  // namespace fc
+
+using namespace fc;
+
+extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,
+                              int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss,
+                              const float *basis, int r, int k, void *out, int64_t o_sb,
+                              int64_t o_sh, int64_t o_sn, int64_t o_sj, void *scales,
+                              int scale_dtype, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                              int *err, void *stream) {
+    clear_error();
+    if (!is_float_dtype(x_dtype)) { set_error("jpeg_encode: x dtype must be f32/bf16/f16"); return FC_EINVAL; }
+    if (B < 0 || H < 0 || S < 0 || D <= 0) { set_error("jpeg_encode: bad shape"); return FC_EINVAL; }
+    if (r < 1 || r > kMaxR || k < 1 || k > r) { set_error("jpeg_encode: need 1 <= k <= r <= %d", kMaxR); return FC_EINVAL; }
+    if (scales && scale_dtype != FC_F32 && scale_dtype != FC_F16) { set_error("jpeg_encode: scale dtype must be f32 or f16"); return FC_EINVAL; }
+    const int64_t nblk = (S + r - 1) / r;
+    if (B * H * nblk == 0) return FC_OK;
+    if (!x || !basis || !out) { set_error("jpeg_encode: null pointer"); return FC_EINVAL; }
+    const int es = dtype_size(x_dtype);
+    // 4-element vectors when every row start and the head dim allow it
+    bool v4 = (D % 4 == 0) && aligned(x, 4 * es) && (x_sb % 4 == 0) && (x_sh % 4 == 0) &&
+              (x_ss % 4 == 0);
+    if (scales) v4 = v4 && aligned(out, 4) && (o_sb % 4 == 0) && (o_sh % 4 == 0) &&
+                     (o_sn % 4 == 0) && (o_sj % 4 == 0);
+    EncArgs a{x, B, H, S, D, nblk, x_sb, x_sh, x_ss, basis, r, k, out, o_sb, o_sh, o_sn, o_sj,
+              scales, scale_dtype, s_sb, s_sh, s_sn, err};
+    const size_t smem = (size_t)kWarpsPerCta * kEncTile * D * sizeof(float);
+    if (smem > 160 * 1024) { set_error("jpeg_encode: head dim too large"); return FC_ENOTSUP; }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return launch_typed(x_dtype, [&](auto *tp) -> int {
+        using T = std::remove_pointer_t<decltype(tp)>;
+        if constexpr (std::is_same<T, int8_t>::value) {
+            return FC_EINVAL;
+        } else {
+            auto kern = v4 ? jpeg_encode_kernel<T, 4> : jpeg_encode_kernel<T, 1>;
+            // the kernel also holds a static kMaxR x kMaxR basis table
+            if (smem + sizeof(float) * kMaxR * kMaxR > 48 * 1024)
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            kern<<<grid_for(B * H * nblk), kWarpsPerCta * 32, smem, st>>>(a);
+            return check_launch("jpeg_encode");
+        }
+    });
+}
+
+extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64_t H, int64_t n,
+                              int64_t D, int k, int64_t c_sb, int64_t c_sh, int64_t c_sn,
+                              int64_t c_sj, const void *scales, int scale_dtype, int64_t s_sb,
+                              int64_t s_sh, int64_t s_sn, const float *basis, int r, void *out,
+                              int out_dtype, int64_t out_len, int64_t o_sb, int64_t o_sh,
+                              int64_t o_ss, void *stream) {
+    clear_error();
+    if (dtype_size(coef_dtype) == 0 || !is_float_dtype(out_dtype)) { set_error("jpeg_decode: bad dtype"); return FC_EINVAL; }
+    if (coef_dtype == FC_I8 && !scales) { set_error("jpeg_decode: int8 codes need scales"); return FC_EINVAL; }
+    if (scales && scale_dtype != FC_F32 && scale_dtype != FC_F16) { set_error("jpeg_decode: scale dtype must be f32 or f16"); return FC_EINVAL; }
+    if (r < 1 || r > kMaxR || k < 1 || k > r) { set_error("jpeg_decode: need 1 <= k <= r <= %d", kMaxR); return FC_EINVAL; }
+    if (B < 0 || H < 0 || n < 0 || D <= 0 || out_len < 0 || out_len > n * r) { set_error("jpeg_decode: bad shape"); return FC_EINVAL; }
+    if (B * H * n == 0 || out_len == 0) return FC_OK;
+    if (!coef || !basis || !out) { set_error("jpeg_decode: null pointer"); return FC_EINVAL; }
+    const int es = dtype_size(coef_dtype);
+    const bool v4 = (D % 4 == 0) && aligned(coef, 4 * es) && (c_sb % 4 == 0) && (c_sh % 4 == 0) &&
+                    (c_sn % 4 == 0) && (c_sj % 4 == 0);
+    DecArgs a{coef, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales, scale_dtype, s_sb, s_sh, s_sn,
+              basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(B * H * n);
+    return launch_typed(coef_dtype, [&](auto *tp) -> int {
+        using CT = std::remove_pointer_t<decltype(tp)>;
+        if (k <= 4) {
+            if (v4) jpeg_decode_kernel<CT, 4, 4><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            else jpeg_decode_kernel<CT, 1, 4><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+        } else if (k <= 16) {
+            if (v4) jpeg_decode_kernel<CT, 4, 16><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            else jpeg_decode_kernel<CT, 1, 16><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+        } else {
+            jpeg_decode_kernel<CT, 1, kMaxR><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+        }
+        return check_launch("jpeg_decode");
+    });
+}
+
+extern "C" int fc_png_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,
+                             int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss, int r,
+                             int keep_m, float *deltas, int64_t d_sb, int64_t d_sh, int64_t d_sn,
+                             int64_t d_si, void *anchors, int64_t a_sb, int64_t a_sh,
+                             int64_t a_sn, void *stream) {
+    clear_error();
+    if (!is_float_dtype(x_dtype)) { set_error("png_encode: x dtype must be f32/bf16/f16"); return FC_EINVAL; }
+    if (r < 2 || r > kMaxR) { set_error("png_encode: need 2 <= block_size <= %d", kMaxR); return FC_EINVAL; }
+    if (keep_m < 1 || keep_m > r - 1) { set_error("png_encode: keep_m must be in [1, r-1]"); return FC_EINVAL; }
+    if (B < 0 || H < 0 || S < 0 || D <= 0) { set_error("png_encode: bad shape"); return FC_EINVAL; }
+    const int64_t nblk = (S + r - 1) / r;
+    if (B * H * nblk == 0) return FC_OK;
+    if (!x || !deltas || !anchors) { set_error("png_encode: null pointer"); return FC_EINVAL; }
+    PngEncArgs a{x, B, H, S, D, nblk, x_sb, x_sh, x_ss, r, keep_m, deltas, d_sb, d_sh, d_sn, d_si,
+                 anchors, a_sb, a_sh, a_sn};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return launch_typed(x_dtype, [&](auto *tp) -> int {
+        using T = std::remove_pointer_t<decltype(tp)>;
+        if constexpr (std::is_same<T, int8_t>::value) {
+            return FC_EINVAL;
+        } else {
+            png_encode_kernel<T><<<grid_for(B * H * nblk), kWarpsPerCta * 32, 0, st>>>(a);
+            return check_launch("png_encode");
+        }
+    });
+}
+
+extern "C" int fc_png_decode(const float *deltas, int64_t d_sb, int64_t d_sh, int64_t d_sn,
+                             int64_t d_si, const void *anchors, int a_dtype, int64_t a_sb,
+                             int64_t a_sh, int64_t a_sn, int64_t B, int64_t H, int64_t n, int r,
+                             int64_t D, void *out, int64_t out_len, int64_t o_sb, int64_t o_sh,
+                             int64_t o_ss, void *stream) {
+    clear_error();
+    if (!is_float_dtype(a_dtype)) { set_error("png_decode: anchor dtype must be f32/bf16/f16"); return FC_EINVAL; }
+    if (r < 2 || r > kMaxR) { set_error("png_decode: need 2 <= block_size <= %d", kMaxR); return FC_EINVAL; }
+    if (B < 0 || H < 0 || n < 0 || D <= 0 || out_len < 0 || out_len > n * r) { set_error("png_decode: bad shape"); return FC_EINVAL; }
+    if (B * H * n == 0 || out_len == 0) return FC_OK;
+    if (!deltas || !anchors || !out) { set_error("png_decode: null pointer"); return FC_EINVAL; }
+    PngDecArgs a{deltas, d_sb, d_sh, d_sn, d_si, anchors, a_dtype, a_sb, a_sh, a_sn,
+                 B, H, n, r, D, out, out_len, o_sb, o_sh, o_ss};
+    png_decode_kernel<<<grid_for(B * H * n), kWarpsPerCta * 32, 0,
+                        static_cast<cudaStream_t>(stream)>>>(a);
+    return check_launch("png_decode");
+}

@@ -1,0 +1,196 @@
+/*
+ * flashcodec_b200.h -- C ABI of libflashcodec_sm100.so, the B200 (sm_100a)
+ * kernels behind flashcodec's compressed-KV hot path.
+ *
+ * Conventions
+ *   - Every entry point is asynchronous on `stream` (a cudaStream_t passed as
+ *     void*; NULL = the legacy default stream) and returns an int status.
+ *     FC_OK = 0.  On failure fc_last_error_string() describes the problem
+ *     (thread-local, valid until the next call on the same thread).
+ *   - All pointers are device pointers unless stated otherwise.  The library
+ *     never allocates device memory: buffers, including the attention
+ *     workspace, belong to the caller.
+ *   - Tensors are described by a base pointer plus element strides for the
+ *     outer dimensions; the innermost (head_dim, D) stride is always 1.
+ *     Output pointers already point at the first block to be written (the
+ *     archive's block offset is applied by the caller).
+ *   - Shapes follow the reference's KV contract (B, H, S, D) with the
+ *     compression axis along S (flashcodec/__init__.py:10).
+ *
+ * Paths in citations are relative to the flashcodec project root.
+ */
+#ifndef FLASHCODEC_B200_H
+#define FLASHCODEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FC_API __attribute__((visibility("default")))
+#else
+#define FC_API
+#endif
+
+/* status codes */
+#define FC_OK 0
+#define FC_EINVAL 1   /* invalid argument: shape, stride, dtype or alignment */
+#define FC_ECUDA 2    /* CUDA launch or runtime error */
+#define FC_ERANGE 3   /* workspace too small, or a value outside its storage type */
+#define FC_ENOTSUP 4  /* valid request outside what the kernels implement */
+
+/* element types */
+#define FC_F32 0
+#define FC_BF16 1
+#define FC_F16 2
+#define FC_I8 3
+
+/* Library version string ("flashcodec_b200 <semver> sm_100a"). */
+FC_API const char *fc_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+FC_API const char *fc_last_error_string(void);
+
+/*
+ * jpeg archive / compress.
+ * Replaces flashcodec/codecs/jpeg.py:55-67 (dct_compress) followed by
+ * jpeg.py:85-100 (quantize_coeffs) and the in-place slice writes of
+ * flashcodec/cache.py:123-141 (_CodecStream._archive).
+ *
+ * x      (B, H, S, D) of x_dtype (F32/BF16/F16), strides x_sb, x_sh, x_ss.
+ *        S need not be a multiple of r: the last block is zero-padded
+ *        (jpeg.py:43-52).  n = ceil(S / r) blocks are written.
+ * basis  (k, r) fp32, the reference's dct_basis(r, k) (jpeg.py:24-40).
+ * out    (B, H, n, k, D): FC_I8 codes when `scales` is non-NULL, otherwise
+ *        coefficients in x_dtype; strides o_sb, o_sh, o_sn, o_sj.
+ * scales (B, H, n, k) per-(block, frequency) scales of scale_dtype (F32 as the
+ *        reference, or F16), strides s_sb, s_sh, s_sn (frequency stride 1).
+ * err    optional device int; set to 1 when an F16 scale cannot hold the
+ *        reference's scale exactly (the code is still computed with the
+ *        reference's scale).
+ * Coefficients use the reference's arithmetic bit-for-bit: a sequential fp32
+ * fused multiply-add chain over the r samples, rounded to x_dtype, amax,
+ * scale = x_dtype(amax / 127) (1 if zero), code = clamp(rint(c / scale), +-127).
+ */
+FC_API int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                   int64_t x_sb, int64_t x_sh, int64_t x_ss,
+                   const float *basis, int r, int k,
+                   void *out, int64_t o_sb, int64_t o_sh, int64_t o_sn, int64_t o_sj,
+                   void *scales, int scale_dtype, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                   int *err, void *stream);
+
+/*
+ * jpeg read path.
+ * Replaces flashcodec/codecs/jpeg.py:103-105 (dequantize_coeffs, fp32) and
+ * jpeg.py:70-82 (dct_decompress), as used by flashcodec/cache.py:161-193
+ * (_CodecStream._decode_pending) and JPEGCodec.decompress (jpeg.py:138-142).
+ *
+ * coef   (B, H, n, k, D): FC_I8 codes with `scales`, or F32/BF16/F16 coefficients.
+ * scales (B, H, n, k) of scale_dtype, or NULL.
+ * out    (B, H, out_len, D) of out_dtype, out_len <= n * r (positions past
+ *        out_len are not written -- the reference's trim).
+ * rec[i][d] = out_dtype(sum_j (c[j][d] * scale[j]) * basis[j][i]) as a
+ * sequential fp32 fused multiply-add chain over j.
+ */
+FC_API int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64_t H, int64_t n,
+                   int64_t D, int k, int64_t c_sb, int64_t c_sh, int64_t c_sn, int64_t c_sj,
+                   const void *scales, int scale_dtype, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                   const float *basis, int r,
+                   void *out, int out_dtype, int64_t out_len,
+                   int64_t o_sb, int64_t o_sh, int64_t o_ss, void *stream);
+
+/*
+ * png archive / filter.
+ * Replaces flashcodec/codecs/png.py:36-60 (png_filter) and the png branch of
+ * flashcodec/cache.py:137-140.
+ *
+ * x       (B, H, S, D) of x_dtype; the last block is zero-padded.
+ * deltas  (B, H, n, r-1, D) fp32, strides d_sb, d_sh, d_sn, d_si:
+ *         f32(x_i) - f32(x_{i-1}).
+ * anchors (B, H, n, D) of x_dtype, strides a_sb, a_sh, a_sn: x_0 of each block.
+ * keep_m  number of deltas kept per (block, channel), 1..r-1; r-1 keeps all
+ *         (keep_ratio = 1).  Otherwise the keep_m largest |delta| survive and
+ *         the rest are multiplied by 0 (png.py:54-59); ties keep the lower
+ *         index (torch.topk's tie order is implementation-defined).
+ */
+FC_API int fc_png_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                  int64_t x_sb, int64_t x_sh, int64_t x_ss, int r, int keep_m,
+                  float *deltas, int64_t d_sb, int64_t d_sh, int64_t d_sn, int64_t d_si,
+                  void *anchors, int64_t a_sb, int64_t a_sh, int64_t a_sn, void *stream);
+
+/*
+ * png read path: segmented prefix sum.
+ * Replaces flashcodec/codecs/png.py:63-74 (png_reconstruct) as used by
+ * flashcodec/cache.py:189-191.
+ *
+ * rec_0 = anchor, rec_i = a_dtype(f32(anchor) + f32(prefix_i)) where prefix_i
+ * is the sum of the first i deltas accumulated in fp64 (what torch's CPU
+ * cumsum does), so results are bit-identical to the reference's CPU output.
+ * out (B, H, out_len, D) of the anchor dtype, out_len <= n * r.
+ */
+FC_API int fc_png_decode(const float *deltas, int64_t d_sb, int64_t d_sh, int64_t d_sn, int64_t d_si,
+                  const void *anchors, int a_dtype, int64_t a_sb, int64_t a_sh, int64_t a_sn,
+                  int64_t B, int64_t H, int64_t n, int r, int64_t D,
+                  void *out, int64_t out_len, int64_t o_sb, int64_t o_sh, int64_t o_ss,
+                  void *stream);
+
+/*
+ * Bytes of workspace fc_decode_attn needs for these sizes.  The workspace
+ * (256-byte aligned) starts with a 256-byte header whose first int32 is a
+ * status word: a launch whose bounded wait for a staged tile gave up (100 ms)
+ * stores its positive launch number there, so nonzero means some call since
+ * the workspace was zeroed produced invalid output.  The rest holds the
+ * split partials and per-(batch, KV head) arrival counters.  The workspace
+ * must be zero-filled before its first use; a completed call leaves its
+ * counters at zero again.  Calls sharing one workspace must not overlap on
+ * the GPU (issue them on one stream).
+ */
+FC_API size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t Hk, int64_t D,
+                                     int64_t n_blocks, int s, int r, int64_t n_raw);
+
+/*
+ * Coefficient-domain split-K decode attention.
+ * Replaces flashcodec/triton_attention.py:151-222
+ * (codec_decode_attention_triton with _attn_split_kernel :34-116 and
+ * _attn_combine_kernel :118-144), i.e. the math of
+ * flashcodec/attention.py:64-140 for one decode query:
+ *
+ *   logits = [ scale * (q . rows_K) A^T ,  scale * q . kraw ]
+ *   out    = softmax(logits) . [ rows_V through A ,  vraw ]
+ *
+ * q       (B, Hq, D) of q_dtype, strides q_sb, q_sh.
+ * k_rows, v_rows  (B, Hk, n_blocks, s, D) stored rows of rows_dtype: FC_I8
+ *         codes (with scales), or F32/BF16/F16 coefficients / png rows.
+ *         Strides k_* and v_* (element units).
+ * k_scales, v_scales (B, Hk, n_blocks, s) of scale_dtype (F32/F16) or NULL.
+ * k_raw, v_raw  (B, Hk, n_raw, D) raw tail of raw_dtype, or NULL when n_raw = 0.
+ * A       (r, s) fp32 synthesis matrix (flashcodec/attention.py:35-42).
+ * out     (B, Hq, D) of out_dtype.
+ * Hq must be a multiple of Hk (query heads grouped per KV head, GQA);
+ * D <= 256.  Softmax and all accumulation are fp32.  Splits along the block
+ * axis are merged in the same launch by the last split to finish (LSE merge);
+ * no kernel waits on another.
+ */
+FC_API int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                   int64_t q_sb, int64_t q_sh,
+                   int64_t Hk, int64_t n_blocks, int s, int r, int rows_dtype,
+                   const void *k_rows, int64_t k_sb, int64_t k_sh, int64_t k_sn, int64_t k_sj,
+                   const void *v_rows, int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t v_sj,
+                   const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                   const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                   int scale_dtype,
+                   const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
+                   const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+                   int raw_dtype, int64_t n_raw,
+                   const float *A, float softmax_scale,
+                   void *out, int out_dtype, int64_t o_sb, int64_t o_sh,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHCODEC_B200_H */

@@ -265,3 +265,12 @@ def reference_attention_fp32(q, krows, vrows, kraw, vraw, A, scale=None) -> np.n
     if kraw is not None:
         out += np.einsum("bhgt,bhtd->bhgd", p[..., pos:], vraw, optimize=True)
     return out.reshape(B, Hq, 1, D)
+
+
+def reference_attention_int8(q, kcodes, kscales, vcodes, vscales, kraw, vraw, A, scale=None):
+    """The reference's jpeg-int8 decode attention on CPU: dequantize the codes
+    into fp32 rows (flashcodec/attention.py:45-61, jpeg.py:103-105), then the
+    einsum path of reference_attention_fp32.  The timed CPU baseline."""
+    krows = kcodes.astype(np.float32) * kscales
+    vrows = vcodes.astype(np.float32) * vscales
+    return reference_attention_fp32(q, krows, vrows, kraw, vraw, A, scale)

@@ -1,0 +1,102 @@
+"""The C-ABI library: builds for sm_100a, loads without a GPU, exports every
+symbol include/flashcodec_b200.h declares, and rejects bad arguments on the
+host before any launch.  CPU only (no kernel is launched)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "flashcodec_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from flashcodec_b200 import _lib, build
+    build.build()
+    return _lib.load()
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return re.findall(r"FC_API\s+[\w\s\*]+?\b(fc_\w+)\s*\(", text)
+
+
+def test_header_declares_the_binding_table():
+    from flashcodec_b200 import _lib
+    assert declared_symbols() == list(_lib.SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_version(lib):
+    assert lib.fc_version().decode().startswith("flashcodec_b200 ")
+
+
+def test_host_validation(lib):
+    from flashcodec_b200 import _lib
+    P = ctypes.c_void_p
+    dummy = P(0x1000)
+    # int8 input to the archive kernel
+    rc = lib.fc_jpeg_encode(dummy, _lib.FC_I8, 1, 1, 8, 16, 128, 128, 16, dummy, 8, 2,
+                            dummy, 0, 0, 0, 0, None, 0, 0, 0, 0, None, None)
+    assert rc == _lib.FC_EINVAL
+    assert b"dtype" in lib.fc_last_error_string()
+    # k > r
+    rc = lib.fc_jpeg_encode(dummy, _lib.FC_F32, 1, 1, 8, 16, 128, 128, 16, dummy, 8, 9,
+                            dummy, 0, 0, 0, 0, None, 0, 0, 0, 0, None, None)
+    assert rc == _lib.FC_EINVAL
+    # empty input is a no-op
+    rc = lib.fc_jpeg_encode(dummy, _lib.FC_F32, 1, 1, 0, 16, 128, 128, 16, dummy, 8, 2,
+                            dummy, 0, 0, 0, 0, None, 0, 0, 0, 0, None, None)
+    assert rc == _lib.FC_OK
+    # png keep_m out of range
+    rc = lib.fc_png_encode(dummy, _lib.FC_F32, 1, 1, 16, 16, 256, 256, 16, 8, 9,
+                           dummy, 0, 0, 0, 0, dummy, 0, 0, 0, None)
+    assert rc == _lib.FC_EINVAL
+    # int8 codes without scales on the read path
+    rc = lib.fc_jpeg_decode(dummy, _lib.FC_I8, 1, 1, 2, 16, 2, 0, 0, 0, 0, None, 0, 0, 0, 0,
+                            dummy, 8, dummy, _lib.FC_F32, 16, 0, 0, 0, None)
+    assert rc == _lib.FC_EINVAL
+
+
+def _attn(lib, **kw):
+    from flashcodec_b200 import _lib
+    a = dict(q=ctypes.c_void_p(0x1000), q_dtype=_lib.FC_F32, B=1, Hq=4, D=64, q_sb=256, q_sh=64,
+             Hk=2, n=4, s=2, r=8, rows_dtype=_lib.FC_I8, k=ctypes.c_void_p(0x2000),
+             v=ctypes.c_void_p(0x3000), ks=ctypes.c_void_p(0x4000), vs=ctypes.c_void_p(0x5000),
+             sc_dtype=_lib.FC_F32, n_raw=0, A=ctypes.c_void_p(0x6000),
+             out=ctypes.c_void_p(0x7000), out_dtype=_lib.FC_F32, ws=None, ws_bytes=0)
+    a.update(kw)
+    return lib.fc_decode_attn(
+        a["q"], a["q_dtype"], a["B"], a["Hq"], a["D"], a["q_sb"], a["q_sh"],
+        a["Hk"], a["n"], a["s"], a["r"], a["rows_dtype"],
+        a["k"], 0, 0, 0, 0, a["v"], 0, 0, 0, 0,
+        a["ks"], 0, 0, 0, a["vs"], 0, 0, 0, a["sc_dtype"],
+        None, 0, 0, 0, None, 0, 0, 0, _lib.FC_F32, a["n_raw"],
+        a["A"], 0.125, a["out"], a["out_dtype"], 256, 64, a["ws"], a["ws_bytes"], None)
+
+
+def test_attention_host_validation(lib):
+    from flashcodec_b200 import _lib
+    assert _attn(lib, Hq=3) == _lib.FC_EINVAL                  # GQA divisibility
+    assert _attn(lib, D=512) == _lib.FC_ENOTSUP                # head dim > 256
+    assert _attn(lib, ks=None) == _lib.FC_EINVAL               # int8 rows need scales
+    assert _attn(lib, n_raw=8) == _lib.FC_EINVAL               # tail must be < r
+    assert _attn(lib, n=0, n_raw=0) == _lib.FC_EINVAL          # empty: caller returns zeros
+    assert _attn(lib) == _lib.FC_ERANGE                        # no workspace
+    assert b"workspace" in lib.fc_last_error_string()
+
+
+def test_workspace_size_is_host_only(lib):
+    n = lib.fc_decode_attn_workspace_size(16, 32, 8, 128, 4096, 4, 8, 5)
+    assert n >= 256
+    # the partials: units * splits * G * (D + 2) floats at most a few percent
+    # of the 553 MB archive of this shape (config 2, one layer)
+    assert n < 0.05 * 553_648_128
+    assert lib.fc_decode_attn_workspace_size(1, 3, 2, 64, 8, 2, 8, 0) == 0

@@ -1,0 +1,185 @@
+"""GPU parity of the split-K decode-attention kernel.
+
+Tolerances (the attention bar): fp32 outputs within 1e-5 absolute of the fp64
+oracle on the same archive; bf16 outputs within 2e-3 absolute plus one bf16
+rounding of the output (2^-8 relative) of the oracle.  Against the reference's
+own bf16 torch path (which rounds its intermediates to bf16) the bound is two
+bf16 units of the largest output, as in the oracle pinning test.
+"""
+
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT / "tests" / "golden"))
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+import cases  # noqa: E402
+from cases import f32  # noqa: E402
+from oracle import oracle as orc  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def oracle_rows(st):
+    """Stored rows, raw tail and A of a product stream, read back to the host."""
+    n = st.n_blocks
+    raw = f32(st.raw) if st.raw is not None else None
+    if n == 0:
+        return None, raw
+    if st.codec.name == "jpeg":
+        if st.codec.quantized:
+            codes = st._coeffs[:, :, :n].cpu().numpy().astype(np.float32)
+            return orc.stored_rows("jpeg", codes=codes, scales=f32(st._scales[:, :, :n])), raw
+        return orc.stored_rows("jpeg", codes=f32(st._coeffs[:, :, :n])), raw
+    return orc.stored_rows("png", anchors=f32(st._anchors[:, :, :n]),
+                           deltas=f32(st._deltas[:, :, :n])), raw
+
+
+def oracle_attention(q, ks, vs, scale=None):
+    import flashcodec_b200 as fc
+    kr, kraw = oracle_rows(ks)
+    vr, vraw = oracle_rows(vs)
+    A = f32(fc.block_basis(ks.codec, ks.block_size))
+    return orc.decode_attention(f32(q), kr, vr, kraw, vraw, A, scale)
+
+
+def check_close(out, ref, dtype):
+    o = f32(out)
+    if dtype == torch.float32:
+        err = np.abs(o - ref).max()
+        assert err <= 1e-5, err
+    else:
+        bound = 2e-3 + 2.0 ** -8 * np.abs(ref)
+        assert np.all(np.abs(o - ref) <= bound), np.abs(o - ref).max()
+
+
+def build(mode, kw, k, v, r=8):
+    import flashcodec_b200 as fc
+    ks = fc._CodecStream(fc.make_codec(mode, block_size=r, **kw))
+    vs = fc._CodecStream(fc.make_codec(mode, block_size=r, **kw))
+    ks.append(k)
+    vs.append(v)
+    return ks, vs
+
+
+@pytest.mark.parametrize("i", range(len(cases.ATTN_CASES)))
+def test_attention_golden_cases(golden, i):
+    import flashcodec_b200 as fc
+    data, _ = golden
+    name, mode, kw, dt, B, Hk, G, S, D, tail = cases.ATTN_CASES[i]
+    k, v, q = cases.attn_input(i)
+    ks, vs = build(mode, kw, k.to(DEV), v.to(DEV))
+    out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+    assert out.shape == q.shape and out.dtype == q.dtype
+    assert ks._rec is None and vs._rec is None          # no materialization
+    ref = oracle_attention(q, ks, vs)
+    check_close(out, ref, q.dtype)
+    gold = data[f"{name}/out"]
+    if dt == "f32":
+        assert np.abs(f32(out) - gold).max() <= 1e-5
+    else:
+        assert np.abs(f32(out) - data[f"{name}/out_f32math"]).max() <= 2e-3 + 2.0 ** -8 * np.abs(gold).max()
+        assert np.abs(f32(out) - gold).max() <= max(2e-3, 2.0 ** -7 * np.abs(gold).max())
+
+
+def test_cfg1_attention(golden):
+    """Config 1 at full size, t=0 and t=1 raw tail tokens."""
+    import flashcodec_b200 as fc
+    data, meta = golden
+    c = meta["cfg1"]
+    k, v, q = cases.cfg1_input()
+    for t in (0, 1):
+        ks, vs = build("jpeg", dict(keep_freqs=2, quant_bits=8),
+                       k[:, :, :c["S"] + t].to(DEV), v[:, :, :c["S"] + t].to(DEV))
+        out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+        assert np.abs(f32(out) - data[f"cfg1_t{t}/out"]).max() <= 1e-5
+        check_close(out, oracle_attention(q, ks, vs), torch.float32)
+
+
+@pytest.mark.parametrize("G,D,dt,K,quant,S,tail", [
+    (4, 128, torch.bfloat16, 4, 8, 8 * 3001, 5),    # config-2 shape, odd block count
+    (1, 64, torch.float32, 2, 8, 8 * 40, 0),
+    (2, 256, torch.bfloat16, 2, 8, 8 * 70, 7),
+    (8, 128, torch.float16, 2, 8, 8 * 90, 1),
+    (3, 96, torch.float32, 2, 8, 8 * 50, 2),        # G not a power of two, D off the fast path
+    (12, 128, torch.bfloat16, 4, 8, 8 * 33, 4),     # two head groups
+    (4, 128, torch.bfloat16, 4, 0, 8 * 300, 3),     # unquantized bf16 coefficients
+    (2, 80, torch.bfloat16, 3, 0, 8 * 30, 6),
+])
+def test_attention_shapes_vs_oracle(G, D, dt, K, quant, S, tail):
+    import flashcodec_b200 as fc
+    B, Hk = 2, 2
+    k, v, q = bench.synth_case(B, Hk * G, Hk, S + tail, D, 0.95, 11, dtype=dt)
+    ks, vs = build("jpeg", dict(keep_freqs=K, quant_bits=quant), k.to(DEV), v.to(DEV))
+    out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+    check_close(out, oracle_attention(q, ks, vs), dt)
+
+
+def test_attention_raw_only_and_single_block():
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(2, 8, 4, 13, 128, 0.95, 5)
+    for S in (5, 8, 13):
+        ks, vs = build("jpeg", dict(keep_freqs=2, quant_bits=8), k[:, :, :S].to(DEV),
+                       v[:, :, :S].to(DEV))
+        out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+        check_close(out, oracle_attention(q, ks, vs), torch.float32)
+
+
+def test_empty_cache_and_prefill_guard():
+    import flashcodec_b200 as fc
+    cfg = dict(mode="jpeg", block_size=8, keep_freqs=2)
+    ks, vs = fc._CodecStream(fc.make_codec(**cfg)), fc._CodecStream(fc.make_codec(**cfg))
+    q = torch.randn(2, 4, 1, 32, device=DEV)
+    out = fc.codec_decode_attention(q, ks, vs)
+    assert torch.equal(out, torch.zeros_like(out))
+    with pytest.raises(ValueError):
+        fc.codec_decode_attention(torch.randn(2, 4, 4, 32, device=DEV), ks, vs)
+
+
+def test_png_attention_vs_oracle():
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(2, 8, 4, 96 + 3, 32, 0.98, 9)
+    for keep in (1.0, 0.5):
+        ks, vs = build("png", dict(keep_ratio=keep), k.to(DEV), v.to(DEV))
+        out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+        check_close(out, oracle_attention(q, ks, vs), torch.float32)
+
+
+def test_attention_repeated_calls_reuse_workspace():
+    """The last-arriver counters reset themselves: many launches in a row on
+    one workspace give identical results and a clean status word."""
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as K
+    k, v, q = bench.synth_case(4, 32, 8, 8 * 1500 + 3, 128, 0.95, 2, dtype=torch.bfloat16)
+    ks, vs = build("jpeg", dict(keep_freqs=4, quant_bits=8), k.to(DEV), v.to(DEV))
+    qd = q.to(DEV)
+    first = fc.codec_decode_attention(qd, ks, vs)
+    for _ in range(20):
+        again = fc.codec_decode_attention(qd, ks, vs)
+        assert torch.equal(again, first)
+    assert K.attn_status(qd.device) == 0
+
+
+def test_scale_argument_and_impl_names():
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(1, 4, 2, 64 + 2, 64, 0.95, 4)
+    ks, vs = build("jpeg", dict(keep_freqs=2, quant_bits=8), k.to(DEV), v.to(DEV))
+    for impl in ("auto", "cuda", "triton", "torch"):
+        out = fc.codec_decode_attention(q.to(DEV), ks, vs, scale=0.3, impl=impl)
+        check_close(out, oracle_attention(q, ks, vs, scale=0.3), torch.float32)
+    with pytest.raises(ValueError):
+        fc.codec_decode_attention(q.to(DEV), ks, vs, impl="bogus")
+
+
+def test_cpu_tensors_are_rejected():
+    import flashcodec_b200 as fc
+    with pytest.raises(RuntimeError):
+        fc.dct_compress(torch.randn(1, 1, 8, 16), 8, 2)
