@@ -339,11 +339,14 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="flashcodec_b200", choices=["flashcodec_b200", "reference"])
-    ap.add_argument("--layers", type=int, default=CFG2["layers"])
+    ap.add_argument("--layers", type=int, default=CFG2["layers"],
+                    help="layers (default 36; fewer only for profiling a small case)")
+    ap.add_argument("--batch", type=int, default=CFG2["B"],
+                    help="sequences per GPU (default 16; smaller only for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = dict(CFG2, layers=args.layers)
+    cfg = dict(CFG2, layers=args.layers, B=args.batch)
     if args.impl == "reference":
         run_reference(args, cfg)
         return
@@ -376,6 +379,7 @@ def main():
     t_wall0 = time.time()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
+    torch.cuda.nvtx.range_push("timed")
     j = 0
     for _ in range(args.steps):
         for i, (ks, vs, q) in enumerate(layers):
@@ -383,6 +387,7 @@ def main():
             outs[i] = fc.codec_decode_attention(q, ks, vs)
             ev[j][1].record(stream)
             j += 1
+    torch.cuda.nvtx.range_pop()
     end.record(stream)
     torch.cuda.synchronize()
     t_wall1 = time.time()

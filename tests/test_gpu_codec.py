@@ -75,8 +75,12 @@ def test_png_codec_matches_reference(golden, i):
     rec = fc.png_reconstruct(d, a)
     assert rec.dtype == x.dtype
     assert same(f32(rec), data[f"{name}/rec"])
-    if keep == 1.0:
-        assert torch.equal(rec[..., :S, :], x)           # lossless, bitwise
+    if keep == 1.0 and dt == "bf16":
+        assert torch.equal(rec[..., :S, :], x)           # bf16: lossless bitwise (png.py:46-47)
+    elif keep == 1.0:
+        # fp32: rounding of the prefix sums only (reference test_png.py:26-29
+        # bounds it by 1e-6 on unit-scale data; scaled to the data here)
+        assert (rec[..., :S, :] - x).abs().max().item() <= 1e-6 * x.abs().max().item()
 
 
 @pytest.mark.parametrize("shape,r,k,dt", [
