@@ -189,6 +189,45 @@ FC_API int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int
                    void *out, int out_dtype, int64_t o_sb, int64_t o_sh,
                    void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * Decode attention that allocates nothing.  No counterpart in the reference:
+ * an addition of this library for callers that cannot allocate device
+ * memory -- engines that hand all of HBM to their KV block pool at start-up
+ * (a later cudaMalloc fails or fragments the pool), or plugins loaded through
+ * an FFI that may not call cudaMalloc and cannot reach their host framework's
+ * allocator.  Same arguments and result as fc_decode_attn, without the
+ * workspace: the split partials live in a scratch array compiled into the
+ * library, FC_NOALLOC_SCRATCH_BYTES per GPU, held on every GPU that loads the
+ * library's kernels until the process exits.
+ *
+ * - Calls whose plan needs more scratch than that return FC_ERANGE (use
+ *   fc_decode_attn with a workspace); fc_decode_attn_workspace_size tells the
+ *   size in advance.
+ * - The first call on a device looks up the scratch address on that device
+ *   (cudaGetSymbolAddress, with the device current); make that first call
+ *   before any stream capture.
+ * - Each call clears the scratch counters (cudaMemsetAsync on `stream`) and
+ *   then launches the attention kernel; no cudaMalloc, cudaFree or other
+ *   allocating call is made.
+ * - All calls on a device share one scratch array: calls that can overlap on
+ *   the GPU (different streams, or host threads without ordering) race and
+ *   must not be issued that way.
+ */
+#define FC_NOALLOC_SCRATCH_BYTES (16u << 20)
+FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                   int64_t q_sb, int64_t q_sh,
+                   int64_t Hk, int64_t n_blocks, int s, int r, int rows_dtype,
+                   const void *k_rows, int64_t k_sb, int64_t k_sh, int64_t k_sn, int64_t k_sj,
+                   const void *v_rows, int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t v_sj,
+                   const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                   const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                   int scale_dtype,
+                   const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
+                   const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+                   int raw_dtype, int64_t n_raw,
+                   const float *A, float softmax_scale,
+                   void *out, int out_dtype, int64_t o_sb, int64_t o_sh, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
