@@ -157,6 +157,18 @@ def attn_status(device: torch.device) -> int:
     return 0 if ws is None else int(ws[:4].view(torch.int32).item())
 
 
+def set_attn_kernel(which: str) -> str:
+    """Select the decode-attention kernel process-wide: "auto" (tensor cores
+    whenever the archive allows, the default), "cuda-core" or "tensor-core".
+    Returns the previous selection.  For tests and benchmarks."""
+    codes = {"auto": _lib.FC_ATTN_AUTO, "cuda-core": _lib.FC_ATTN_CUDA_CORE,
+             "tensor-core": _lib.FC_ATTN_TENSOR_CORE}
+    if which not in codes:
+        raise ValueError(f"unknown attention kernel {which!r}")
+    prev = _lib.load().fc_set_attn_kernel(codes[which])
+    return {v: k for k, v in codes.items()}[prev]
+
+
 def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
                 ws: torch.Tensor | None = None) -> None:
     """q (B,Hq,1,D); krows/vrows (B,Hk,n,s,D) or None; k/vscales (B,Hk,n,s,1)

@@ -31,10 +31,18 @@
 #include <algorithm>
 #include <atomic>
 
-#include "fc_common.cuh"
+#include "fc_attn_common.cuh"
 
 namespace fc {
+
+int tc_chunk_blocks(int s);
+bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype);
+int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows,
+                   int64_t krows_total, int64_t vrows_total, cudaStream_t st);
+
 namespace {
+
+std::atomic<int> g_attn_kernel{FC_ATTN_AUTO};
 
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
@@ -44,8 +52,6 @@ constexpr int kMaxRS = 64;            // r, s <= 64
 constexpr int kMaxD = 256;
 constexpr int kTargetChunk = 128;     // blocks per split (upper target)
 constexpr int kMinChunk = 16;
-constexpr uint64_t kWaitNs = 100000000ull;  // 100 ms bound on any mbarrier wait
-constexpr int kWsHeader = 256;        // workspace bytes before the counters
 constexpr size_t kSmemBudget = 96 * 1024;  // per-CTA shared-memory plan budget
 
 struct AttnArgs {
@@ -80,72 +86,6 @@ struct AttnArgs {
     // shared-memory carve-up (byte offsets)
     int off_A, off_ksc, off_vsc, off_sc, off_lg, off_red, off_stat, off_ring, off_bar;
 };
-
-// ------------------------------------------------------------ PTX wrappers
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
-                 : "memory");
-}
-
-__device__ __forceinline__ void fence_mbar_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
-                     smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-// 1D bulk async copy global -> shared, completing on `bar` (no multicast).
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes,
-                                         uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-            "r"(smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Bounded wait on an mbarrier phase.  Gives up after kWaitNs of wall time,
-// recording this launch's epoch in *status (atomicMax), or as soon as another
-// CTA of the same launch has recorded it.  Returns false when it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity, int *status,
-                                                  int epoch) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    for (;;) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*reinterpret_cast<volatile int *>(status) == epoch) return false;
-        if (global_ns() - t0 > kWaitNs) {
-            atomicMax(status, epoch);
-            return false;
-        }
-    }
-}
 
 // ------------------------------------------------------------------ kernel
 template <typename RT, int VEC, int NCH, int GT, bool BULK>
@@ -518,49 +458,24 @@ attn_kernel(AttnArgs a) {
         a.pm[slot * GT + tid] = s_m[tid];
         a.pl[slot * GT + tid] = s_l[tid];
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(a.cnt + grp, 1) == a.n_split - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // merge: M = max m_i, L = sum l_i 2^(m_i - M), O = sum acc_i 2^(m_i - M) / L
-    float *s_fac = sred;  // reuse: n_split x GT factors
-    if (tid < GT) {
-        float M = -INFINITY;
-        for (int i = 0; i < a.n_split; i++) M = fmaxf(M, __ldcg(a.pm + (grp * a.n_split + i) * GT + tid));
-        float L = 0.0f;
-        for (int i = 0; i < a.n_split; i++) {
-            const int64_t si = (grp * a.n_split + i) * GT + tid;
-            const float f = exp2f(__ldcg(a.pm + si) - M);
-            s_fac[i * GT + tid] = f;
-            L += __ldcg(a.pl + si) * f;
-        }
-        s_l[tid] = L;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < GT * a.D; idx += kThreads) {
-        const int g = idx / (int)a.D;
-        const int64_t d = idx % a.D;
-        if (g >= grun) continue;
-        float o = 0.0f;
-        for (int i = 0; i < a.n_split; i++)
-            o = fmaf(__ldcg(a.pacc + ((grp * a.n_split + i) * GT + g) * a.D + d), s_fac[i * GT + g], o);
-        store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, o / s_l[g]);
-    }
-    if (tid == 0) a.cnt[grp] = 0;  // ready for the next launch
+    __syncthreads();  // sred is reused as merge scratch below
+    const Partials P{a.cnt, a.pm, a.pl, a.pacc, a.n_split, GT, a.D};
+    merge_last_arriver(P, grp, split, s_m, s_l, sred, &s_last, a.out, a.out_dtype, b * a.o_sb,
+                       a.o_sh, hq0, grun, tid, kThreads);
 }
 
 // ---------------------------------------------------------------- planning
-// Launch epochs: a positive, increasing tag per call (wraps after 2^31 - 1).
-int next_epoch() {
-    static std::atomic<int> e{0};
-    int v = e.fetch_add(1) + 1;
-    if (v <= 0) {
-        e.store(1);
-        v = 1;
-    }
-    return v;
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+size_t workspace_for(int64_t units, int n_split, int GT, int64_t D) {
+    if (n_split <= 1) return kWsHeader;
+    const size_t slots = (size_t)units * n_split;
+    size_t w = kWsHeader;
+    w = align_up(w + (size_t)units * 4, 256);
+    w = align_up(w + slots * GT * 4, 256);
+    w = align_up(w + slots * GT * 4, 256);
+    w = align_up(w + slots * GT * D * 4, 256);
+    return w;
 }
 
 struct Plan {
@@ -577,7 +492,6 @@ inline int pick_gt(int64_t G) {
     return 8;
 }
 
-inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Shared by fc_decode_attn_workspace_size and fc_decode_attn so both agree.
 Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, int r,
@@ -638,24 +552,21 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     p.off_vsc = take((size_t)std::max(p.chunk, 1) * s * 4);
     p.off_sc = take(((size_t)std::max(p.chunk, 1) * s + raw_max) * p.GT * 4);
     p.off_lg = take(((size_t)std::max(p.chunk, 1) * r + raw_max) * p.GT * 4);
-    p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4, (size_t)p.n_split * p.GT * 4));
+    p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4, (size_t)(p.n_split + 1) * p.GT * 4));
     p.off_stat = take((size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4);
     p.off_ring = take(vec_mode == 2 ? (size_t)kStages * kStageBytes : 0);
     p.off_bar = take(vec_mode == 2 ? (size_t)kStages * 8 : 0);
     p.smem = off;
     // workspace: header | counters | pm | pl | pacc
-    if (p.n_split > 1) {
-        const size_t slots = (size_t)units * p.n_split;
-        size_t w = kWsHeader;
-        w = align_up(w + (size_t)units * 4, 256);
-        w = align_up(w + slots * p.GT * 4, 256);
-        w = align_up(w + slots * p.GT * 4, 256);
-        w = align_up(w + slots * p.GT * D * 4, 256);
-        p.ws = w;
-    } else {
-        p.ws = kWsHeader;
-    }
+    p.ws = workspace_for(units, p.n_split, p.GT, D);
     return p;
+}
+
+// Split plan of the tensor-core kernel: chunks of 512 code rows (4 tiles).
+void tc_plan(int64_t n, int s, int &n_split, int &chunk) {
+    const int c = tc_chunk_blocks(s);
+    n_split = (int)std::max<int64_t>(1, (n + c - 1) / c);
+    chunk = (int)((n + n_split - 1) / n_split);
 }
 
 int pick_vec_mode(int64_t D, int es, const void *k, const void *v, int64_t k_sb, int64_t k_sh,
@@ -702,6 +613,17 @@ int launch_rt(const Plan &p, AttnArgs &args, dim3 grid, cudaStream_t st) {
 }
 
 }  // namespace
+
+int next_epoch() {
+    static std::atomic<int> e{0};
+    int v = e.fetch_add(1) + 1;
+    if (v <= 0) {
+        e.store(1);
+        v = 1;
+    }
+    return v;
+}
+
 }  // namespace fc
 
 using namespace fc;
@@ -715,6 +637,11 @@ extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
     for (int es : {1, 2, 4})
         for (int vm : {0, 1, 2})
             w = std::max(w, make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm).ws);
+    if (n_blocks > 0 && s <= 32 && (32 % s) == 0 && Hq / Hk <= 8) {
+        int ns, chunk;
+        tc_plan(n_blocks, s, ns, chunk);
+        w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
+    }
     return w;
 }
 
@@ -748,6 +675,57 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
     if (!q || !out || (n_blocks > 0 && (!k_rows || !v_rows || !A))) { set_error("decode_attn: null pointer"); return FC_EINVAL; }
     if (n_blocks == 0) { s = 1; r = std::max<int>(r, 1); rows_dtype = FC_F32; }
 
+    const int sel = g_attn_kernel.load();
+    if (n_blocks > 0 && sel != FC_ATTN_CUDA_CORE) {
+        const int64_t G = Hq / Hk, row = (int64_t)s * D;
+        const bool contig = tc_supported(D, s, r, G, rows_dtype) && k_sj == D && k_sn == row &&
+                            v_sj == D && v_sn == row && k_sh % row == 0 && v_sh % row == 0 &&
+                            k_sb == Hk * k_sh && v_sb == Hk * v_sh && aligned(k_rows, 16) &&
+                            aligned(v_rows, 16) && n_raw < r;
+        if (contig) {
+            int ns, chunk;
+            tc_plan(n_blocks, s, ns, chunk);
+            const int GT = pick_gt(G);
+            const size_t need = workspace_for(B * Hk, ns, GT, D);
+            if (!workspace || workspace_bytes < need) {
+                set_error("decode_attn: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+                return FC_ERANGE;
+            }
+            if (!aligned(workspace, 256)) { set_error("decode_attn: workspace must be 256-byte aligned"); return FC_EINVAL; }
+            TcArgs t{};
+            t.q = q; t.q_dtype = q_dtype; t.q_sb = q_sb; t.q_sh = q_sh;
+            t.Hk = Hk; t.n = n_blocks; t.s = s; t.r = r; t.G = (int)G; t.GT = GT;
+            t.k_cap = k_sh / row; t.v_cap = v_sh / row;
+            t.ksc = k_scales; t.vsc = v_scales; t.sc_dtype = scale_dtype;
+            t.ks_sb = ks_sb; t.ks_sh = ks_sh; t.ks_sn = ks_sn;
+            t.vs_sb = vs_sb; t.vs_sh = vs_sh; t.vs_sn = vs_sn;
+            t.kraw = k_raw; t.vraw = v_raw; t.raw_dtype = raw_dtype;
+            t.kr_sb = kr_sb; t.kr_sh = kr_sh; t.kr_st = kr_st;
+            t.vr_sb = vr_sb; t.vr_sh = vr_sh; t.vr_st = vr_st;
+            t.n_raw = (int)n_raw; t.A = A; t.scale_log2 = softmax_scale * 1.4426950408889634f;
+            t.out = out; t.out_dtype = out_dtype; t.o_sb = o_sb; t.o_sh = o_sh;
+            t.n_split = ns; t.chunk = chunk;
+            unsigned char *wsb = static_cast<unsigned char *>(workspace);
+            t.status = reinterpret_cast<int *>(wsb);
+            t.epoch = next_epoch();
+            size_t off = kWsHeader;
+            t.cnt = reinterpret_cast<int *>(wsb + off);
+            off = align_up(off + (size_t)B * Hk * 4, 256);
+            const size_t slots = (size_t)B * Hk * ns;
+            t.pm = reinterpret_cast<float *>(wsb + off);
+            off = align_up(off + slots * GT * 4, 256);
+            t.pl = reinterpret_cast<float *>(wsb + off);
+            off = align_up(off + slots * GT * 4, 256);
+            t.pacc = reinterpret_cast<float *>(wsb + off);
+            return launch_attn_tc(t, B, k_rows, v_rows, B * Hk * (k_sh / row) * s,
+                                  B * Hk * (v_sh / row) * s, static_cast<cudaStream_t>(stream));
+        }
+        if (sel == FC_ATTN_TENSOR_CORE) {
+            set_error("decode_attn: the tensor-core kernel needs contiguous int8 (B,H,cap,s,128) "
+                      "archives with s | 32 and Hq/Hk <= 8");
+            return FC_ENOTSUP;
+        }
+    }
     const int es = dtype_size(rows_dtype);
     const int vm = n_blocks > 0 ? pick_vec_mode(D, es, k_rows, v_rows, k_sb, k_sh, k_sn, k_sj,
                                                 v_sb, v_sh, v_sn, v_sj, s)
@@ -805,4 +783,10 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
         case FC_F16: return launch_rt<__half>(p, a, grid, st);
         default: return launch_rt<float>(p, a, grid, st);
     }
+}
+
+extern "C" int fc_set_attn_kernel(int which) {
+    if (which != FC_ATTN_AUTO && which != FC_ATTN_CUDA_CORE && which != FC_ATTN_TENSOR_CORE)
+        return -1;
+    return g_attn_kernel.exchange(which);
 }

@@ -1,0 +1,171 @@
+// Pieces shared by the two decode-attention kernels: PTX wrappers for
+// mbarriers and bulk copies, bounded waits, the launch epoch, the arguments of
+// the tensor-core kernel, and the last-arriver log-sum-exp merge of split
+// partials.
+#pragma once
+
+#include <atomic>
+
+#include "fc_common.cuh"
+
+namespace fc {
+
+constexpr uint64_t kWaitNs = 100000000ull;  // 100 ms bound on any wait
+constexpr int kWsHeader = 256;              // workspace bytes before the counters
+
+// Launch epochs: a positive, increasing tag per call (wraps after 2^31 - 1).
+int next_epoch();
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  Gives up after kWaitNs of wall time,
+// recording this launch's epoch in *status (atomicMax), or as soon as another
+// CTA of the same launch has recorded it.  Returns false when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity, int *status,
+                                                  int epoch) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*reinterpret_cast<volatile int *>(status) == epoch) return false;
+        if (global_ns() - t0 > kWaitNs) {
+            atomicMax(status, epoch);
+            return false;
+        }
+    }
+}
+
+// 1D bulk async copy global -> shared, completing on `bar` (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Arguments of the tensor-core decode-attention kernel (fc_attention_tc.cu).
+struct TcArgs {
+    const void *q;
+    int q_dtype;
+    int64_t q_sb, q_sh;
+    int64_t Hk, n;
+    int s, r, G, GT;
+    int64_t k_cap, v_cap;  // archive capacity (blocks) per (batch, head)
+    const void *ksc, *vsc;
+    int sc_dtype;
+    int64_t ks_sb, ks_sh, ks_sn, vs_sb, vs_sh, vs_sn;
+    const void *kraw, *vraw;
+    int raw_dtype;
+    int64_t kr_sb, kr_sh, kr_st, vr_sb, vr_sh, vr_st;
+    int n_raw;
+    const float *A;
+    float scale_log2;
+    void *out;
+    int out_dtype;
+    int64_t o_sb, o_sh;
+    int n_split, chunk;
+    int *status;
+    int epoch;
+    int *cnt;
+    float *pm, *pl, *pacc;
+    // shared memory carve-up (bytes from a 1024-aligned base)
+    int off_bq, off_bw, off_lg, off_wf, off_ksc, off_vsc, off_qf, off_stat, off_bar;
+};
+
+// Partials of one split of one (batch, KV head, head group): running max m,
+// sum l (both per head, base-2 logits) and the unnormalised output acc[g][d].
+struct Partials {
+    int *cnt;
+    float *pm, *pl, *pacc;
+    int n_split, GT;
+    int64_t D;
+};
+
+// Publish this split's partials; the split that arrives last merges all of
+// them (M = max m_i, L = sum l_i 2^(m_i - M), O = sum acc_i 2^(m_i - M) / L)
+// and writes the output rows of heads [hq0, hq0 + grun).  `scratch` holds at
+// least (n_split + 1) * GT floats of shared memory; every thread of the CTA
+// calls this (it contains barriers).  The counter is left at zero.
+__device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t grp, int split,
+                                                   const float *s_m, const float *s_l,
+                                                   float *scratch, int *s_flag, void *out,
+                                                   int out_dtype, int64_t o_base, int64_t o_sh,
+                                                   int64_t hq0, int grun, int tid, int nthr) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *s_flag = (atomicAdd(P.cnt + grp, 1) == P.n_split - 1);
+    __syncthreads();
+    if (!*s_flag) return;
+    __threadfence();
+    float *fac = scratch;
+    float *Ls = scratch + P.n_split * P.GT;
+    if (tid < P.GT) {
+        float M = -INFINITY;
+        for (int i = 0; i < P.n_split; i++)
+            M = fmaxf(M, __ldcg(P.pm + (grp * P.n_split + i) * P.GT + tid));
+        float L = 0.0f;
+        for (int i = 0; i < P.n_split; i++) {
+            const int64_t si = (grp * P.n_split + i) * P.GT + tid;
+            const float f = exp2f(__ldcg(P.pm + si) - M);
+            fac[i * P.GT + tid] = f;
+            L += __ldcg(P.pl + si) * f;
+        }
+        Ls[tid] = L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < P.GT * P.D; idx += nthr) {
+        const int g = idx / (int)P.D;
+        const int64_t d = idx % P.D;
+        if (g >= grun) continue;
+        float o = 0.0f;
+        for (int i = 0; i < P.n_split; i++)
+            o = fmaf(__ldcg(P.pacc + ((grp * P.n_split + i) * P.GT + g) * P.D + d), fac[i * P.GT + g], o);
+        store_from_f32(out, o_base + (hq0 + g) * o_sh + d, out_dtype, o / Ls[g]);
+    }
+    if (tid == 0) P.cnt[grp] = 0;  // ready for the next launch
+}
+
+}  // namespace fc

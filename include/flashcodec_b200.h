@@ -228,6 +228,18 @@ FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t
                    const float *A, float softmax_scale,
                    void *out, int out_dtype, int64_t o_sb, int64_t o_sh, void *stream);
 
+/* Decode-attention kernel selection (process-wide; for tests and benchmarks).
+ * AUTO uses the tcgen05 int8 tensor-core kernel whenever the archive allows
+ * it (contiguous (B, Hk, cap, s, 128) int8 codes, s | 32, Hq/Hk <= 8) and the
+ * CUDA-core kernel otherwise.  CUDA_CORE forces the CUDA-core kernel;
+ * TENSOR_CORE makes unsupported layouts fail with FC_ENOTSUP instead of
+ * falling back.  Returns the previous setting, or -1 for an unknown value.
+ * No counterpart in the reference (it has one GPU kernel). */
+#define FC_ATTN_AUTO 0
+#define FC_ATTN_CUDA_CORE 1
+#define FC_ATTN_TENSOR_CORE 2
+FC_API int fc_set_attn_kernel(int which);
+
 #ifdef __cplusplus
 }
 #endif

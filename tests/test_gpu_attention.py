@@ -183,3 +183,48 @@ def test_cpu_tensors_are_rejected():
     import flashcodec_b200 as fc
     with pytest.raises(RuntimeError):
         fc.dct_compress(torch.randn(1, 1, 8, 16), 8, 2)
+
+
+@pytest.fixture
+def kernel_choice():
+    from flashcodec_b200 import _kernels as K
+    prev = K.set_attn_kernel("auto")
+    yield K.set_attn_kernel
+    K.set_attn_kernel(prev)
+
+
+@pytest.mark.parametrize("G,K,dt,S,tail,sdt", [
+    (4, 4, torch.bfloat16, 8 * 2000 + 0, 5, torch.float32),   # config-2 layer shape
+    (4, 2, torch.float32, 8 * 512, 1, torch.float32),         # config-1 shape, fp32 q/out
+    (8, 2, torch.bfloat16, 8 * 300, 3, torch.float32),        # N = 32 columns
+    (1, 1, torch.float16, 8 * 70, 0, torch.float32),          # s = 1
+    (3, 8, torch.bfloat16, 8 * 90, 7, torch.float32),         # s = 8, G not a power of 2
+    (4, 2, torch.bfloat16, 8 * 3000, 2, torch.float16),       # fp16 scales (config 5 format)
+    (2, 4, torch.bfloat16, 8 * 20, 4, torch.float32),         # one split, partial tile
+])
+def test_tensor_core_and_cuda_core_kernels_vs_oracle(kernel_choice, G, K, dt, S, tail, sdt):
+    """Both decode-attention kernels on the same archive against the oracle."""
+    import flashcodec_b200 as fc
+    B, Hk = 2, 4
+    k, v, q = bench.synth_case(B, Hk * G, Hk, S + tail, 128, 0.95, 23, dtype=dt)
+    kw = dict(keep_freqs=K, quant_bits=8, scale_dtype=sdt)
+    ks, vs = build("jpeg", kw, k.to(DEV), v.to(DEV))
+    ref = oracle_attention(q, ks, vs)
+    outs = {}
+    for which in ("tensor-core", "cuda-core"):
+        kernel_choice(which)
+        outs[which] = fc.codec_decode_attention(q.to(DEV), ks, vs)
+        check_close(outs[which], ref, dt)
+    from flashcodec_b200 import _kernels as Kn
+    assert Kn.attn_status(q.to(DEV).device) == 0
+
+
+def test_tensor_core_refuses_unsupported_layout(kernel_choice):
+    """Forcing the tensor-core kernel on a layout it does not take fails
+    loudly instead of silently using another kernel."""
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(1, 4, 2, 8 * 20, 64, 0.95, 3)   # head_dim 64
+    ks, vs = build("jpeg", dict(keep_freqs=2, quant_bits=8), k.to(DEV), v.to(DEV))
+    kernel_choice("tensor-core")
+    with pytest.raises(NotImplementedError):
+        fc.codec_decode_attention(q.to(DEV), ks, vs)
