@@ -9,28 +9,33 @@
 // the CUDA cores only touch one value per (row, head).
 //
 // Exact integer formulation.  q (per head g) and the softmax weights w (per
-// head) are written as three int8 limbs relative to a per-head scale sigma:
+// head, per tile) are written as three int8 limbs relative to a scale sigma:
 //     x / sigma = l0 + l1/128 + l2/16384,  |l0| <= 127, |l1|, |l2| <= 64,
 // which represents x to 2.4e-7 of max|x| (finer than fp32 accumulation of
 // the same dot products).  The tensor core then computes exact int32 sums:
 //   scores  S[row][(g,l)] = sum_d code[row][d] * qlimb[(g,l)][d]
 //           (A = code tile, K-major;  M = 128 rows, N = 16|32, K = 128)
-//   output  O[d][(g,l)]  += sum_row code_v[row][d] * wlimb[(g,l)][row]
+//   output  O[d][(g,l)]   = sum_row code_v[row][d] * wlimb[(g,l)][row]
 //           (A = the same kind of tile read MN-major: M = 128 = head_dim)
 // accumulated in TMEM.  One swizzled (128B) TMA tile of 128 code rows serves
 // as the K-major A operand for the scores and as the MN-major A operand for
 // the output.
 //
-// CTA = 5 warps.  Warp 4 lane 0 issues the TMA loads and the MMAs (the
-// producer); warps 0-3 (TMEM lane quarters 0-3) run the epilogues: scores ->
-// logits -> chunk softmax -> weights -> weight limbs, and finally the output.
-// Two passes over the chunk (K tiles, then V tiles) with the chunk max known
-// before any weight exists, so the int32 output accumulator is never rescaled.
+// Streaming pipeline per tile t of 128 archive rows (CTA = 5 warps; warp 4
+// lane 0 issues TMA and MMAs, warps 0-3 own TMEM lane quarters 0-3):
+//   producer: K MMA(t+1) | V MMA(t) once tile t's weight limbs are written
+//   epilogue: scores(t) -> logits -> tile max -> probabilities -> weights
+//             -> weight limbs -> (V result of tile t-1 folded into fp32
+//             registers with an online log-sum-exp rescale)
+// TMEM holds two score buffers and two output buffers, the weight-limb tile is
+// double-buffered in shared memory, and K and V tiles stream through a TMA ring,
+// so loads, MMAs and the CUDA-core epilogue of neighbouring tiles overlap.
 // Every wait is bounded (100 ms wall time, launch-epoch status word); an
 // aborting CTA waits (bounded) for its copies in flight and frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <math.h>
+#include <stdlib.h>
 
 #include <algorithm>
 
@@ -42,8 +47,9 @@ namespace {
 constexpr int kTcThreads = 160;
 constexpr int kTileRows = 128;
 constexpr int kTileBytes = kTileRows * 128;  // 128 rows x 128 code bytes
-constexpr int kTcStages = 4;
+constexpr int kTcStages = 3;                 // TMA ring depth (K and V tiles interleaved)
 constexpr int kLimbs = 3;
+constexpr int kDefaultChunkTiles = 8;        // tiles (of 128 rows) per split
 
 // ------------------------------------------------------------ tcgen05 PTX
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
@@ -136,72 +142,83 @@ __device__ __forceinline__ void limbs3(float x, int &l0, int &l1, int &l2) {
     l2 = (int)rintf(r2);
 }
 
-template <int N>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__device__ __forceinline__ float limb_value(const int32_t *v, int g) {
+    return (float)v[3 * g] + (float)v[3 * g + 1] * (1.0f / 128.0f) +
+           (float)v[3 * g + 2] * (1.0f / 16384.0f);
+}
+
+template <int GT>
+__global__ void __launch_bounds__(kTcThreads, 3)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                const TcArgs a) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *ring = smem;
-    unsigned char *bq = smem + a.off_bq;
-    unsigned char *bw = smem + a.off_bw;
-    float *lg = reinterpret_cast<float *>(smem + a.off_lg);
-    float *wf = reinterpret_cast<float *>(smem + a.off_wf);
-    float *sks = reinterpret_cast<float *>(smem + a.off_ksc);
-    float *svs = reinterpret_cast<float *>(smem + a.off_vsc);
-    float *qf = reinterpret_cast<float *>(smem + a.off_qf);  // G x 128 fp32 q
-    float *stat = reinterpret_cast<float *>(smem + a.off_stat);
+    unsigned char *bq = smem + a.off_bq;                 // N x 128 q limbs (K-major B)
+    unsigned char *bw = smem + a.off_bw;                 // 2 x N x 128 weight limbs
+    float *lgt = reinterpret_cast<float *>(smem + a.off_lg);   // tile logits / probabilities
+    float *sA = reinterpret_cast<float *>(smem + a.off_A);     // r x s synthesis matrix
+    float *qf = reinterpret_cast<float *>(smem + a.off_qf);    // G x 128 fp32 q
+    float *red = reinterpret_cast<float *>(smem + a.off_red);  // reductions, raw logits
+    float *scr = reinterpret_cast<float *>(smem + a.off_scr);  // merge scratch
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
-    uint64_t *full = bars;                   // [kTcStages] TMA landed
-    uint64_t *sdone = bars + kTcStages;      // [2] score MMA done (per TMEM buffer)
-    uint64_t *sfree = bars + kTcStages + 2;  // [2] scores read back (4 warps)
-    uint64_t *vstage = bars + kTcStages + 4; // output MMA of one tile done
-    uint64_t *vdone = bars + kTcStages + 5;  // all output MMAs done
+    uint64_t *full = bars;                    // [kTcStages] TMA landed
+    uint64_t *sdone = bars + kTcStages;       // [2] score MMA done
+    uint64_t *sfree = bars + kTcStages + 2;   // [2] scores read back (4 warps)
+    uint64_t *wready = bars + kTcStages + 4;  // [2] weight limbs written (4 warps)
+    uint64_t *vdone = bars + kTcStages + 6;   // [2] output MMA done
+    uint64_t *vfree = bars + kTcStages + 8;   // [2] output read back (4 warps)
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
+    __shared__ int s_abort;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool producer = warp == 4;
-    const int G = a.G, GT = a.GT, s = a.s, r = a.r;
+    constexpr int N = GT <= 4 ? 16 : 32;    // B columns: 3 limbs x GT heads, padded
+    const int G = a.G, s = a.s, r = a.r;
     const int split = blockIdx.x % a.n_split;
     const int64_t unit = blockIdx.x / a.n_split;
     const int64_t b = unit / a.Hk, hk = unit % a.Hk;
     const int64_t n0 = (int64_t)split * a.chunk;
     const int nb = (int)max((int64_t)0, min((int64_t)a.chunk, a.n - n0));
-    const int R = nb * s;                                  // code rows in this chunk
-    const int T = (R + kTileRows - 1) / kTileRows;         // tiles per pass
+    const int R = nb * s;                                  // code rows in this split
+    const int T = (R + kTileRows - 1) / kTileRows;         // tiles
     const int nraw = (split == a.n_split - 1) ? a.n_raw : 0;
     const int64_t hq0 = hk * G;
-    float *s_sq = stat;          // [GT] q scale per head
-    float *s_sw = stat + 8;      // [GT] weight scale per head
-    float *s_m = stat + 16;      // [GT] chunk max (base-2 logits)
-    float *s_l = stat + 24;      // [GT] chunk sum
-    float *s_red = stat + 32;    // [4 warps][GT] reduction scratch
+    // reduction slots: [parity][kind: 0 max, 1 sum, 2 |w| max][warp][8]
+    float *s_sq = red + 192;      // [8] q scale per head
+    float *s_fin = red + 200;     // [16] final M, L per head
+    float *rawlg = red + 216;     // [n_raw x GT] raw-tail logits
     const int64_t k_row0 = ((b * a.Hk + hk) * a.k_cap + n0) * s;  // first code row (tensor map y)
     const int64_t v_row0 = ((b * a.Hk + hk) * a.v_cap + n0) * s;
     const uint32_t idesc_s = i8_idesc(N, 0), idesc_o = i8_idesc(N, 1);
-    constexpr int kAlloc = N * 3 <= 64 ? 64 : 128;  // TMEM columns (power of 2 >= 32)
+    constexpr int kAlloc = N * 4 <= 64 ? 64 : 128;  // TMEM columns: 2 score + 2 output buffers
 
     // ---------------------------------------------------------------- setup
     int issued = 0, consumed = 0;  // producer bookkeeping (lane 0 of warp 4)
-    auto issue = [&](int u) {      // ring tile u: K tiles [0, T), V tiles [T, 2T)
+    auto issue = [&](int u) {      // ring tile u in consumption order K0, K1, V0, K2, V1, ...
         const int st = u % kTcStages;
-        const bool isk = u < T;
-        const int t = isk ? u : u - T;
+        bool isk;
+        int t;
+        if (u == 0) { isk = true; t = 0; }
+        else if (u <= 2 * T - 3) { isk = (u & 1) != 0; t = isk ? (u + 1) >> 1 : (u >> 1) - 1; }
+        else { isk = false; t = u - T; }
         const int y = (int)((isk ? k_row0 : v_row0) + (int64_t)t * kTileRows);
         mbar_expect_tx(full + st, kTileBytes);
         tma_load_2d(ring + st * kTileBytes, isk ? &tmk : &tmv, 0, y, full + st);
     };
+    if (tid == 0) s_abort = 0;
     if (producer) {
         if (lane == 0) {
             for (int i = 0; i < kTcStages; i++) mbar_init(full + i, 1);
-            mbar_init(sdone + 0, 1);
-            mbar_init(sdone + 1, 1);
-            mbar_init(sfree + 0, 4);
-            mbar_init(sfree + 1, 4);
-            mbar_init(vstage, 1);
-            mbar_init(vdone, 1);
+            for (int i = 0; i < 2; i++) {
+                mbar_init(sdone + i, 1);
+                mbar_init(sfree + i, 4);
+                mbar_init(wready + i, 4);
+                mbar_init(vdone + i, 1);
+                mbar_init(vfree + i, 4);
+            }
             fence_mbar_init();
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmk) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmv) : "memory");
@@ -216,9 +233,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     } else {
         // q of the group's heads: fp32 copy, per-head scale, int8 limbs (K-major B tile)
         const int d = tid;  // head_dim == 128 == epilogue threads
-        float qmax[8];
+        float qmax[GT];
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
+        for (int g = 0; g < GT; g++) {
             float v = 0.0f;
             if (g < G) v = load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype);
             if (g < G) qf[g * 128 + d] = v;
@@ -227,15 +244,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             qmax[g] = m;
         }
         if (lane == 0)
-            for (int g = 0; g < GT; g++) s_red[warp * GT + g] = qmax[g];
-        for (int i = tid; i < R; i += 128) {
-            const int blk = i / s, j = i % s;
-            sks[i] = load_as_f32(a.ksc, b * a.ks_sb + hk * a.ks_sh + (n0 + blk) * a.ks_sn + j, a.sc_dtype);
-            svs[i] = load_as_f32(a.vsc, b * a.vs_sb + hk * a.vs_sh + (n0 + blk) * a.vs_sn + j, a.sc_dtype);
-        }
+#pragma unroll
+            for (int g = 0; g < GT; g++) red[warp * 8 + g] = qmax[g];
+        for (int i = tid; i < r * s; i += 128) sA[i] = a.A[i];
         epi_bar();
         if (tid < GT) {
-            const float m = fmaxf(fmaxf(s_red[tid], s_red[GT + tid]), fmaxf(s_red[2 * GT + tid], s_red[3 * GT + tid]));
+            const float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
             s_sq[tid] = m > 0.0f ? m / 127.0f : 1.0f;
         }
         epi_bar();
@@ -248,239 +262,312 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 v = l == 0 ? l0 : (l == 1 ? l1 : l2);
             }
             bq[sw128_off(row, d)] = (unsigned char)(int8_t)v;
+            if (row >= kLimbs * G) {   // unused weight-limb rows stay zero in both buffers
+                bw[sw128_off(row, d)] = 0;
+                bw[N * 128 + sw128_off(row, d)] = 0;
+            }
         }
         fence_async_smem();
     }
     tc_fence_before();
-    __syncthreads();  // (1) barriers, TMEM address, q limbs and scales ready
+    __syncthreads();  // (1) barriers, TMEM address, q limbs, A ready
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     bool ab = false;
 
-    // ------------------------------------------------ pass 1: K tiles -> scores
     if (producer) {
-        if (lane == 0) {
-            for (int t = 0; t < T && !ab; t++) {
-                const int st = t % kTcStages;
-                if (!mbar_wait_bounded(full + st, (t / kTcStages) & 1, a.status, a.epoch)) { ab = true; break; }
-                if (t >= 2 && !mbar_wait_bounded(sfree + (t & 1), ((t - 2) >> 1) & 1, a.status, a.epoch)) { ab = true; break; }
-                tc_fence_after();
-                const uint32_t at = smem_addr(ring + st * kTileBytes), bt = smem_addr(bq);
+        // ------------------------------------------------------- producer
+        // Ring tiles are issued and consumed in one order: K0, K1, V0, K2, V1,
+        // ..., K(T-1), V(T-2), V(T-1) (the scores of tile t+1 are computed while
+        // the epilogue turns tile t into weights).  Each stage is refilled as
+        // soon as the MMA that read it has completed.
+        if (lane == 0 && T > 0) {
+            auto consume_tile = [&](int u, bool isk, int t) -> bool {
+                const int st = u % kTcStages;
+                if (!mbar_wait_bounded(full + st, (u / kTcStages) & 1, a.status, a.epoch)) return false;
+                const uint32_t at = smem_addr(ring + st * kTileBytes);
+                if (isk) {
+                    if (t >= 2 && !mbar_wait_bounded(sfree + (t & 1), ((t - 2) >> 1) & 1, a.status, a.epoch))
+                        return false;
+                    tc_fence_after();
+                    const uint32_t bt = smem_addr(bq);
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    mma_i8(tmem + (t & 1) * N, sw128_desc(at + k * 32), sw128_desc(bt + k * 32), idesc_s, k > 0);
-                mma_commit(sdone + (t & 1));
-                if (!mbar_wait_bounded(sdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) { ab = true; break; }
-                consumed = t + 1;
+                    for (int k = 0; k < 4; k++)
+                        mma_i8(tmem + (t & 1) * N, sw128_desc(at + k * 32), sw128_desc(bt + k * 32),
+                               idesc_s, k > 0);
+                    mma_commit(sdone + (t & 1));
+                    if (!mbar_wait_bounded(sdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
+                } else {
+                    if (!mbar_wait_bounded(wready + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
+                    if (t >= 2 && !mbar_wait_bounded(vfree + (t & 1), ((t - 2) >> 1) & 1, a.status, a.epoch))
+                        return false;
+                    tc_fence_after();
+                    const uint32_t bt = smem_addr(bw + (t & 1) * (N * 128));
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        mma_i8(tmem + (2 + (t & 1)) * N, sw128_desc(at + k * 4096),
+                               sw128_desc(bt + k * 32), idesc_o, k > 0);
+                    mma_commit(vdone + (t & 1));
+                    if (!mbar_wait_bounded(vdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
+                }
+                consumed = u + 1;
                 if (issued < 2 * T) issue(issued++);
+                return true;
+            };
+            bool ok = consume_tile(0, true, 0);
+            int u = 1;
+            for (int t = 0; ok && t < T; t++) {
+                if (t + 1 < T && !(ok = consume_tile(u++, true, t + 1))) break;
+                ok = consume_tile(u++, false, t);
             }
+            ab = !ok;
         }
     } else {
-        float tmax[8];
+        // ------------------------------------------------------- epilogue
+        const int jb = lane & ~(s - 1);   // first lane of this row's block (s | 32)
+        const int j = lane - jb;
+        const int lrow = warp * 32 + lane;          // row within the tile
+        const int lblk = lrow / s;                  // block within the tile
+        float M[GT], L[GT], acc[GT], pm[GT], pl[GT], psig[GT];
 #pragma unroll
-        for (int g = 0; g < 8; g++) tmax[g] = -INFINITY;
-        const int jb = lane & ~(s - 1);  // first lane of this row's block (s | 32)
-        for (int t = 0; t < T && !ab; t++) {
-            // warp-uniform outcome: tcgen05.ld below needs the whole warp
-            const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(sdone + (t & 1), (t >> 1) & 1,
+        for (int g = 0; g < GT; g++) {
+            M[g] = -INFINITY; L[g] = 0.0f; acc[g] = 0.0f; pm[g] = 0.0f; pl[g] = 0.0f; psig[g] = 1.0f;
+        }
+        auto scale_at = [&](const void *p, int64_t sb, int64_t sh, int64_t sn, int row) {
+            const int blk = row / s, jj = row % s;
+            return load_as_f32(p, b * sb + hk * sh + (n0 + blk) * sn + jj, a.sc_dtype);
+        };
+        // fold the output of tile u (pending stats pm/pl/psig) into M, L, acc
+        auto consume = [&](int u) {
+            const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(vdone + (u & 1), (u >> 1) & 1,
                                                                       a.status, a.epoch));
-            if (!ok) { ab = true; break; }
+            if (!ok) {
+                s_abort = 1;
+                return;
+            }
             tc_fence_after();
             int32_t v[N];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (t & 1) * N, v);
-            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (t & 1) * N + 16, v + 16);
+            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N, v);
+            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N + 16, v + 16);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(sfree + (t & 1));
-            const int row = t * kTileRows + warp * 32 + lane;
-            const bool valid = row < R;
-            const float ks = valid ? sks[row] : 0.0f;
-            float sg[8];
+            if (lane == 0) mbar_arrive(vfree + (u & 1));
 #pragma unroll
-            for (int g = 0; g < 8; g++) {
-                sg[g] = 0.0f;
-                if (g < G)
-                    sg[g] = ((float)v[3 * g] + (float)v[3 * g + 1] * (1.0f / 128.0f) +
-                             (float)v[3 * g + 2] * (1.0f / 16384.0f)) * s_sq[g] * ks;
+            for (int g = 0; g < GT; g++) {
+                if (g < G) {
+                    const float mn = fmaxf(M[g], pm[g]);
+                    const float f_old = exp2f(M[g] - mn), f_new = exp2f(pm[g] - mn);
+                    acc[g] = acc[g] * f_old + limb_value(v, g) * psig[g] * f_new;
+                    L[g] = L[g] * f_old + pl[g] * f_new;
+                    M[g] = mn;
+                }
             }
-            // logits of this block: lane j of the block takes positions j, j+s, ...
-            const int j = lane - jb;
-            const int blk = row / s;
+        };
+        float ks_next = 0.0f, vs_next = 0.0f;
+        if (T > 0 && lrow < R) {
+            ks_next = scale_at(a.ksc, a.ks_sb, a.ks_sh, a.ks_sn, lrow);
+            vs_next = scale_at(a.vsc, a.vs_sb, a.vs_sh, a.vs_sn, lrow);
+        }
+        for (int t = 0; t < T; t++) {
+            const int par = t & 1;
+            const int row = t * kTileRows + lrow;
+            const bool valid = row < R;
+            const float ks = ks_next, vsr = vs_next;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(sdone + par, (t >> 1) & 1,
+                                                                      a.status, a.epoch));
+            if (!ok) s_abort = 1;
+            epi_bar();
+            if (s_abort) { ab = true; break; }
+            // prefetch the next tile's row scales
+            if (row + kTileRows < R) {
+                ks_next = scale_at(a.ksc, a.ks_sb, a.ks_sh, a.ks_sn, row + kTileRows);
+                vs_next = scale_at(a.vsc, a.vs_sb, a.vs_sh, a.vs_sn, row + kTileRows);
+            }
+            tc_fence_after();
+            int32_t v[N];
+            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N, v);
+            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N + 16, v + 16);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfree + par);
+            float sg[GT];
+#pragma unroll
+            for (int g = 0; g < GT; g++) sg[g] = (g < G && valid) ? limb_value(v, g) * s_sq[g] * ks : 0.0f;
+            // logits of this block: lane j takes positions j, j+s, ...
+            float tmax[GT];
+#pragma unroll
+            for (int g = 0; g < GT; g++) tmax[g] = -INFINITY;
             for (int p0 = 0; p0 < r; p0 += s) {
                 const int p = p0 + j;
-                float lgv[8];
+                float lgv[GT];
 #pragma unroll
-                for (int g = 0; g < 8; g++) lgv[g] = 0.0f;
+                for (int g = 0; g < GT; g++) lgv[g] = 0.0f;
                 for (int jj = 0; jj < s; jj++) {
-                    const float am = (p < r) ? a.A[p * s + jj] : 0.0f;
+                    const float am = (p < r) ? sA[p * s + jj] : 0.0f;
 #pragma unroll
-                    for (int g = 0; g < 8; g++) {
-                        const float o = __shfl_sync(0xffffffffu, sg[g], jb + jj);
-                        if (g < G) lgv[g] = fmaf(am, o, lgv[g]);
+                    for (int g = 0; g < GT; g++) {
+                        if (g < G) lgv[g] = fmaf(am, __shfl_sync(0xffffffffu, sg[g], jb + jj), lgv[g]);
                     }
                 }
-                if (valid && p < r) {
+                if (p < r) {
 #pragma unroll
-                    for (int g = 0; g < 8; g++) {
+                    for (int g = 0; g < GT; g++) {
                         if (g < G) {
-                            const float x = lgv[g] * a.scale_log2;
-                            lg[(blk * r + p) * GT + g] = x;
+                            const float x = valid ? lgv[g] * a.scale_log2 : -INFINITY;
+                            lgt[(lblk * r + p) * GT + g] = x;
                             tmax[g] = fmaxf(tmax[g], x);
                         }
                     }
                 }
             }
-        }
-        // raw tail logits (last split): warp w takes tokens w, w+4, ...
-        for (int t = warp; t < nraw && !ab; t += 4) {
-            float part[8];
 #pragma unroll
-            for (int g = 0; g < 8; g++) part[g] = 0.0f;
-            for (int d = lane; d < 128; d += 32) {
-                const float x = load_as_f32(a.kraw, b * a.kr_sb + hk * a.kr_sh + (int64_t)t * a.kr_st + d, a.raw_dtype);
+            for (int g = 0; g < GT; g++)
+                for (int off = 16; off > 0; off >>= 1) tmax[g] = fmaxf(tmax[g], __shfl_xor_sync(0xffffffffu, tmax[g], off));
+            if (lane == 0)
 #pragma unroll
-                for (int g = 0; g < 8; g++)
-                    if (g < G) part[g] = fmaf(qf[g * 128 + d], x, part[g]);
-            }
+                for (int g = 0; g < GT; g++) red[((par * 3 + 0) * 4 + warp) * 8 + g] = tmax[g];
+            epi_bar();
+            float mt[GT];
 #pragma unroll
-            for (int g = 0; g < 8; g++) {
-                for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-                if (g < G) {
-                    const float x = part[g] * a.scale_log2;
-                    if (lane == 0) lg[(nb * r + t) * GT + g] = x;
-                    tmax[g] = fmaxf(tmax[g], x);
-                }
+            for (int g = 0; g < GT; g++) {
+                const float *rm = red + (par * 3 + 0) * 32 + g;
+                mt[g] = fmaxf(fmaxf(rm[0], rm[8]), fmaxf(rm[16], rm[24]));
             }
-        }
+            // probabilities in place (this lane's positions), partial sums
+            float lsum[GT];
 #pragma unroll
-        for (int g = 0; g < 8; g++)
-            for (int off = 16; off > 0; off >>= 1) tmax[g] = fmaxf(tmax[g], __shfl_xor_sync(0xffffffffu, tmax[g], off));
-        if (lane == 0)
-            for (int g = 0; g < GT; g++) s_red[warp * GT + g] = tmax[g];
-    }
-    ab = __syncthreads_or(ab);  // (2) all scores consumed (or a wait gave up)
-
-    // ------------------------- chunk softmax, weights, weight limbs (warps 0-3)
-    if (!producer && !ab) {
-        if (tid < GT) {
-            s_m[tid] = fmaxf(fmaxf(s_red[tid], s_red[GT + tid]), fmaxf(s_red[2 * GT + tid], s_red[3 * GT + tid]));
-        }
-        epi_bar();
-        const int npos = nb * r + nraw;
-        const int my_g = tid % GT;
-        float tsum = 0.0f;
-        for (int idx = tid; idx < npos * GT; idx += 128) {
-            if (my_g < G) {
-                const float p = exp2f(lg[idx] - s_m[my_g]);
-                lg[idx] = p;
-                tsum += p;
-            }
-        }
-        for (int off = 16; off >= GT; off >>= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
-        if (lane < GT) s_red[warp * GT + lane] = tsum;
-        epi_bar();
-        if (tid < GT) s_l[tid] = s_red[tid] + s_red[GT + tid] + s_red[2 * GT + tid] + s_red[3 * GT + tid];
-        // w[row][g] = vscale[row] * sum_p p[blk*r+p][g] A[p][j]
-        float wmax = 0.0f;
-        for (int idx = tid; idx < R * GT; idx += 128) {
-            const int row = idx / GT, blk = row / s, j = row % s;
-            float w = 0.0f;
-            if (my_g < G) {
-                for (int p = 0; p < r; p++) w = fmaf(lg[(blk * r + p) * GT + my_g], a.A[p * s + j], w);
-                w *= svs[row];
-            }
-            wf[idx] = w;
-            wmax = fmaxf(wmax, fabsf(w));
-        }
-        for (int off = 16; off >= GT; off >>= 1) wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
-        epi_bar();
-        if (lane < GT) s_red[warp * GT + lane] = wmax;
-        epi_bar();
-        if (tid < GT) {
-            const float m = fmaxf(fmaxf(s_red[tid], s_red[GT + tid]), fmaxf(s_red[2 * GT + tid], s_red[3 * GT + tid]));
-            s_sw[tid] = m > 0.0f ? m / 127.0f : 1.0f;
-        }
-        epi_bar();
-        // weight limbs: tile t, B row (g, l), column = row within the tile;
-        // four consecutive columns per 32-bit store (inside one 16-byte chunk)
-        const int words = T * N * (kTileRows / 4);
-        for (int wi = tid; wi < words; wi += 128) {
-            const int t = wi / (N * 32), rem = wi % (N * 32);
-            const int brow = rem / 32, c4 = (rem % 32) * 4;
-            const int g = brow / kLimbs, l = brow % kLimbs;
-            uint32_t packed = 0;
-            if (g < G) {
-                for (int e = 0; e < 4; e++) {
-                    const int row = t * kTileRows + c4 + e;
-                    int val = 0;
-                    if (row < R) {
-                        int l0, l1, l2;
-                        limbs3(wf[row * GT + g] / s_sw[g], l0, l1, l2);
-                        val = l == 0 ? l0 : (l == 1 ? l1 : l2);
+            for (int g = 0; g < GT; g++) lsum[g] = 0.0f;
+            for (int p = j; p < r; p += s) {
+#pragma unroll
+                for (int g = 0; g < GT; g++) {
+                    if (g < G) {
+                        float* cell = &lgt[(lblk * r + p) * GT + g];
+                        const float pr = valid ? exp2f(*cell - mt[g]) : 0.0f;
+                        *cell = pr;
+                        lsum[g] += pr;
                     }
-                    packed |= ((uint32_t)(val & 0xFF)) << (8 * e);
                 }
             }
-            *reinterpret_cast<uint32_t *>(bw + t * (N * 128) + sw128_off(brow, c4)) = packed;
-        }
-        fence_async_smem();
-    }
-    tc_fence_before();
-    __syncthreads();  // (3) weight limbs ready
-    tc_fence_after();
-
-    // ----------------------------------------- pass 2: V tiles -> output (int32)
-    if (producer) {
-        if (lane == 0 && !ab) {
-            for (int t = 0; t < T; t++) {
-                const int u = T + t, st = u % kTcStages;
-                if (!mbar_wait_bounded(full + st, (u / kTcStages) & 1, a.status, a.epoch)) { ab = true; break; }
-                tc_fence_after();
-                const uint32_t at = smem_addr(ring + st * kTileBytes);
-                const uint32_t bt = smem_addr(bw + t * (N * 128));
+            __syncwarp();  // the block's probabilities were written by lanes of this warp
+            // weights of this row: w = vscale * sum_p P[p] A[p][j]
+            float wv[GT], wmax[GT];
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    mma_i8(tmem + 2 * N, sw128_desc(at + k * 4096), sw128_desc(bt + k * 32), idesc_o,
-                           (t > 0 || k > 0) ? 1u : 0u);
-                mma_commit(vstage);
-                if (!mbar_wait_bounded(vstage, t & 1, a.status, a.epoch)) { ab = true; break; }
-                consumed = u + 1;
-                if (issued < 2 * T) issue(issued++);
+            for (int g = 0; g < GT; g++) wv[g] = 0.0f;
+            if (valid) {
+                for (int p = 0; p < r; p++) {
+                    const float am = sA[p * s + j];
+#pragma unroll
+                    for (int g = 0; g < GT; g++)
+                        if (g < G) wv[g] = fmaf(lgt[(lblk * r + p) * GT + g], am, wv[g]);
+                }
             }
-            if (!ab) mma_commit(vdone);
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                wv[g] *= vsr;
+                wmax[g] = fabsf(wv[g]);
+                for (int off = 16; off > 0; off >>= 1) {
+                    lsum[g] += __shfl_xor_sync(0xffffffffu, lsum[g], off);
+                    wmax[g] = fmaxf(wmax[g], __shfl_xor_sync(0xffffffffu, wmax[g], off));
+                }
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int g = 0; g < GT; g++) {
+                    red[((par * 3 + 1) * 4 + warp) * 8 + g] = lsum[g];
+                    red[((par * 3 + 2) * 4 + warp) * 8 + g] = wmax[g];
+                }
+            }
+            epi_bar();
+            float lt[GT], sig[GT];
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                const float *rs = red + (par * 3 + 1) * 32 + g;
+                const float *rw = red + (par * 3 + 2) * 32 + g;
+                lt[g] = rs[0] + rs[8] + rs[16] + rs[24];
+                const float wm = fmaxf(fmaxf(rw[0], rw[8]), fmaxf(rw[16], rw[24]));
+                sig[g] = wm > 0.0f ? wm / 127.0f : 1.0f;
+            }
+            // weight limbs of this row (column lrow of the B tile)
+            unsigned char *bwt = bw + par * (N * 128);
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                if (g < G) {
+                    int l0 = 0, l1 = 0, l2 = 0;
+                    if (valid) limbs3(wv[g] / sig[g], l0, l1, l2);
+                    bwt[sw128_off(3 * g + 0, lrow)] = (unsigned char)(int8_t)l0;
+                    bwt[sw128_off(3 * g + 1, lrow)] = (unsigned char)(int8_t)l1;
+                    bwt[sw128_off(3 * g + 2, lrow)] = (unsigned char)(int8_t)l2;
+                }
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(wready + par);
+            // the previous tile's output, then this tile's stats become pending
+            if (t >= 1) consume(t - 1);
+#pragma unroll
+            for (int g = 0; g < GT; g++) { pm[g] = mt[g]; pl[g] = lt[g]; psig[g] = sig[g]; }
         }
-    }
-    float acc[8];
+        if (!ab && T > 0) consume(T - 1);
+        epi_bar();  // a failed wait in any warp's consume() is seen by all warps
+        if (s_abort) ab = true;
+        // raw tail (last split), folded in fp32 like one more tile
+        if (!ab && nraw > 0) {
+            for (int t = warp; t < nraw; t += 4) {
+                float part[GT];
 #pragma unroll
-    for (int g = 0; g < 8; g++) acc[g] = 0.0f;
-    if (!producer && !ab) {
-        const int d = tid;
-        if (T > 0) {
-            if (__all_sync(0xffffffffu, mbar_wait_bounded(vdone, 0, a.status, a.epoch))) {
-                tc_fence_after();
-                int32_t v[N];
-                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + 2 * N, v);
-                if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + 2 * N + 16, v + 16);
-                tmem_wait_ld();
+                for (int g = 0; g < GT; g++) part[g] = 0.0f;
+                for (int d = lane; d < 128; d += 32) {
+                    const float x = load_as_f32(a.kraw, b * a.kr_sb + hk * a.kr_sh + (int64_t)t * a.kr_st + d, a.raw_dtype);
 #pragma unroll
-                for (int g = 0; g < 8; g++)
-                    if (g < G)
-                        acc[g] = ((float)v[3 * g] + (float)v[3 * g + 1] * (1.0f / 128.0f) +
-                                  (float)v[3 * g + 2] * (1.0f / 16384.0f)) * s_sw[g];
+                    for (int g = 0; g < GT; g++)
+                        if (g < G) part[g] = fmaf(qf[g * 128 + d], x, part[g]);
+                }
+#pragma unroll
+                for (int g = 0; g < GT; g++) {
+                    for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+                    if (lane == 0 && g < GT) rawlg[t * GT + g] = part[g] * a.scale_log2;
+                }
+            }
+            epi_bar();
+            const int d = tid;
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                if (g < G) {
+                    float mr = -INFINITY;
+                    for (int t = 0; t < nraw; t++) mr = fmaxf(mr, rawlg[t * GT + g]);
+                    const float mn = fmaxf(M[g], mr);
+                    const float f = exp2f(M[g] - mn);
+                    acc[g] *= f;
+                    L[g] *= f;
+                    for (int t = 0; t < nraw; t++) {
+                        const float pr = exp2f(rawlg[t * GT + g] - mn);
+                        const float x = load_as_f32(a.vraw, b * a.vr_sb + hk * a.vr_sh + (int64_t)t * a.vr_st + d, a.raw_dtype);
+                        L[g] += pr;
+                        acc[g] = fmaf(pr, x, acc[g]);
+                    }
+                    M[g] = mn;
+                }
+            }
+        }
+        if (!ab) {
+            const int d = tid;
+            if (a.n_split == 1) {
+                for (int g = 0; g < G; g++)
+                    store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, acc[g] / L[g]);
             } else {
-                ab = true;
+                const int64_t slot = unit * a.n_split + split;
+                for (int g = 0; g < GT; g++) a.pacc[(slot * GT + g) * 128 + d] = g < G ? acc[g] : 0.0f;
+                if (tid < GT) {
+                    a.pm[slot * GT + tid] = tid < G ? M[tid] : 0.0f;
+                    a.pl[slot * GT + tid] = tid < G ? L[tid] : 1.0f;
+                }
             }
-        }
-        for (int t = 0; t < nraw; t++) {
-            const float x = load_as_f32(a.vraw, b * a.vr_sb + hk * a.vr_sh + (int64_t)t * a.vr_st + d, a.raw_dtype);
-#pragma unroll
-            for (int g = 0; g < 8; g++)
-                if (g < G) acc[g] = fmaf(lg[(nb * r + t) * GT + g], x, acc[g]);
         }
     }
     tc_fence_before();
-    ab = __syncthreads_or(ab);  // (4) TMEM reads done
+    ab = __syncthreads_or(ab);  // (2) all TMEM reads done
     tc_fence_after();
     if (producer) {
         if (ab && lane == 0) {
@@ -495,28 +582,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         __syncwarp();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAlloc));
     }
-    if (ab) return;
+    if (ab || a.n_split == 1) return;
 
-    // ---------------------------------------------------- partials and merge
-    const int64_t grp = unit;
-    if (a.n_split == 1) {
-        if (!producer) {
-            for (int g = 0; g < G; g++)
-                store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + tid, a.out_dtype, acc[g] / s_l[g]);
-        }
-        return;
-    }
-    const int64_t slot = grp * a.n_split + split;
-    if (!producer) {
-        for (int g = 0; g < GT; g++) a.pacc[(slot * GT + g) * 128 + tid] = g < G ? acc[g] : 0.0f;
-        if (tid < GT) {
-            a.pm[slot * GT + tid] = tid < G ? s_m[tid] : 0.0f;
-            a.pl[slot * GT + tid] = tid < G ? s_l[tid] : 1.0f;
-        }
+    // ------------------------------------------- last-arriver merge of splits
+    if (tid < GT) {
+        s_fin[tid] = a.pm[(unit * a.n_split + split) * GT + tid];
+        s_fin[8 + tid] = a.pl[(unit * a.n_split + split) * GT + tid];
     }
     const Partials P{a.cnt, a.pm, a.pl, a.pacc, a.n_split, GT, 128};
-    merge_last_arriver(P, grp, split, s_m, s_l, wf, &s_last, a.out, a.out_dtype, b * a.o_sb,
-                       a.o_sh, hq0, G, tid, kTcThreads);
+    merge_last_arriver(P, unit, split, s_fin, s_fin + 8, scr, &s_last, a.out, a.out_dtype,
+                       b * a.o_sb, a.o_sh, hq0, G, tid, kTcThreads);
 }
 
 // ----------------------------------------------------------------- host side
@@ -550,14 +625,26 @@ bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows) {
 
 size_t align_to(size_t x, size_t al) { return (x + al - 1) / al * al; }
 
+int chunk_tiles() {
+    static int tiles = [] {
+        const char *e = getenv("FLASHCODEC_TC_CHUNK_TILES");  // tuning override (1..64)
+        const int v = e ? atoi(e) : 0;
+        return (v >= 1 && v <= 64) ? v : kDefaultChunkTiles;
+    }();
+    return tiles;
+}
+
 }  // namespace
 
-// Chunk (blocks per split) used by the tensor-core path: 4 tiles of 128 rows.
-int tc_chunk_blocks(int s) { return 4 * kTileRows / s; }
+// Blocks per split of the tensor-core path: chunk_tiles() tiles of 128 rows.
+int tc_chunk_blocks(int s) { return chunk_tiles() * kTileRows / s; }
 
 bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype) {
+    // tile logits buffer (128/s blocks x r positions x GT heads) <= 32 KB
+    const int64_t GT = G <= 1 ? 1 : (G <= 2 ? 2 : (G <= 4 ? 4 : 8));
     return D == 128 && rows_dtype == FC_I8 && s >= 1 && s <= 32 && (32 % s) == 0 && r >= s &&
-           r <= 64 && G >= 1 && G <= 8 && get_encode() != nullptr;
+           r <= 64 && G >= 1 && G <= 8 && (kTileRows / s) * r * GT * 4 <= 32768 &&
+           get_encode() != nullptr;
 }
 
 int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, int64_t krows_total,
@@ -567,35 +654,35 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
         set_error("decode_attn: tensor map encoding failed");
         return FC_ECUDA;
     }
-    const int N = a.G * kLimbs <= 16 ? 16 : 32;
-    const int chunk = a.chunk, R = chunk * a.s;
+    const int N = a.GT <= 4 ? 16 : 32;
     size_t off = (size_t)kTcStages * kTileBytes;
     a.off_bq = (int)off;
     off = align_to(off + (size_t)N * 128, 1024);
     a.off_bw = (int)off;
-    off += (size_t)4 * N * 128;
+    off += (size_t)2 * N * 128;
     a.off_lg = (int)off;
-    off = align_to(off + ((size_t)chunk * a.r + a.n_raw + 1) * a.GT * 4, 16);
-    a.off_wf = (int)off;
-    off = align_to(off + std::max((size_t)R * a.GT * 4, (size_t)(a.n_split + 1) * a.GT * 4), 16);
-    a.off_ksc = (int)off;
-    off += (size_t)R * 4;
-    a.off_vsc = (int)off;
-    off += (size_t)R * 4;
+    off = align_to(off + (size_t)(kTileRows / a.s) * a.r * a.GT * 4, 16);
+    a.off_A = (int)off;
+    off = align_to(off + (size_t)a.r * a.s * 4, 16);
     a.off_qf = (int)off;
     off += (size_t)8 * 128 * 4;
-    a.off_stat = (int)off;
-    off += 64 * 4;
+    a.off_red = (int)off;
+    off = align_to(off + (size_t)(216 + 64 * 8) * 4, 16);
+    a.off_scr = (int)off;
+    off = align_to(off + (size_t)(a.n_split + 1) * a.GT * 4, 16);
     a.off_bar = (int)align_to(off, 8);
-    off = a.off_bar + 16 * 8;
+    off = a.off_bar + (kTcStages + 10) * 8;
     const size_t smem = off + 1024;  // room to align the dynamic base to 1024
     dim3 grid((unsigned)(B * a.Hk * a.n_split));
-    if (N == 16) {
-        cudaFuncSetAttribute(attn_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_tc_kernel<16><<<grid, kTcThreads, smem, st>>>(mk, mv, a);
-    } else {
-        cudaFuncSetAttribute(attn_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_tc_kernel<32><<<grid, kTcThreads, smem, st>>>(mk, mv, a);
+    auto go = [&](auto kern) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, kTcThreads, smem, st>>>(mk, mv, a);
+    };
+    switch (a.GT) {
+        case 1: go(attn_tc_kernel<1>); break;
+        case 2: go(attn_tc_kernel<2>); break;
+        case 4: go(attn_tc_kernel<4>); break;
+        default: go(attn_tc_kernel<8>); break;
     }
     return check_launch("decode_attn (tcgen05)");
 }
