@@ -637,7 +637,7 @@ extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
     for (int es : {1, 2, 4})
         for (int vm : {0, 1, 2})
             w = std::max(w, make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm).ws);
-    if (n_blocks > 0 && s <= 32 && (32 % s) == 0 && Hq / Hk <= 8) {
+    if (n_blocks > 0 && r == 8 && s <= 8 && (8 % s) == 0 && Hq / Hk <= 8) {
         int ns, chunk;
         tc_plan(n_blocks, s, ns, chunk);
         w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
@@ -722,7 +722,7 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
         }
         if (sel == FC_ATTN_TENSOR_CORE) {
             set_error("decode_attn: the tensor-core kernel needs contiguous int8 (B,H,cap,s,128) "
-                      "archives with s | 32 and Hq/Hk <= 8");
+                      "archives with block size 8, s in {1,2,4,8} and Hq/Hk <= 8");
             return FC_ENOTSUP;
         }
     }

@@ -9,10 +9,12 @@
 // the CUDA cores only touch one value per (row, head).
 //
 // Exact integer formulation.  q (per head g) and the softmax weights w (per
-// head, per tile) are written as three int8 limbs relative to a scale sigma:
-//     x / sigma = l0 + l1/128 + l2/16384,  |l0| <= 127, |l1|, |l2| <= 64,
-// which represents x to 2.4e-7 of max|x| (finer than fp32 accumulation of
-// the same dot products).  The tensor core then computes exact int32 sums:
+// head, per tile) are written as four int8 limbs relative to a scale sigma:
+//     x / sigma = l0 + l1/2^7 + l2/2^14 + l3/2^21,  |l0| <= 127, |l1..3| <= 64,
+// which represents x to 2^-22 of sigma (below fp32 rounding of the same dot
+// products; three limbs, 2^-15, left q.k errors near 1e-5 of the logits).
+// 4 limbs x GT heads fill N = 16 (GT <= 4) or 32 (GT = 8) B columns.  The
+// tensor core then computes exact int32 sums:
 //   scores  S[row][(g,l)] = sum_d code[row][d] * qlimb[(g,l)][d]
 //           (A = code tile, K-major;  M = 128 rows, N = 16|32, K = 128)
 //   output  O[d][(g,l)]   = sum_row code_v[row][d] * wlimb[(g,l)][row]
@@ -24,9 +26,14 @@
 // Streaming pipeline per tile t of 128 archive rows (CTA = 5 warps; warp 4
 // lane 0 issues TMA and MMAs, warps 0-3 own TMEM lane quarters 0-3):
 //   producer: K MMA(t+1) | V MMA(t) once tile t's weight limbs are written
-//   epilogue: scores(t) -> logits -> tile max -> probabilities -> weights
-//             -> weight limbs -> (V result of tile t-1 folded into fp32
-//             registers with an online log-sum-exp rescale)
+//   epilogue: scores(t) -> logits -> warp max -> probabilities -> weights
+//             (all in registers, block synthesis by xor shuffles) -> one
+//             exchange of warp maxima across the 4 warps -> weight limbs ->
+//             (V result of tile t-1 folded into fp32 registers; every rescale
+//             is an exact power of two)
+// The kernel takes archives of block length 8 with s in {1, 2, 4, 8} stored
+// rows per block (every configuration of the benchmarks); other shapes use the
+// CUDA-core kernel.
 // TMEM holds two score buffers and two output buffers, the weight-limb tile is
 // double-buffered in shared memory, and K and V tiles stream through a TMA ring,
 // so loads, MMAs and the CUDA-core epilogue of neighbouring tiles overlap.
@@ -48,7 +55,8 @@ constexpr int kTcThreads = 160;
 constexpr int kTileRows = 128;
 constexpr int kTileBytes = kTileRows * 128;  // 128 rows x 128 code bytes
 constexpr int kTcStages = 3;                 // TMA ring depth (K and V tiles interleaved)
-constexpr int kLimbs = 3;
+constexpr int kLimbs = 4;
+constexpr int kR = 8;                        // archive block length this kernel takes
 constexpr int kDefaultChunkTiles = 8;        // tiles (of 128 rows) per split
 
 // ------------------------------------------------------------ tcgen05 PTX
@@ -131,36 +139,70 @@ __device__ __forceinline__ int sw128_off(int row, int col) {
     return (row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 4) ^ (row & 7)) & 7) << 4) + (col & 15);
 }
 
-// x (|x| <= 127 after scaling) -> limbs l0 + l1/128 + l2/16384.
-__device__ __forceinline__ void limbs3(float x, int &l0, int &l1, int &l2) {
-    const float a = rintf(x);
-    const float r1 = (x - a) * 128.0f;
-    const float b = rintf(r1);
-    const float r2 = (r1 - b) * 128.0f;
-    l0 = (int)a;
-    l1 = (int)b;
-    l2 = (int)rintf(r2);
+// x (|x| <= 127 after scaling) -> limbs l[0] + l[1]/2^7 + l[2]/2^14 + l[3]/2^21
+// (q, once per CTA).
+__device__ __forceinline__ void limbs4(float x, int l[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float a = rintf(x);
+        l[i] = (int)a;
+        x = (x - a) * 128.0f;
+    }
 }
 
 __device__ __forceinline__ float limb_value(const int32_t *v, int g) {
-    return (float)v[3 * g] + (float)v[3 * g + 1] * (1.0f / 128.0f) +
-           (float)v[3 * g + 2] * (1.0f / 16384.0f);
+    const float lo = fmaf((float)v[4 * g + 3], 1.0f / 128.0f, (float)v[4 * g + 2]);
+    return fmaf(lo, 1.0f / 16384.0f, fmaf((float)v[4 * g + 1], 1.0f / 128.0f, (float)v[4 * g]));
 }
 
-template <int GT>
+// 2^(e - 127) as fp32 from a biased exponent e, clamped to [0, 254] (0 gives +0).
+__device__ __forceinline__ float pow2_biased(int e) {
+    return __int_as_float(min(max(e, 0), 254) << 23);
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {  // PTX ex2.approx.ftz.f32
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// x + 1.5 * 2^23 rounds x (|x| < 2^22) to the nearest integer, ties to even,
+// and leaves that integer's two's-complement low byte in the low byte of the
+// sum's bit pattern.
+constexpr float kRoundMagic = 12582912.0f;
+constexpr int kMaxLog = 1 << 29;  // clamp of the integer logit maxima
+
+// Epilogue of one archive block row, for block length kR = 8 and s = S stored
+// rows per block.  The S lanes of a block (lane = block * S + j, j the stored
+// frequency) own positions p = j + k * S (k < 8 / S).  Synthesis matrix entries
+// are held per lane in xor-relative order, Ar[k][x] = A[j + kS][j ^ x], so that
+// both directions of the block synthesis are butterflies over xor partners:
+//   logit[p]  = sum_x Ar[k][x] * sg(lane ^ x)          (gather, S-1 shuffles)
+//   weight[j] = sum_p P[p] A[p][j], reduce-scatter: c[x] = sum_k P[k] Ar[k][x]
+//               holds this lane's share of frequency j ^ x; halving rounds
+//               c[x] += shfl_xor(c[x + h], h) leave frequency j's total in c[0].
+//
+// Softmax bookkeeping uses integer maxima so that every rescale is an exact
+// power of two: a warp's max m_w = floor(max logit) + 1; the CTA's tile max
+// m = max_w m_w; the weight limbs of tile t are relative to
+// sigma = 2^(AX - m - 132), AX = max_w (biased exponent of max|w| + m_w), which
+// keeps |w / sigma| < 64.  The running reference Mref (per head) is the max of
+// the tile maxima; acc and the per-thread partial sums L live in 2^Mref units.
+template <int GT, int S>
 __global__ void __launch_bounds__(kTcThreads, 3)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                const TcArgs a) {
+    constexpr int N = GT <= 4 ? 16 : 32;  // B columns: 4 limbs x GT heads, padded
+    constexpr int PP = kR / S;            // positions of a block per lane
+    constexpr int XS = 2 * GT + 1;        // exchange words per warp and tile
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *ring = smem;
-    unsigned char *bq = smem + a.off_bq;                 // N x 128 q limbs (K-major B)
-    unsigned char *bw = smem + a.off_bw;                 // 2 x N x 128 weight limbs
-    float *lgt = reinterpret_cast<float *>(smem + a.off_lg);   // tile logits / probabilities
-    float *sA = reinterpret_cast<float *>(smem + a.off_A);     // r x s synthesis matrix
-    float *qf = reinterpret_cast<float *>(smem + a.off_qf);    // G x 128 fp32 q
-    float *red = reinterpret_cast<float *>(smem + a.off_red);  // reductions, raw logits
+    unsigned char *bq = smem + a.off_bq;                       // N x 128 q limbs (K-major B)
+    unsigned char *bw = smem + a.off_bw;                       // 2 x N x 128 weight limbs
+    int *xch = reinterpret_cast<int *>(smem + a.off_xch);      // [2][4][XS] tile exchange, [4] flags
+    float *red = reinterpret_cast<float *>(smem + a.off_red);  // small reductions
     float *scr = reinterpret_cast<float *>(smem + a.off_scr);  // merge scratch
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
     uint64_t *full = bars;                    // [kTcStages] TMA landed
@@ -171,27 +213,26 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     uint64_t *vfree = bars + kTcStages + 8;   // [2] output read back (4 warps)
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
-    __shared__ int s_abort;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool producer = warp == 4;
-    constexpr int N = GT <= 4 ? 16 : 32;    // B columns: 3 limbs x GT heads, padded
-    const int G = a.G, s = a.s, r = a.r;
+    const int G = a.G;
     const int split = blockIdx.x % a.n_split;
     const int64_t unit = blockIdx.x / a.n_split;
     const int64_t b = unit / a.Hk, hk = unit % a.Hk;
     const int64_t n0 = (int64_t)split * a.chunk;
     const int nb = (int)max((int64_t)0, min((int64_t)a.chunk, a.n - n0));
-    const int R = nb * s;                                  // code rows in this split
+    const int R = nb * S;                                  // code rows in this split
     const int T = (R + kTileRows - 1) / kTileRows;         // tiles
     const int nraw = (split == a.n_split - 1) ? a.n_raw : 0;
     const int64_t hq0 = hk * G;
-    // reduction slots: [parity][kind: 0 max, 1 sum, 2 |w| max][warp][8]
-    float *s_sq = red + 192;      // [8] q scale per head
-    float *s_fin = red + 200;     // [16] final M, L per head
-    float *rawlg = red + 216;     // [n_raw x GT] raw-tail logits
-    const int64_t k_row0 = ((b * a.Hk + hk) * a.k_cap + n0) * s;  // first code row (tensor map y)
-    const int64_t v_row0 = ((b * a.Hk + hk) * a.v_cap + n0) * s;
+    float *s_sq = red + 32;       // [8] q scale per head
+    float *s_fin = red + 40;      // [16] final M, L per head
+    float *lred = red + 56;       // [4 warps][8] partial sums
+    float *rawlg = red + 88;      // [n_raw x GT] raw-tail logits
+    int *s_badf = xch + 2 * 4 * XS;  // [4] abort flags after the last tile
+    const int64_t k_row0 = ((b * a.Hk + hk) * a.k_cap + n0) * S;  // first code row (tensor map y)
+    const int64_t v_row0 = ((b * a.Hk + hk) * a.v_cap + n0) * S;
     const uint32_t idesc_s = i8_idesc(N, 0), idesc_o = i8_idesc(N, 1);
     constexpr int kAlloc = N * 4 <= 64 ? 64 : 128;  // TMEM columns: 2 score + 2 output buffers
 
@@ -208,7 +249,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         mbar_expect_tx(full + st, kTileBytes);
         tma_load_2d(ring + st * kTileBytes, isk ? &tmk : &tmv, 0, y, full + st);
     };
-    if (tid == 0) s_abort = 0;
+    float qv[GT];  // q of the group's heads at d = tid (epilogue threads)
     if (producer) {
         if (lane == 0) {
             for (int i = 0; i < kTcStages; i++) mbar_init(full + i, 1);
@@ -231,46 +272,40 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         if (lane == 0)
             for (; issued < min(kTcStages, 2 * T); issued++) issue(issued);
     } else {
-        // q of the group's heads: fp32 copy, per-head scale, int8 limbs (K-major B tile)
+        // q of the group's heads: per-head scale, int8 limbs (K-major B tile)
         const int d = tid;  // head_dim == 128 == epilogue threads
-        float qmax[GT];
 #pragma unroll
         for (int g = 0; g < GT; g++) {
             float v = 0.0f;
             if (g < G) v = load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype);
-            if (g < G) qf[g * 128 + d] = v;
+            qv[g] = v;
             float m = fabsf(v);
             for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            qmax[g] = m;
+            if (lane == 0) red[warp * 8 + g] = m;
         }
-        if (lane == 0)
-#pragma unroll
-            for (int g = 0; g < GT; g++) red[warp * 8 + g] = qmax[g];
-        for (int i = tid; i < r * s; i += 128) sA[i] = a.A[i];
         epi_bar();
         if (tid < GT) {
             const float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
             s_sq[tid] = m > 0.0f ? m / 127.0f : 1.0f;
         }
         epi_bar();
+#pragma unroll
         for (int row = 0; row < N; row++) {
             const int g = row / kLimbs, l = row % kLimbs;
             int v = 0;
-            if (g < G) {
-                int l0, l1, l2;
-                limbs3(qf[g * 128 + d] / s_sq[g], l0, l1, l2);
-                v = l == 0 ? l0 : (l == 1 ? l1 : l2);
+            if (g < GT && g < G) {
+                int lq[4];
+                limbs4(qv[g] / s_sq[g], lq);
+                v = lq[l];
             }
             bq[sw128_off(row, d)] = (unsigned char)(int8_t)v;
-            if (row >= kLimbs * G) {   // unused weight-limb rows stay zero in both buffers
-                bw[sw128_off(row, d)] = 0;
-                bw[N * 128 + sw128_off(row, d)] = 0;
-            }
+            bw[sw128_off(row, d)] = 0;
+            bw[N * 128 + sw128_off(row, d)] = 0;
         }
         fence_async_smem();
     }
     tc_fence_before();
-    __syncthreads();  // (1) barriers, TMEM address, q limbs, A ready
+    __syncthreads();  // (1) barriers, TMEM address, q limbs ready
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     bool ab = false;
@@ -324,194 +359,203 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         }
     } else {
         // ------------------------------------------------------- epilogue
-        const int jb = lane & ~(s - 1);   // first lane of this row's block (s | 32)
-        const int j = lane - jb;
-        const int lrow = warp * 32 + lane;          // row within the tile
-        const int lblk = lrow / s;                  // block within the tile
-        float M[GT], L[GT], acc[GT], pm[GT], pl[GT], psig[GT];
+        const int j = lane & (S - 1);
+        const int lrow = warp * 32 + lane;  // row within the tile (= TMEM lane, = d)
+        float Ar[PP][S];
+#pragma unroll
+        for (int k = 0; k < PP; k++)
+#pragma unroll
+            for (int x = 0; x < S; x++) Ar[k][x] = __ldg(a.A + (j + k * S) * S + (j ^ x));
+        float cq[GT], acc[GT], Ls[GT];
+        int Mref[GT], AXp[GT];
 #pragma unroll
         for (int g = 0; g < GT; g++) {
-            M[g] = -INFINITY; L[g] = 0.0f; acc[g] = 0.0f; pm[g] = 0.0f; pl[g] = 0.0f; psig[g] = 1.0f;
+            cq[g] = s_sq[g] * a.scale_log2;
+            acc[g] = 0.0f;
+            Ls[g] = 0.0f;
+            Mref[g] = -kMaxLog - 1;
+            AXp[g] = 0;
         }
-        auto scale_at = [&](const void *p, int64_t sb, int64_t sh, int64_t sn, int row) {
-            const int blk = row / s, jj = row % s;
-            return load_as_f32(p, b * sb + hk * sh + (n0 + blk) * sn + jj, a.sc_dtype);
+        const int64_t ksb = b * a.ks_sb + hk * a.ks_sh + n0 * a.ks_sn;
+        const int64_t vsb = b * a.vs_sb + hk * a.vs_sh + n0 * a.vs_sn;
+        const bool sc16 = a.sc_dtype == FC_F16;
+        auto scale_at = [&](const void *p, int64_t base, int64_t sn, int row) -> float {
+            const int64_t i = base + (int64_t)(row / S) * sn + (row & (S - 1));
+            return sc16 ? __half2float(static_cast<const __half *>(p)[i])
+                        : static_cast<const float *>(p)[i];
         };
-        // fold the output of tile u (pending stats pm/pl/psig) into M, L, acc
-        auto consume = [&](int u) {
+        // fold the output of tile u (limbs relative to 2^(AXp - 132)) into acc
+        auto fold = [&](int u) -> bool {
             const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(vdone + (u & 1), (u >> 1) & 1,
                                                                       a.status, a.epoch));
-            if (!ok) {
-                s_abort = 1;
-                return;
-            }
+            if (!ok) return false;
             tc_fence_after();
-            int32_t v[N];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N, v);
-            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N + 16, v + 16);
+            int32_t o[N];
+            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N, o);
+            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N + 16, o + 16);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(vfree + (u & 1));
 #pragma unroll
-            for (int g = 0; g < GT; g++) {
-                if (g < G) {
-                    const float mn = fmaxf(M[g], pm[g]);
-                    const float f_old = exp2f(M[g] - mn), f_new = exp2f(pm[g] - mn);
-                    acc[g] = acc[g] * f_old + limb_value(v, g) * psig[g] * f_new;
-                    L[g] = L[g] * f_old + pl[g] * f_new;
-                    M[g] = mn;
-                }
-            }
+            for (int g = 0; g < GT; g++)
+                acc[g] = fmaf(limb_value(o, g), pow2_biased(AXp[g] - 5 - Mref[g]), acc[g]);
+            return true;
         };
+        int pend_bad = 0;
         float ks_next = 0.0f, vs_next = 0.0f;
         if (T > 0 && lrow < R) {
-            ks_next = scale_at(a.ksc, a.ks_sb, a.ks_sh, a.ks_sn, lrow);
-            vs_next = scale_at(a.vsc, a.vs_sb, a.vs_sh, a.vs_sn, lrow);
+            ks_next = scale_at(a.ksc, ksb, a.ks_sn, lrow);
+            vs_next = scale_at(a.vsc, vsb, a.vs_sn, lrow);
         }
         for (int t = 0; t < T; t++) {
             const int par = t & 1;
             const int row = t * kTileRows + lrow;
-            const bool valid = row < R;
             const float ks = ks_next, vsr = vs_next;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(sdone + par, (t >> 1) & 1,
-                                                                      a.status, a.epoch));
-            if (!ok) s_abort = 1;
-            epi_bar();
-            if (s_abort) { ab = true; break; }
-            // prefetch the next tile's row scales
-            if (row + kTileRows < R) {
-                ks_next = scale_at(a.ksc, a.ks_sb, a.ks_sh, a.ks_sn, row + kTileRows);
-                vs_next = scale_at(a.vsc, a.vs_sb, a.vs_sh, a.vs_sn, row + kTileRows);
+            if (row + kTileRows < R) {  // the next tile's row scales
+                ks_next = scale_at(a.ksc, ksb, a.ks_sn, row + kTileRows);
+                vs_next = scale_at(a.vsc, vsb, a.vs_sn, row + kTileRows);
+            } else {
+                ks_next = 0.0f;
+                vs_next = 0.0f;
             }
-            tc_fence_after();
-            int32_t v[N];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N, v);
-            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N + 16, v + 16);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(sfree + par);
-            float sg[GT];
-#pragma unroll
-            for (int g = 0; g < GT; g++) sg[g] = (g < G && valid) ? limb_value(v, g) * s_sq[g] * ks : 0.0f;
-            // logits of this block: lane j takes positions j, j+s, ...
-            float tmax[GT];
-#pragma unroll
-            for (int g = 0; g < GT; g++) tmax[g] = -INFINITY;
-            for (int p0 = 0; p0 < r; p0 += s) {
-                const int p = p0 + j;
-                float lgv[GT];
-#pragma unroll
-                for (int g = 0; g < GT; g++) lgv[g] = 0.0f;
-                for (int jj = 0; jj < s; jj++) {
-                    const float am = (p < r) ? sA[p * s + jj] : 0.0f;
-#pragma unroll
-                    for (int g = 0; g < GT; g++) {
-                        if (g < G) lgv[g] = fmaf(am, __shfl_sync(0xffffffffu, sg[g], jb + jj), lgv[g]);
-                    }
-                }
-                if (p < r) {
-#pragma unroll
-                    for (int g = 0; g < GT; g++) {
-                        if (g < G) {
-                            const float x = valid ? lgv[g] * a.scale_log2 : -INFINITY;
-                            lgt[(lblk * r + p) * GT + g] = x;
-                            tmax[g] = fmaxf(tmax[g], x);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < GT; g++)
-                for (int off = 16; off > 0; off >>= 1) tmax[g] = fmaxf(tmax[g], __shfl_xor_sync(0xffffffffu, tmax[g], off));
-            if (lane == 0)
-#pragma unroll
-                for (int g = 0; g < GT; g++) red[((par * 3 + 0) * 4 + warp) * 8 + g] = tmax[g];
-            epi_bar();
-            float mt[GT];
-#pragma unroll
-            for (int g = 0; g < GT; g++) {
-                const float *rm = red + (par * 3 + 0) * 32 + g;
-                mt[g] = fmaxf(fmaxf(rm[0], rm[8]), fmaxf(rm[16], rm[24]));
-            }
-            // probabilities in place (this lane's positions), partial sums
-            float lsum[GT];
-#pragma unroll
-            for (int g = 0; g < GT; g++) lsum[g] = 0.0f;
-            for (int p = j; p < r; p += s) {
+            int mw[GT], wx[GT];
+            float w[GT], lsum[GT];
+            const bool okS = __all_sync(0xffffffffu, mbar_wait_bounded(sdone + par, (t >> 1) & 1,
+                                                                       a.status, a.epoch));
+            if (okS) {
+                tc_fence_after();
+                int32_t v[N];
+                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N, v);
+                if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N + 16, v + 16);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sfree + par);
+                const bool mask = row >= R;  // rows past the split (last tile only)
 #pragma unroll
                 for (int g = 0; g < GT; g++) {
-                    if (g < G) {
-                        float* cell = &lgt[(lblk * r + p) * GT + g];
-                        const float pr = valid ? exp2f(*cell - mt[g]) : 0.0f;
-                        *cell = pr;
-                        lsum[g] += pr;
+                    const float sg = limb_value(v, g) * (cq[g] * ks);
+                    float lg[PP];
+#pragma unroll
+                    for (int k = 0; k < PP; k++) lg[k] = Ar[k][0] * sg;
+#pragma unroll
+                    for (int x = 1; x < S; x++) {
+                        const float o = __shfl_xor_sync(0xffffffffu, sg, x);
+#pragma unroll
+                        for (int k = 0; k < PP; k++) lg[k] = fmaf(Ar[k][x], o, lg[k]);
                     }
+                    float mx = lg[0];
+#pragma unroll
+                    for (int k = 1; k < PP; k++) mx = fmaxf(mx, lg[k]);
+                    if (mask) mx = -INFINITY;
+                    int mi = __reduce_max_sync(0xffffffffu, __float2int_rd(mx));
+                    mi = min(max(mi, -kMaxLog), kMaxLog) + 1;
+                    const float mf = (float)mi;
+                    float P[PP], ls = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < PP; k++) {
+                        P[k] = mask ? 0.0f : ex2_approx(lg[k] - mf);
+                        ls += P[k];
+                    }
+                    float c[S];
+#pragma unroll
+                    for (int x = 0; x < S; x++) {
+                        c[x] = P[0] * Ar[0][x];
+#pragma unroll
+                        for (int k = 1; k < PP; k++) c[x] = fmaf(P[k], Ar[k][x], c[x]);
+                    }
+#pragma unroll
+                    for (int h = S / 2; h >= 1; h >>= 1)
+#pragma unroll
+                        for (int x = 0; x < h; x++) c[x] += __shfl_xor_sync(0xffffffffu, c[x + h], h);
+                    w[g] = c[0] * vsr;
+                    const unsigned wb =
+                        __reduce_max_sync(0xffffffffu, __float_as_uint(w[g]) & 0x7fffffffu);
+                    mw[g] = mi;
+                    wx[g] = (int)(wb >> 23) + mi;
+                    lsum[g] = ls;
                 }
             }
-            __syncwarp();  // the block's probabilities were written by lanes of this warp
-            // weights of this row: w = vscale * sum_p P[p] A[p][j]
-            float wv[GT], wmax[GT];
-#pragma unroll
-            for (int g = 0; g < GT; g++) wv[g] = 0.0f;
-            if (valid) {
-                for (int p = 0; p < r; p++) {
-                    const float am = sA[p * s + j];
-#pragma unroll
-                    for (int g = 0; g < GT; g++)
-                        if (g < G) wv[g] = fmaf(lgt[(lblk * r + p) * GT + g], am, wv[g]);
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < GT; g++) {
-                wv[g] *= vsr;
-                wmax[g] = fabsf(wv[g]);
-                for (int off = 16; off > 0; off >>= 1) {
-                    lsum[g] += __shfl_xor_sync(0xffffffffu, lsum[g], off);
-                    wmax[g] = fmaxf(wmax[g], __shfl_xor_sync(0xffffffffu, wmax[g], off));
-                }
-            }
+            // one exchange per tile: warp maxima, weight exponents, abort flags
+            int *xw = xch + (par * 4 + warp) * XS;
             if (lane == 0) {
+                if (okS) {
 #pragma unroll
-                for (int g = 0; g < GT; g++) {
-                    red[((par * 3 + 1) * 4 + warp) * 8 + g] = lsum[g];
-                    red[((par * 3 + 2) * 4 + warp) * 8 + g] = wmax[g];
+                    for (int g = 0; g < GT; g++) { xw[g] = mw[g]; xw[GT + g] = wx[g]; }
                 }
+                xw[2 * GT] = (okS ? 0 : 1) | pend_bad;
             }
             epi_bar();
-            float lt[GT], sig[GT];
+            const int *xr = xch + par * 4 * XS;
+            if (xr[2 * GT] | xr[XS + 2 * GT] | xr[2 * XS + 2 * GT] | xr[3 * XS + 2 * GT]) {
+                ab = true;
+                break;
+            }
+            int m[GT], AX[GT];
 #pragma unroll
             for (int g = 0; g < GT; g++) {
-                const float *rs = red + (par * 3 + 1) * 32 + g;
-                const float *rw = red + (par * 3 + 2) * 32 + g;
-                lt[g] = rs[0] + rs[8] + rs[16] + rs[24];
-                const float wm = fmaxf(fmaxf(rw[0], rw[8]), fmaxf(rw[16], rw[24]));
-                sig[g] = wm > 0.0f ? wm / 127.0f : 1.0f;
+                m[g] = max(max(xr[g], xr[XS + g]), max(xr[2 * XS + g], xr[3 * XS + g]));
+                AX[g] = max(max(xr[GT + g], xr[XS + GT + g]), max(xr[2 * XS + GT + g], xr[3 * XS + GT + g]));
             }
             // weight limbs of this row (column lrow of the B tile)
             unsigned char *bwt = bw + par * (N * 128);
 #pragma unroll
             for (int g = 0; g < GT; g++) {
-                if (g < G) {
-                    int l0 = 0, l1 = 0, l2 = 0;
-                    if (valid) limbs3(wv[g] / sig[g], l0, l1, l2);
-                    bwt[sw128_off(3 * g + 0, lrow)] = (unsigned char)(int8_t)l0;
-                    bwt[sw128_off(3 * g + 1, lrow)] = (unsigned char)(int8_t)l1;
-                    bwt[sw128_off(3 * g + 2, lrow)] = (unsigned char)(int8_t)l2;
-                }
+                // x = w * 2^(132 + m_w - AX), |x| < 64, applied in two exact halves
+                // (each factor <= 2^66) so that no factor overflows
+                const int e = 132 + mw[g] - AX[g], e1 = e >> 1;
+                const float x = (w[g] * pow2_biased(127 + e1)) * pow2_biased(127 + e - e1);
+                const float y0 = x + kRoundMagic;
+                const float d0 = x - (y0 - kRoundMagic);
+                const float y1 = fmaf(d0, 128.0f, kRoundMagic);
+                const float d1 = fmaf(d0, 128.0f, -(y1 - kRoundMagic));
+                const float y2 = fmaf(d1, 128.0f, kRoundMagic);
+                const float d2 = fmaf(d1, 128.0f, -(y2 - kRoundMagic));
+                const float y3 = fmaf(d2, 128.0f, kRoundMagic);
+                bwt[sw128_off(4 * g + 0, lrow)] = (unsigned char)__float_as_uint(y0);
+                bwt[sw128_off(4 * g + 1, lrow)] = (unsigned char)__float_as_uint(y1);
+                bwt[sw128_off(4 * g + 2, lrow)] = (unsigned char)__float_as_uint(y2);
+                bwt[sw128_off(4 * g + 3, lrow)] = (unsigned char)__float_as_uint(y3);
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(wready + par);
-            // the previous tile's output, then this tile's stats become pending
-            if (t >= 1) consume(t - 1);
+            // the previous tile's output (in the reference before this tile's max)
+            if (t >= 1 && !fold(t - 1)) pend_bad = 1;
+            // this tile's max joins the running reference; the local sums join L
 #pragma unroll
-            for (int g = 0; g < GT; g++) { pm[g] = mt[g]; pl[g] = lt[g]; psig[g] = sig[g]; }
+            for (int g = 0; g < GT; g++) {
+                if (m[g] > Mref[g]) {
+                    const float f = pow2_biased(127 + Mref[g] - m[g]);
+                    acc[g] *= f;
+                    Ls[g] *= f;
+                    Mref[g] = m[g];
+                }
+                Ls[g] = fmaf(lsum[g], pow2_biased(127 + mw[g] - Mref[g]), Ls[g]);
+                AXp[g] = AX[g];
+            }
         }
-        if (!ab && T > 0) consume(T - 1);
-        epi_bar();  // a failed wait in any warp's consume() is seen by all warps
-        if (s_abort) ab = true;
+        float M[GT], L[GT];
+#pragma unroll
+        for (int g = 0; g < GT; g++) { M[g] = 0.0f; L[g] = 1.0f; }
+        if (!ab) {
+            if (T > 0 && !fold(T - 1)) pend_bad = 1;
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                float l = Ls[g];
+                for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+                if (lane == 0) lred[warp * 8 + g] = l;
+            }
+            if (lane == 0) s_badf[warp] = pend_bad;
+            epi_bar();
+            ab = (s_badf[0] | s_badf[1] | s_badf[2] | s_badf[3]) != 0;
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                M[g] = (float)Mref[g];
+                L[g] = (lred[g] + lred[8 + g]) + (lred[16 + g] + lred[24 + g]);
+            }
+        }
         // raw tail (last split), folded in fp32 like one more tile
         if (!ab && nraw > 0) {
             for (int t = warp; t < nraw; t += 4) {
@@ -521,13 +565,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 for (int d = lane; d < 128; d += 32) {
                     const float x = load_as_f32(a.kraw, b * a.kr_sb + hk * a.kr_sh + (int64_t)t * a.kr_st + d, a.raw_dtype);
 #pragma unroll
-                    for (int g = 0; g < GT; g++)
-                        if (g < G) part[g] = fmaf(qf[g * 128 + d], x, part[g]);
+                    for (int g = 0; g < GT; g++) {
+                        const float qd = g < G ? load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype) : 0.0f;
+                        part[g] = fmaf(qd, x, part[g]);
+                    }
                 }
 #pragma unroll
                 for (int g = 0; g < GT; g++) {
                     for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-                    if (lane == 0 && g < GT) rawlg[t * GT + g] = part[g] * a.scale_log2;
+                    if (lane == 0) rawlg[t * GT + g] = part[g] * a.scale_log2;
                 }
             }
             epi_bar();
@@ -554,14 +600,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         if (!ab) {
             const int d = tid;
             if (a.n_split == 1) {
-                for (int g = 0; g < G; g++)
-                    store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, acc[g] / L[g]);
+#pragma unroll
+                for (int g = 0; g < GT; g++)
+                    if (g < G)
+                        store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, acc[g] / L[g]);
             } else {
                 const int64_t slot = unit * a.n_split + split;
+#pragma unroll
                 for (int g = 0; g < GT; g++) a.pacc[(slot * GT + g) * 128 + d] = g < G ? acc[g] : 0.0f;
-                if (tid < GT) {
-                    a.pm[slot * GT + tid] = tid < G ? M[tid] : 0.0f;
-                    a.pl[slot * GT + tid] = tid < G ? L[tid] : 1.0f;
+                if (tid == 0) {
+#pragma unroll
+                    for (int g = 0; g < GT; g++) {
+                        a.pm[slot * GT + g] = g < G ? M[g] : 0.0f;
+                        a.pl[slot * GT + g] = g < G ? L[g] : 1.0f;
+                    }
                 }
             }
         }
@@ -640,11 +692,8 @@ int chunk_tiles() {
 int tc_chunk_blocks(int s) { return chunk_tiles() * kTileRows / s; }
 
 bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype) {
-    // tile logits buffer (128/s blocks x r positions x GT heads) <= 32 KB
-    const int64_t GT = G <= 1 ? 1 : (G <= 2 ? 2 : (G <= 4 ? 4 : 8));
-    return D == 128 && rows_dtype == FC_I8 && s >= 1 && s <= 32 && (32 % s) == 0 && r >= s &&
-           r <= 64 && G >= 1 && G <= 8 && (kTileRows / s) * r * GT * 4 <= 32768 &&
-           get_encode() != nullptr;
+    return D == 128 && rows_dtype == FC_I8 && r == kR && (s == 1 || s == 2 || s == 4 || s == 8) &&
+           G >= 1 && G <= 8 && get_encode() != nullptr;
 }
 
 int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, int64_t krows_total,
@@ -660,14 +709,10 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
     off = align_to(off + (size_t)N * 128, 1024);
     a.off_bw = (int)off;
     off += (size_t)2 * N * 128;
-    a.off_lg = (int)off;
-    off = align_to(off + (size_t)(kTileRows / a.s) * a.r * a.GT * 4, 16);
-    a.off_A = (int)off;
-    off = align_to(off + (size_t)a.r * a.s * 4, 16);
-    a.off_qf = (int)off;
-    off += (size_t)8 * 128 * 4;
+    a.off_xch = (int)off;
+    off = align_to(off + (size_t)(2 * 4 * (2 * a.GT + 1) + 4) * 4, 16);
     a.off_red = (int)off;
-    off = align_to(off + (size_t)(216 + 64 * 8) * 4, 16);
+    off = align_to(off + (size_t)(88 + 8 * 8) * 4, 16);
     a.off_scr = (int)off;
     off = align_to(off + (size_t)(a.n_split + 1) * a.GT * 4, 16);
     a.off_bar = (int)align_to(off, 8);
@@ -678,11 +723,20 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         kern<<<grid, kTcThreads, smem, st>>>(mk, mv, a);
     };
+    auto by_s = [&](auto gt) {
+        constexpr int GT = decltype(gt)::value;
+        switch (a.s) {
+            case 1: go(attn_tc_kernel<GT, 1>); break;
+            case 2: go(attn_tc_kernel<GT, 2>); break;
+            case 4: go(attn_tc_kernel<GT, 4>); break;
+            default: go(attn_tc_kernel<GT, 8>); break;
+        }
+    };
     switch (a.GT) {
-        case 1: go(attn_tc_kernel<1>); break;
-        case 2: go(attn_tc_kernel<2>); break;
-        case 4: go(attn_tc_kernel<4>); break;
-        default: go(attn_tc_kernel<8>); break;
+        case 1: by_s(std::integral_constant<int, 1>{}); break;
+        case 2: by_s(std::integral_constant<int, 2>{}); break;
+        case 4: by_s(std::integral_constant<int, 4>{}); break;
+        default: by_s(std::integral_constant<int, 8>{}); break;
     }
     return check_launch("decode_attn (tcgen05)");
 }

@@ -112,7 +112,7 @@ struct TcArgs {
     int *cnt;
     float *pm, *pl, *pacc;
     // shared memory carve-up (bytes from a 1024-aligned base)
-    int off_bq, off_bw, off_lg, off_A, off_qf, off_red, off_scr, off_bar;
+    int off_bq, off_bw, off_xch, off_red, off_scr, off_bar;
 };
 
 // Partials of one split of one (batch, KV head, head group): running max m,
