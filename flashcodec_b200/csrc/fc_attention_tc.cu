@@ -45,6 +45,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "fc_attn_common.cuh"
 
@@ -150,9 +151,12 @@ __device__ __forceinline__ void limbs4(float x, int l[4]) {
     }
 }
 
+// v0 + v1/2^7 + v2/2^14 + v3/2^21 from the four limb columns of head g; the
+// limb pairs are joined in int32 (|v0| < 2^21, so v0 * 2^7 + v1 fits).
 __device__ __forceinline__ float limb_value(const int32_t *v, int g) {
-    const float lo = fmaf((float)v[4 * g + 3], 1.0f / 128.0f, (float)v[4 * g + 2]);
-    return fmaf(lo, 1.0f / 16384.0f, fmaf((float)v[4 * g + 1], 1.0f / 128.0f, (float)v[4 * g]));
+    const float hi = (float)(v[4 * g] * 128 + v[4 * g + 1]);
+    const float lo = (float)(v[4 * g + 2] * 128 + v[4 * g + 3]);
+    return fmaf(lo, 1.0f / 2097152.0f, hi * (1.0f / 128.0f));
 }
 
 // 2^(e - 127) as fp32 from a biased exponent e, clamped to [0, 254] (0 gives +0).
@@ -194,14 +198,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                const TcArgs a) {
     constexpr int N = GT <= 4 ? 16 : 32;  // B columns: 4 limbs x GT heads, padded
     constexpr int PP = kR / S;            // positions of a block per lane
-    constexpr int XS = 2 * GT + 1;        // exchange words per warp and tile
+    constexpr int XF = 2 * GT + 1;        // exchange fields per tile (x 4 warps)
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *ring = smem;
     unsigned char *bq = smem + a.off_bq;                       // N x 128 q limbs (K-major B)
     unsigned char *bw = smem + a.off_bw;                       // 2 x N x 128 weight limbs
-    int *xch = reinterpret_cast<int *>(smem + a.off_xch);      // [2][4][XS] tile exchange, [4] flags
+    int *xch = reinterpret_cast<int *>(smem + a.off_xch);      // [2][XF][4 warps] exchange, [4] flags
     float *red = reinterpret_cast<float *>(smem + a.off_red);  // small reductions
     float *scr = reinterpret_cast<float *>(smem + a.off_scr);  // merge scratch
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
@@ -211,6 +215,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     uint64_t *wready = bars + kTcStages + 4;  // [2] weight limbs written (4 warps)
     uint64_t *vdone = bars + kTcStages + 6;   // [2] output MMA done
     uint64_t *vfree = bars + kTcStages + 8;   // [2] output read back (4 warps)
+    uint64_t *xbar = bars + kTcStages + 10;   // [2] tile exchange published (4 warps)
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
 
@@ -230,7 +235,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     float *s_fin = red + 40;      // [16] final M, L per head
     float *lred = red + 56;       // [4 warps][8] partial sums
     float *rawlg = red + 88;      // [n_raw x GT] raw-tail logits
-    int *s_badf = xch + 2 * 4 * XS;  // [4] abort flags after the last tile
+    int *s_badf = xch + 2 * XF * 4;  // [4] abort flags after the last tile
     const int64_t k_row0 = ((b * a.Hk + hk) * a.k_cap + n0) * S;  // first code row (tensor map y)
     const int64_t v_row0 = ((b * a.Hk + hk) * a.v_cap + n0) * S;
     const uint32_t idesc_s = i8_idesc(N, 0), idesc_o = i8_idesc(N, 1);
@@ -259,6 +264,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 mbar_init(wready + i, 4);
                 mbar_init(vdone + i, 1);
                 mbar_init(vfree + i, 4);
+                mbar_init(xbar + i, 4);
             }
             fence_mbar_init();
             asm volatile("prefetch.tensormap [%0];" ::"l"(&tmk) : "memory");
@@ -376,13 +382,17 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             Mref[g] = -kMaxLog - 1;
             AXp[g] = 0;
         }
-        const int64_t ksb = b * a.ks_sb + hk * a.ks_sh + n0 * a.ks_sn;
-        const int64_t vsb = b * a.vs_sb + hk * a.vs_sh + n0 * a.vs_sn;
+        // row scales: split base (uniform) + this thread's offset, one tile per step
+        const int64_t kb0 = b * a.ks_sb + hk * a.ks_sh + n0 * a.ks_sn;
+        const int64_t vb0 = b * a.vs_sb + hk * a.vs_sh + n0 * a.vs_sn;
+        int kidx = (lrow / S) * (int)a.ks_sn + (lrow & (S - 1));
+        int vidx = (lrow / S) * (int)a.vs_sn + (lrow & (S - 1));
+        const int kstep = (kTileRows / S) * (int)a.ks_sn;
+        const int vstep = (kTileRows / S) * (int)a.vs_sn;
         const bool sc16 = a.sc_dtype == FC_F16;
-        auto scale_at = [&](const void *p, int64_t base, int64_t sn, int row) -> float {
-            const int64_t i = base + (int64_t)(row / S) * sn + (row & (S - 1));
-            return sc16 ? __half2float(static_cast<const __half *>(p)[i])
-                        : static_cast<const float *>(p)[i];
+        auto scale_at = [&](const void *p, int64_t base, int i) -> float {
+            return sc16 ? __half2float(static_cast<const __half *>(p)[base + i])
+                        : static_cast<const float *>(p)[base + i];
         };
         // fold the output of tile u (limbs relative to 2^(AXp - 132)) into acc
         auto fold = [&](int u) -> bool {
@@ -405,16 +415,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         int pend_bad = 0;
         float ks_next = 0.0f, vs_next = 0.0f;
         if (T > 0 && lrow < R) {
-            ks_next = scale_at(a.ksc, ksb, a.ks_sn, lrow);
-            vs_next = scale_at(a.vsc, vsb, a.vs_sn, lrow);
+            ks_next = scale_at(a.ksc, kb0, kidx);
+            vs_next = scale_at(a.vsc, vb0, vidx);
         }
         for (int t = 0; t < T; t++) {
             const int par = t & 1;
             const int row = t * kTileRows + lrow;
             const float ks = ks_next, vsr = vs_next;
+            kidx += kstep;
+            vidx += vstep;
             if (row + kTileRows < R) {  // the next tile's row scales
-                ks_next = scale_at(a.ksc, ksb, a.ks_sn, row + kTileRows);
-                vs_next = scale_at(a.vsc, vsb, a.vs_sn, row + kTileRows);
+                ks_next = scale_at(a.ksc, kb0, kidx);
+                vs_next = scale_at(a.vsc, vb0, vidx);
             } else {
                 ks_next = 0.0f;
                 vs_next = 0.0f;
@@ -432,13 +444,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(sfree + par);
-                const bool mask = row >= R;  // rows past the split (last tile only)
+                const float nb = row >= R ? -INFINITY : 0.0f;  // rows past the split
 #pragma unroll
                 for (int g = 0; g < GT; g++) {
                     const float sg = limb_value(v, g) * (cq[g] * ks);
                     float lg[PP];
 #pragma unroll
-                    for (int k = 0; k < PP; k++) lg[k] = Ar[k][0] * sg;
+                    for (int k = 0; k < PP; k++) lg[k] = fmaf(Ar[k][0], sg, nb);
 #pragma unroll
                     for (int x = 1; x < S; x++) {
                         const float o = __shfl_xor_sync(0xffffffffu, sg, x);
@@ -448,14 +460,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     float mx = lg[0];
 #pragma unroll
                     for (int k = 1; k < PP; k++) mx = fmaxf(mx, lg[k]);
-                    if (mask) mx = -INFINITY;
                     int mi = __reduce_max_sync(0xffffffffu, __float2int_rd(mx));
                     mi = min(max(mi, -kMaxLog), kMaxLog) + 1;
                     const float mf = (float)mi;
                     float P[PP], ls = 0.0f;
 #pragma unroll
                     for (int k = 0; k < PP; k++) {
-                        P[k] = mask ? 0.0f : ex2_approx(lg[k] - mf);
+                        P[k] = ex2_approx(lg[k] - mf);
                         ls += P[k];
                     }
                     float c[S];
@@ -477,35 +488,45 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     lsum[g] = ls;
                 }
             }
-            // one exchange per tile: warp maxima, weight exponents, abort flags
-            int *xw = xch + (par * 4 + warp) * XS;
+            // one exchange per tile: warp maxima, weight exponents, abort flags.
+            // Split phase: publish and arrive, fold the previous tile's output
+            // (independent of this exchange), then wait for the other warps.
+            int *xw = xch + par * XF * 4 + warp;   // field f of this warp at xw[4 f]
             if (lane == 0) {
                 if (okS) {
 #pragma unroll
-                    for (int g = 0; g < GT; g++) { xw[g] = mw[g]; xw[GT + g] = wx[g]; }
+                    for (int g = 0; g < GT; g++) { xw[4 * g] = mw[g]; xw[4 * (GT + g)] = wx[g]; }
                 }
-                xw[2 * GT] = (okS ? 0 : 1) | pend_bad;
+                xw[4 * 2 * GT] = (okS ? 0 : 1) | pend_bad;
+                mbar_arrive(xbar + par);
             }
-            epi_bar();
-            const int *xr = xch + par * 4 * XS;
-            if (xr[2 * GT] | xr[XS + 2 * GT] | xr[2 * XS + 2 * GT] | xr[3 * XS + 2 * GT]) {
+            // the previous tile's output (in the reference before this tile's max)
+            if (t >= 1 && !fold(t - 1)) pend_bad = 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(xbar + par, (t >> 1) & 1, a.status, a.epoch))) {
+                ab = true;
+                break;
+            }
+            // lane f reduces field f over the 4 warps, shuffles broadcast it
+            const int4 q4 = reinterpret_cast<const int4 *>(xch + par * XF * 4)[min(lane, XF - 1)];
+            const int fmx = max(max(q4.x, q4.y), max(q4.z, q4.w));
+            if (__shfl_sync(0xffffffffu, q4.x | q4.y | q4.z | q4.w, XF - 1)) {
                 ab = true;
                 break;
             }
             int m[GT], AX[GT];
 #pragma unroll
             for (int g = 0; g < GT; g++) {
-                m[g] = max(max(xr[g], xr[XS + g]), max(xr[2 * XS + g], xr[3 * XS + g]));
-                AX[g] = max(max(xr[GT + g], xr[XS + GT + g]), max(xr[2 * XS + GT + g], xr[3 * XS + GT + g]));
+                m[g] = __shfl_sync(0xffffffffu, fmx, g);
+                AX[g] = __shfl_sync(0xffffffffu, fmx, GT + g);
             }
             // weight limbs of this row (column lrow of the B tile)
             unsigned char *bwt = bw + par * (N * 128);
 #pragma unroll
             for (int g = 0; g < GT; g++) {
-                // x = w * 2^(132 + m_w - AX), |x| < 64, applied in two exact halves
-                // (each factor <= 2^66) so that no factor overflows
-                const int e = 132 + mw[g] - AX[g], e1 = e >> 1;
-                const float x = (w[g] * pow2_biased(127 + e1)) * pow2_biased(127 + e - e1);
+                // x = w * 2^(132 + m_w - AX), |x| < 64.  The factor's exponent is
+                // clamped at 127, reached only when every weight of this warp is
+                // below 2^-121 (contributions under 2^-114 of the output scale).
+                const float x = w[g] * pow2_biased(259 + mw[g] - AX[g]);
                 const float y0 = x + kRoundMagic;
                 const float d0 = x - (y0 - kRoundMagic);
                 const float y1 = fmaf(d0, 128.0f, kRoundMagic);
@@ -521,8 +542,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(wready + par);
-            // the previous tile's output (in the reference before this tile's max)
-            if (t >= 1 && !fold(t - 1)) pend_bad = 1;
             // this tile's max joins the running reference; the local sums join L
 #pragma unroll
             for (int g = 0; g < GT; g++) {
@@ -539,6 +558,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         float M[GT], L[GT];
 #pragma unroll
         for (int g = 0; g < GT; g++) { M[g] = 0.0f; L[g] = 1.0f; }
+        // After a failed wait the warps may leave the tile loop at different
+        // tiles; every epilogue warp reaches this barrier once either way.
         if (!ab) {
             if (T > 0 && !fold(T - 1)) pend_bad = 1;
 #pragma unroll
@@ -547,9 +568,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
                 if (lane == 0) lred[warp * 8 + g] = l;
             }
-            if (lane == 0) s_badf[warp] = pend_bad;
-            epi_bar();
-            ab = (s_badf[0] | s_badf[1] | s_badf[2] | s_badf[3]) != 0;
+        }
+        if (lane == 0) s_badf[warp] = (ab ? 1 : 0) | pend_bad;
+        epi_bar();
+        ab = (s_badf[0] | s_badf[1] | s_badf[2] | s_badf[3]) != 0;
+        if (!ab) {
 #pragma unroll
             for (int g = 0; g < GT; g++) {
                 M[g] = (float)Mref[g];
@@ -677,6 +700,10 @@ bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows) {
 
 size_t align_to(size_t x, size_t al) { return (x + al - 1) / al * al; }
 
+// Dynamic shared memory already opted in, per kernel variant (GT x s) and device.
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_smem_opted[16][kMaxDevices];
+
 int chunk_tiles() {
     static int tiles = [] {
         const char *e = getenv("FLASHCODEC_TC_CHUNK_TILES");  // tuning override (1..64)
@@ -716,27 +743,34 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
     a.off_scr = (int)off;
     off = align_to(off + (size_t)(a.n_split + 1) * a.GT * 4, 16);
     a.off_bar = (int)align_to(off, 8);
-    off = a.off_bar + (kTcStages + 10) * 8;
+    off = a.off_bar + (kTcStages + 12) * 8;
     const size_t smem = off + 1024;  // room to align the dynamic base to 1024
     dim3 grid((unsigned)(B * a.Hk * a.n_split));
-    auto go = [&](auto kern) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto go = [&](auto kern, int id) {
+        // the shared-memory opt-in is set once per kernel variant, device and size
+        std::atomic<int> *opted = (dev >= 0 && dev < kMaxDevices) ? &g_smem_opted[id][dev] : nullptr;
+        if (!opted || opted->load() < (int)smem) {
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (opted) opted->store((int)smem);
+        }
         kern<<<grid, kTcThreads, smem, st>>>(mk, mv, a);
     };
-    auto by_s = [&](auto gt) {
+    auto by_s = [&](auto gt, int gi) {
         constexpr int GT = decltype(gt)::value;
         switch (a.s) {
-            case 1: go(attn_tc_kernel<GT, 1>); break;
-            case 2: go(attn_tc_kernel<GT, 2>); break;
-            case 4: go(attn_tc_kernel<GT, 4>); break;
-            default: go(attn_tc_kernel<GT, 8>); break;
+            case 1: go(attn_tc_kernel<GT, 1>, gi * 4 + 0); break;
+            case 2: go(attn_tc_kernel<GT, 2>, gi * 4 + 1); break;
+            case 4: go(attn_tc_kernel<GT, 4>, gi * 4 + 2); break;
+            default: go(attn_tc_kernel<GT, 8>, gi * 4 + 3); break;
         }
     };
     switch (a.GT) {
-        case 1: by_s(std::integral_constant<int, 1>{}); break;
-        case 2: by_s(std::integral_constant<int, 2>{}); break;
-        case 4: by_s(std::integral_constant<int, 4>{}); break;
-        default: by_s(std::integral_constant<int, 8>{}); break;
+        case 1: by_s(std::integral_constant<int, 1>{}, 0); break;
+        case 2: by_s(std::integral_constant<int, 2>{}, 1); break;
+        case 4: by_s(std::integral_constant<int, 4>{}, 2); break;
+        default: by_s(std::integral_constant<int, 8>{}, 3); break;
     }
     return check_launch("decode_attn (tcgen05)");
 }

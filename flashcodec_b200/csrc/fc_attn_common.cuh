@@ -59,15 +59,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `ns` nanoseconds pass, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, unsigned parity, unsigned ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr unsigned kSleepNs = 500000;  // suspend hint of one bounded-wait step (0.5 ms)
+
 // Bounded wait on an mbarrier phase.  Gives up after kWaitNs of wall time,
 // recording this launch's epoch in *status (atomicMax), or as soon as another
 // CTA of the same launch has recorded it.  Returns false when it gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, unsigned parity, int *status,
                                                   int epoch) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kSleepNs)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, kSleepNs)) return true;
         if (*reinterpret_cast<volatile int *>(status) == epoch) return false;
         if (global_ns() - t0 > kWaitNs) {
             atomicMax(status, epoch);
