@@ -562,10 +562,12 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     return p;
 }
 
-// Split plan of the tensor-core kernel: chunks of 512 code rows (4 tiles).
+// Split plan of the tensor-core kernel: chunks of tc_chunk_blocks(s) blocks,
+// at most 1024 splits per unit (the merge scratch, (n_split + 1) x 8 floats,
+// lives in the kernel's 48 KB tile ring); longer contexts get longer chunks.
 void tc_plan(int64_t n, int s, int &n_split, int &chunk) {
     const int c = tc_chunk_blocks(s);
-    n_split = (int)std::max<int64_t>(1, (n + c - 1) / c);
+    n_split = (int)std::min<int64_t>(1024, std::max<int64_t>(1, (n + c - 1) / c));
     chunk = (int)((n + n_split - 1) / n_split);
 }
 

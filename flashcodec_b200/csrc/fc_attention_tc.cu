@@ -193,7 +193,7 @@ constexpr int kMaxLog = 1 << 29;  // clamp of the integer logit maxima
 // keeps |w / sigma| < 64.  The running reference Mref (per head) is the max of
 // the tile maxima; acc and the per-thread partial sums L live in 2^Mref units.
 template <int GT, int S>
-__global__ void __launch_bounds__(kTcThreads, 3)
+__global__ void __launch_bounds__(kTcThreads, GT <= 4 ? 4 : 3)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                const TcArgs a) {
     constexpr int N = GT <= 4 ? 16 : 32;  // B columns: 4 limbs x GT heads, padded
@@ -207,7 +207,6 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     unsigned char *bw = smem + a.off_bw;                       // 2 x N x 128 weight limbs
     int *xch = reinterpret_cast<int *>(smem + a.off_xch);      // [2][XF][4 warps] exchange, [4] flags
     float *red = reinterpret_cast<float *>(smem + a.off_red);  // small reductions
-    float *scr = reinterpret_cast<float *>(smem + a.off_scr);  // merge scratch
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
     uint64_t *full = bars;                    // [kTcStages] TMA landed
     uint64_t *sdone = bars + kTcStages;       // [2] score MMA done
@@ -232,9 +231,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     const int nraw = (split == a.n_split - 1) ? a.n_raw : 0;
     const int64_t hq0 = hk * G;
     float *s_sq = red + 32;       // [8] q scale per head
-    float *s_fin = red + 40;      // [16] final M, L per head
-    float *lred = red + 56;       // [4 warps][8] partial sums
-    float *rawlg = red + 88;      // [n_raw x GT] raw-tail logits
+    // after the last tile every copy into the ring has landed and every MMA
+    // that read it has completed: the ring holds the end-of-split scratch
+    float *lred = reinterpret_cast<float *>(ring);            // [4 warps][8] partial sums
+    float *rawlg = reinterpret_cast<float *>(ring + 256);     // [n_raw x GT] raw-tail logits
+    float *s_fin = reinterpret_cast<float *>(ring + 512);     // [16] final M, L per head
+    float *scr = reinterpret_cast<float *>(ring + 1024);      // merge scratch
     int *s_badf = xch + 2 * XF * 4;  // [4] abort flags after the last tile
     const int64_t k_row0 = ((b * a.Hk + hk) * a.k_cap + n0) * S;  // first code row (tensor map y)
     const int64_t v_row0 = ((b * a.Hk + hk) * a.v_cap + n0) * S;
@@ -739,9 +741,8 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
     a.off_xch = (int)off;
     off = align_to(off + (size_t)(2 * 4 * (2 * a.GT + 1) + 4) * 4, 16);
     a.off_red = (int)off;
-    off = align_to(off + (size_t)(88 + 8 * 8) * 4, 16);
-    a.off_scr = (int)off;
-    off = align_to(off + (size_t)(a.n_split + 1) * a.GT * 4, 16);
+    off = align_to(off + (size_t)40 * 4, 16);
+    a.off_scr = 0;  // merge scratch lives in the ring after the last tile
     a.off_bar = (int)align_to(off, 8);
     off = a.off_bar + (kTcStages + 12) * 8;
     const size_t smem = off + 1024;  // room to align the dynamic base to 1024
@@ -753,6 +754,8 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
         std::atomic<int> *opted = (dev >= 0 && dev < kMaxDevices) ? &g_smem_opted[id][dev] : nullptr;
         if (!opted || opted->load() < (int)smem) {
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
             if (opted) opted->store((int)smem);
         }
         kern<<<grid, kTcThreads, smem, st>>>(mk, mv, a);
