@@ -35,7 +35,7 @@
 
 namespace fc {
 
-int tc_chunk_blocks(int s);
+void tc_plan(int64_t n, int s, int64_t units, int GT, int &n_split, int &chunk);
 bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype);
 int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows,
                    int64_t krows_total, int64_t vrows_total, cudaStream_t st);
@@ -562,15 +562,6 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     return p;
 }
 
-// Split plan of the tensor-core kernel: chunks of tc_chunk_blocks(s) blocks,
-// at most 1024 splits per unit (the merge scratch, (n_split + 1) x 8 floats,
-// lives in the kernel's 48 KB tile ring); longer contexts get longer chunks.
-void tc_plan(int64_t n, int s, int &n_split, int &chunk) {
-    const int c = tc_chunk_blocks(s);
-    n_split = (int)std::min<int64_t>(1024, std::max<int64_t>(1, (n + c - 1) / c));
-    chunk = (int)((n + n_split - 1) / n_split);
-}
-
 int pick_vec_mode(int64_t D, int es, const void *k, const void *v, int64_t k_sb, int64_t k_sh,
                   int64_t k_sn, int64_t k_sj, int64_t v_sb, int64_t v_sh, int64_t v_sn,
                   int64_t v_sj, int s) {
@@ -641,7 +632,7 @@ extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
             w = std::max(w, make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm).ws);
     if (n_blocks > 0 && r == 8 && s <= 8 && (8 % s) == 0 && Hq / Hk <= 8) {
         int ns, chunk;
-        tc_plan(n_blocks, s, ns, chunk);
+        tc_plan(n_blocks, s, B * Hk, pick_gt(Hq / Hk), ns, chunk);
         w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
     }
     return w;
@@ -685,9 +676,9 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
                             k_sb == Hk * k_sh && v_sb == Hk * v_sh && aligned(k_rows, 16) &&
                             aligned(v_rows, 16) && n_raw < r;
         if (contig) {
-            int ns, chunk;
-            tc_plan(n_blocks, s, ns, chunk);
             const int GT = pick_gt(G);
+            int ns, chunk;
+            tc_plan(n_blocks, s, B * Hk, GT, ns, chunk);
             const size_t need = workspace_for(B * Hk, ns, GT, D);
             if (!workspace || workspace_bytes < need) {
                 set_error("decode_attn: workspace of %zu bytes needed, %zu given", need, workspace_bytes);

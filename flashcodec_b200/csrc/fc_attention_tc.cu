@@ -58,7 +58,6 @@ constexpr int kTileBytes = kTileRows * 128;  // 128 rows x 128 code bytes
 constexpr int kTcStages = 3;                 // TMA ring depth (K and V tiles interleaved)
 constexpr int kLimbs = 4;
 constexpr int kR = 8;                        // archive block length this kernel takes
-constexpr int kDefaultChunkTiles = 8;        // tiles (of 128 rows) per split
 
 // ------------------------------------------------------------ tcgen05 PTX
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
@@ -706,19 +705,40 @@ size_t align_to(size_t x, size_t al) { return (x + al - 1) / al * al; }
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_smem_opted[16][kMaxDevices];
 
-int chunk_tiles() {
+// Tiles per split forced by FLASHCODEC_TC_CHUNK_TILES (tuning), 0 when unset.
+int chunk_tiles_override() {
     static int tiles = [] {
-        const char *e = getenv("FLASHCODEC_TC_CHUNK_TILES");  // tuning override (1..64)
+        const char *e = getenv("FLASHCODEC_TC_CHUNK_TILES");
         const int v = e ? atoi(e) : 0;
-        return (v >= 1 && v <= 64) ? v : kDefaultChunkTiles;
+        return (v >= 1 && v <= 1 << 20) ? v : 0;
     }();
     return tiles;
 }
 
 }  // namespace
 
-// Blocks per split of the tensor-core path: chunk_tiles() tiles of 128 rows.
-int tc_chunk_blocks(int s) { return chunk_tiles() * kTileRows / s; }
+// Resident CTAs per SM of the tensor-core kernel (its launch bounds and
+// shared-memory footprint): 4 for GT <= 4, 3 for GT = 8.
+int tc_ctas_per_sm(int GT) { return GT <= 4 ? 4 : 3; }
+
+// Split plan of the tensor-core kernel.  Every CTA pays a pipeline fill and
+// drain, and CTAs of a second wave run behind an idle tail, so the plan takes
+// the most splits per (batch, KV head) unit that still fit one wave of
+// resident CTAs, in whole 128-row tiles, and at most 1024 splits per unit (the
+// merge scratch, (n_split + 1) x 8 floats, lives in the 48 KB tile ring).
+void tc_plan(int64_t n, int s, int64_t units, int GT, int &n_split, int &chunk) {
+    const int64_t tiles = std::max<int64_t>(1, (n * s + kTileRows - 1) / kTileRows);
+    int64_t ct = chunk_tiles_override();
+    if (ct == 0) {
+        const int64_t slots = (int64_t)num_sms() * tc_ctas_per_sm(GT);
+        const int64_t want = std::max<int64_t>(1, slots / std::max<int64_t>(units, 1));
+        ct = (tiles + want - 1) / want;
+    }
+    ct = std::max<int64_t>(ct, (tiles + 1023) / 1024);
+    const int64_t blocks = ct * (kTileRows / s);
+    n_split = (int)std::max<int64_t>(1, (n + blocks - 1) / blocks);
+    chunk = (int)std::min<int64_t>(blocks, n);
+}
 
 bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype) {
     return D == 128 && rows_dtype == FC_I8 && r == kR && (s == 1 || s == 2 || s == 4 || s == 8) &&
