@@ -323,6 +323,82 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+CODEC_WORKLOADS = ("archive", "read", "png-encode", "png-decode")
+
+
+def run_codec(args):
+    """--workload archive|read|png-encode|png-decode: HBM throughput of one
+    codec kernel on one GPU (secondary lines for the codec rooflines; the
+    default run is the config-2 attention line).  Inputs are seeded synthetic
+    tensors of the configs' shapes, larger than L2, resident in HBM; each
+    launch is timed with CUDA events on the launching stream."""
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as K
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = measured_peaks()
+    w = args.workload
+    if w in ("archive", "read"):
+        # config 2 stream shape: one layer's K stream, bf16, r=8, K=4, int8
+        B, H, S, D, r, k = 16, 8, 32768, 128, 8, 4
+        x = synth_stream(B, H, S, D, 0.95, 0, device=dev, dtype=torch.bfloat16)
+        n = S // r
+        basis = fc.codecs.jpeg.device_basis(r, k, dev)
+        codes = torch.empty(B, H, n, k, D, dtype=torch.int8, device=dev)
+        scales = torch.empty(B, H, n, k, 1, dtype=torch.float32, device=dev)
+        K.jpeg_encode(x, basis, r, k, codes, scales)
+        rec = torch.empty_like(x)
+        if w == "archive":
+            launch = lambda: K.jpeg_encode(x, basis, r, k, codes, scales)  # noqa: E731
+        else:
+            launch = lambda: K.jpeg_decode(codes, scales, basis, r, rec, S)  # noqa: E731
+        nbytes = x.numel() * 2 + codes.numel() + scales.numel() * 4
+        config = {"workload": f"jpeg {'archive (dct_compress + quantize_coeffs)' if w == 'archive' else 'read (dequantize + dct_decompress)'}, "
+                              "config 2 stream shape", "B": B, "H": H, "S": S, "D": D, "r": r,
+                  "K": k, "in_dtype": "bf16", "codes": "int8 + fp32 scales"}
+        kernel = "jpeg_encode_kernel" if w == "archive" else "jpeg_decode_kernel"
+    else:
+        # config 3: png lossless tier, fp32, r=16, keep 1.0
+        B, H, S, D, r = 8, 8, 16384, 128, 16
+        x = synth_stream(B, H, S, D, 0.98, 0, device=dev, dtype=torch.float32)
+        n = S // r
+        deltas = torch.empty(B, H, n, r - 1, D, dtype=torch.float32, device=dev)
+        anchors = torch.empty(B, H, n, D, dtype=torch.float32, device=dev)
+        K.png_encode(x, r, r - 1, deltas, anchors)
+        rec = torch.empty_like(x)
+        if w == "png-encode":
+            launch = lambda: K.png_encode(x, r, r - 1, deltas, anchors)  # noqa: E731
+        else:
+            launch = lambda: K.png_decode(deltas, anchors, rec, S)  # noqa: E731
+        nbytes = x.numel() * 4 + deltas.numel() * 4 + anchors.numel() * 4
+        config = {"workload": f"png {'filter' if w == 'png-encode' else 'reconstruct'}, config 3",
+                  "B": B, "H": H, "S": S, "D": D, "r": r, "keep_ratio": 1.0, "dtype": "fp32"}
+        kernel = "png_encode_kernel" if w == "png-encode" else "png_decode_kernel"
+    for _ in range(args.warmup):
+        launch()
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for a, b in ev:
+        a.record(stream)
+        launch()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    line = {"metric": f"{w} HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if w in ("archive", "read") else "fp32", "data": "synthetic",
+            "config": dict(config, l2="no flush: every launch moves > 1 GB, > 8x L2"),
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": gbs, "peak": peak,
+                         "unit": "GB/s", "frac": gbs / peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": nbytes},
+            "gpu_launches": args.steps}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(cfg, world):
     return {"workload": ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K "
                          "decode-attention launch per layer over the int8 DCT archive"),
@@ -344,8 +420,15 @@ def main():
     ap.add_argument("--batch", type=int, default=CFG2["B"],
                     help="sequences per GPU (default 16; smaller only for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="attention", choices=("attention",) + CODEC_WORKLOADS,
+                    help="attention (default, config 2) or one codec kernel's HBM throughput")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload != "attention":
+        if args.impl == "reference":
+            raise SystemExit("--impl reference times the attention workload")
+        run_codec(args)
+        return
     cfg = dict(CFG2, layers=args.layers, B=args.batch)
     if args.impl == "reference":
         run_reference(args, cfg)

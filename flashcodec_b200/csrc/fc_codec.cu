@@ -40,119 +40,242 @@ __device__ __forceinline__ float nan_max(float m, float a) {
 
 // x (B,H,S,D) of T -> coefficients (quantized to int8 + scales when
 // `scales` != nullptr).  Dynamic shared memory: per warp kEncTile x D floats.
-template <typename T, int VEC>
+// R > 0: the block length is the compile-time R (the row loops unroll, so all
+// of a block's row loads are in flight together); R = 0: a.r at run time.
+template <typename T, int VEC, int R>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 jpeg_encode_kernel(EncArgs a) {
     extern __shared__ float smem[];
     __shared__ float s_basis[kMaxR * kMaxR];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < a.k * a.r; i += blockDim.x) s_basis[i] = a.basis[i];
+    const int r = R > 0 ? R : a.r;
+    for (int i = threadIdx.x; i < a.k * r; i += blockDim.x) s_basis[i] = a.basis[i];
     __syncthreads();
 
-    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
     const int64_t total = a.B * a.H * a.nblk;
-    if (gw >= total) return;
-    const int64_t blk = gw % a.nblk;
-    const int64_t bh = gw / a.nblk;
-    const int64_t b = bh / a.H, h = bh % a.H;
-    const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * a.r * a.x_ss;
-    const int rows = (int)min((int64_t)a.r, a.S - blk * a.r);  // rows past S are zero padding
-    float *tile = smem + warp * kEncTile * a.D;
-    constexpr int dt = Elem<T>::code;
-    const bool quant = a.scales != nullptr;
+    for (int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp; gw < total;
+         gw += (int64_t)gridDim.x * kWarpsPerCta) {
+        // block counts are < 2^31 (checked on the host): 32-bit index math
+        const unsigned bh = (unsigned)gw / (unsigned)a.nblk;
+        const int64_t blk = (int64_t)((unsigned)gw - bh * (unsigned)a.nblk);
+        const int64_t b = bh / (unsigned)a.H, h = bh % (unsigned)a.H;
+        const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * r * a.x_ss;
+        const int rows = (int)min((int64_t)r, a.S - blk * r);  // rows past S are zero padding
+        float *tile = smem + warp * kEncTile * a.D;
+        constexpr int dt = Elem<T>::code;
+        const bool quant = a.scales != nullptr;
 
-    for (int j0 = 0; j0 < a.k; j0 += kEncTile) {
-        const int nj = min(kEncTile, a.k - j0);
-        float amax[kEncTile];
-#pragma unroll
-        for (int jj = 0; jj < kEncTile; jj++) amax[jj] = 0.0f;
-        for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
-            float acc[kEncTile][VEC];
-#pragma unroll
-            for (int jj = 0; jj < kEncTile; jj++)
-#pragma unroll
-                for (int v = 0; v < VEC; v++) acc[jj][v] = 0.0f;
-            for (int i = 0; i < a.r; i++) {
-                float xv[VEC];
-                if (i < rows) {
-                    load_vec_f32<T, VEC>(xb + i * a.x_ss + d0, xv);
-                } else {
-#pragma unroll
-                    for (int v = 0; v < VEC; v++) xv[v] = 0.0f;
-                }
-#pragma unroll
-                for (int jj = 0; jj < kEncTile; jj++) {
-                    if (jj < nj) {
-                        const float m = s_basis[(j0 + jj) * a.r + i];
-#pragma unroll
-                        for (int v = 0; v < VEC; v++) acc[jj][v] = __fmaf_rn(xv[v], m, acc[jj][v]);
+        for (int j0 = 0; j0 < a.k; j0 += kEncTile) {
+            const int nj = min(kEncTile, a.k - j0);
+            float amax[kEncTile];
+    #pragma unroll
+            for (int jj = 0; jj < kEncTile; jj++) amax[jj] = 0.0f;
+            for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+                float acc[kEncTile][VEC];
+    #pragma unroll
+                for (int jj = 0; jj < kEncTile; jj++)
+    #pragma unroll
+                    for (int v = 0; v < VEC; v++) acc[jj][v] = 0.0f;
+    #pragma unroll
+                for (int i = 0; i < r; i++) {
+                    float xv[VEC];
+                    if (i < rows) {
+                        load_vec_f32<T, VEC>(xb + i * a.x_ss + d0, xv);
+                    } else {
+    #pragma unroll
+                        for (int v = 0; v < VEC; v++) xv[v] = 0.0f;
+                    }
+    #pragma unroll
+                    for (int jj = 0; jj < kEncTile; jj++) {
+                        if (jj < nj) {
+                            const float m = s_basis[(j0 + jj) * r + i];
+    #pragma unroll
+                            for (int v = 0; v < VEC; v++) acc[jj][v] = __fmaf_rn(xv[v], m, acc[jj][v]);
+                        }
                     }
                 }
+    #pragma unroll
+                for (int jj = 0; jj < kEncTile; jj++) {
+                    if (jj >= nj) continue;
+                    const int64_t orow = b * a.o_sb + h * a.o_sh + blk * a.o_sn + (j0 + jj) * a.o_sj;
+                    float cv[VEC];
+    #pragma unroll
+                    for (int v = 0; v < VEC; v++) {
+                        cv[v] = round_to_dtype(acc[jj][v], dt);  // .to(x.dtype), jpeg.py:67
+                        if (quant) {
+                            tile[jj * a.D + d0 + v] = cv[v];
+                            amax[jj] = nan_max(amax[jj], fabsf(cv[v]));
+                        }
+                    }
+                    if (!quant) store_vec_from_f32<T, VEC>(static_cast<T *>(a.out) + orow + d0, cv);
+                }
             }
-#pragma unroll
+            if (!quant) continue;
+    #pragma unroll
+            for (int jj = 0; jj < kEncTile; jj++)
+    #pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+                    amax[jj] = nan_max(amax[jj], __shfl_xor_sync(0xffffffffu, amax[jj], off));
+            __syncwarp();
+    #pragma unroll
             for (int jj = 0; jj < kEncTile; jj++) {
                 if (jj >= nj) continue;
-                const int64_t orow = b * a.o_sb + h * a.o_sh + blk * a.o_sn + (j0 + jj) * a.o_sj;
-#pragma unroll
-                for (int v = 0; v < VEC; v++) {
-                    const float c = round_to_dtype(acc[jj][v], dt);  // .to(x.dtype), jpeg.py:67
-                    if (quant) {
-                        tile[jj * a.D + d0 + v] = c;
-                        amax[jj] = nan_max(amax[jj], fabsf(c));
-                    } else {
-                        store_from_f32(a.out, orow + d0 + v, dt, c);
+                // scale = amax / 127 in the coefficient dtype; 1 where it is 0
+                float s = round_to_dtype(__fdiv_rn(amax[jj], 127.0f), dt);
+                if (!(s > 0.0f)) s = 1.0f;
+                int8_t *orow = static_cast<int8_t *>(a.out) + b * a.o_sb + h * a.o_sh +
+                               blk * a.o_sn + (j0 + jj) * a.o_sj;
+                for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+                    uint32_t packed[(VEC + 3) / 4];
+    #pragma unroll
+                    for (int w = 0; w < (VEC + 3) / 4; w++) packed[w] = 0u;
+    #pragma unroll
+                    for (int v = 0; v < VEC; v++) {
+                        float q = rintf(__fdiv_rn(tile[jj * a.D + d0 + v], s));
+                        q = fminf(fmaxf(q, -127.0f), 127.0f);
+                        const int qi = (int)q;
+                        if constexpr (VEC % 4 == 0) {
+                            packed[v / 4] |= ((uint32_t)(qi & 0xFF)) << (8 * (v % 4));
+                        } else {
+                            orow[d0 + v] = (int8_t)qi;
+                        }
                     }
-                }
-            }
-        }
-        if (!quant) continue;
-#pragma unroll
-        for (int jj = 0; jj < kEncTile; jj++)
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1)
-                amax[jj] = nan_max(amax[jj], __shfl_xor_sync(0xffffffffu, amax[jj], off));
-        __syncwarp();
-#pragma unroll
-        for (int jj = 0; jj < kEncTile; jj++) {
-            if (jj >= nj) continue;
-            // scale = amax / 127 in the coefficient dtype; 1 where it is 0
-            float s = round_to_dtype(__fdiv_rn(amax[jj], 127.0f), dt);
-            if (!(s > 0.0f)) s = 1.0f;
-            int8_t *orow = static_cast<int8_t *>(a.out) + b * a.o_sb + h * a.o_sh +
-                           blk * a.o_sn + (j0 + jj) * a.o_sj;
-            for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
-                uint32_t packed[(VEC + 3) / 4];
-#pragma unroll
-                for (int w = 0; w < (VEC + 3) / 4; w++) packed[w] = 0u;
-#pragma unroll
-                for (int v = 0; v < VEC; v++) {
-                    float q = rintf(__fdiv_rn(tile[jj * a.D + d0 + v], s));
-                    q = fminf(fmaxf(q, -127.0f), 127.0f);
-                    const int qi = (int)q;
                     if constexpr (VEC % 4 == 0) {
-                        packed[v / 4] |= ((uint32_t)(qi & 0xFF)) << (8 * (v % 4));
-                    } else {
-                        orow[d0 + v] = (int8_t)qi;
+    #pragma unroll
+                        for (int w = 0; w < VEC / 4; w++)
+                            reinterpret_cast<uint32_t *>(orow + d0)[w] = packed[w];
                     }
                 }
-                if constexpr (VEC % 4 == 0) {
-#pragma unroll
-                    for (int w = 0; w < VEC / 4; w++)
-                        reinterpret_cast<uint32_t *>(orow + d0)[w] = packed[w];
+                if (lane == 0) {
+                    const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + (j0 + jj);
+                    if (a.scale_dtype == FC_F16) {
+                        const __half hs = __float2half_rn(s);
+                        static_cast<__half *>(a.scales)[si] = hs;
+                        if (__half2float(hs) != s && a.err) atomicOr(a.err, 1);
+                    } else {
+                        static_cast<float *>(a.scales)[si] = s;
+                    }
                 }
             }
+            __syncwarp();
+        }
+    }
+}
+
+// Fast path of the archive for head dim 128 (four channels per lane), block
+// length R in {8, 16} and k <= KM frequencies.  Each warp takes kEncBlocks
+// consecutive blocks and loads the rows of the next one (as raw words) while
+// it computes the current one, so HBM latency overlaps the FMA chains,
+// amax reduction and quantizer; coefficients stay in registers and the tiny
+// basis is read with uniform loads.  Same operations in the same order as
+// jpeg_encode_kernel.
+constexpr int kEncBlocks = 8;
+
+template <typename T, int R>
+struct RawRows {  // R rows of 4 elements of T, as loaded (8 or 16 bytes per row)
+    using W = typename std::conditional<sizeof(T) == 4, uint4, uint2>::type;
+    W w[R];
+};
+
+template <typename T, int R, int KM>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+jpeg_encode_d128_kernel(EncArgs a) {
+    using Rows = RawRows<T, R>;
+    using W = typename Rows::W;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t total = a.B * a.H * a.nblk;
+    const int64_t g0 = ((int64_t)blockIdx.x * kWarpsPerCta + warp) * kEncBlocks;
+    if (g0 >= total) return;
+    const int nb = (int)min((int64_t)kEncBlocks, total - g0);
+    constexpr int dt = Elem<T>::code;
+    const bool quant = a.scales != nullptr;
+    const int d0 = lane * 4;
+    // block counts are < 2^31 (host check): 32-bit index math
+    auto locate = [&](int64_t gw, int64_t &b, int64_t &h, int64_t &blk) {
+        const unsigned bh = (unsigned)gw / (unsigned)a.nblk;
+        blk = (int64_t)((unsigned)gw - bh * (unsigned)a.nblk);
+        b = bh / (unsigned)a.H;
+        h = bh % (unsigned)a.H;
+    };
+    auto load_rows = [&](int64_t gw, Rows &rw) {
+        int64_t b, h, blk;
+        locate(gw, b, h, blk);
+        const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * R * a.x_ss + d0;
+        const int rows = (int)min((int64_t)R, a.S - blk * R);
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            if (i < rows) rw.w[i] = *reinterpret_cast<const W *>(xb + i * a.x_ss);
+            else rw.w[i] = W{};  // zero padding past S
+        }
+    };
+    // the k x R basis in registers for all of this warp's blocks
+    float mb[KM][R];
+#pragma unroll
+    for (int j = 0; j < KM; j++)
+#pragma unroll
+        for (int i = 0; i < R; i++) mb[j][i] = j < a.k ? __ldg(a.basis + j * R + i) : 0.0f;
+    Rows next;
+    load_rows(g0, next);
+    for (int e = 0; e < nb; e++) {
+        const Rows cur = next;
+        if (e + 1 < nb) load_rows(g0 + e + 1, next);
+        float xv[R][4];
+#pragma unroll
+        for (int i = 0; i < R; i++) load_vec_f32<T, 4>(reinterpret_cast<const T *>(&cur.w[i]), xv[i]);
+        int64_t b, h, blk;
+        locate(g0 + e, b, h, blk);
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
+            if (j >= a.k) break;
+            float c[4];
+#pragma unroll
+            for (int v = 0; v < 4; v++) c[v] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < R; i++)
+#pragma unroll
+                for (int v = 0; v < 4; v++) c[v] = __fmaf_rn(xv[i][v], mb[j][i], c[v]);
+#pragma unroll
+            for (int v = 0; v < 4; v++) c[v] = round_to_dtype(c[v], dt);  // .to(x.dtype), jpeg.py:67
+            const int64_t orow = b * a.o_sb + h * a.o_sh + blk * a.o_sn + j * a.o_sj + d0;
+            if (!quant) {
+                store_vec_from_f32<T, 4>(static_cast<T *>(a.out) + orow, c);
+                continue;
+            }
+            // amax over the row: |c| bit patterns order like the values (a NaN
+            // pattern is above every number, so NaN propagates like torch.amax)
+            unsigned ab = 0u;
+#pragma unroll
+            for (int v = 0; v < 4; v++) ab = max(ab, __float_as_uint(c[v]) & 0x7fffffffu);
+            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, ab));
+            // scale = amax / 127 in the coefficient dtype; 1 where it is 0
+            float sc = round_to_dtype(__fdiv_rn(amax, 127.0f), dt);
+            if (!(sc > 0.0f)) sc = 1.0f;
+            // q = rint(c / scale) with the IEEE quotient.  c * (1/scale) is within
+            // 2^-23 relative (|q| <= 128: 3e-5 absolute) of it, so it rounds to the
+            // same integer unless it lies within 1e-4 of a half-integer; there (and
+            // for NaN or infinities) the exact quotient is taken.
+            const float rs = __frcp_rn(sc);
+            uint32_t packed = 0u;
+#pragma unroll
+            for (int v = 0; v < 4; v++) {
+                const float y = __fmul_rn(c[v], rs);
+                float q = rintf(y);
+                if (!(fabsf(fabsf(y - q) - 0.5f) > 1e-4f)) q = rintf(__fdiv_rn(c[v], sc));
+                q = fminf(fmaxf(q, -127.0f), 127.0f);
+                packed |= ((uint32_t)((int)q & 0xFF)) << (8 * v);
+            }
+            *reinterpret_cast<uint32_t *>(static_cast<int8_t *>(a.out) + orow) = packed;
             if (lane == 0) {
-                const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + (j0 + jj);
+                const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + j;
                 if (a.scale_dtype == FC_F16) {
-                    const __half hs = __float2half_rn(s);
+                    const __half hs = __float2half_rn(sc);
                     static_cast<__half *>(a.scales)[si] = hs;
-                    if (__half2float(hs) != s && a.err) atomicOr(a.err, 1);
+                    if (__half2float(hs) != sc && a.err) atomicOr(a.err, 1);
                 } else {
-                    static_cast<float *>(a.scales)[si] = s;
+                    static_cast<float *>(a.scales)[si] = sc;
                 }
             }
         }
-        __syncwarp();
     }
 }
 
@@ -172,51 +295,116 @@ struct DecArgs {
 };
 
 // coefficients (B,H,n,k,D) -> (B,H,out_len,D); KM >= k coefficient registers.
-template <typename CT, int VEC, int KM>
+// R > 0: compile-time block length (unrolled rows); OT: the output element
+// type for vector stores, or void for element stores of a.out_dtype.
+template <typename CT, int VEC, int KM, int R, typename OT>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 jpeg_decode_kernel(DecArgs a) {
     __shared__ float s_basis[kMaxR * kMaxR];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < a.k * a.r; i += blockDim.x) s_basis[i] = a.basis[i];
+    const int r = R > 0 ? R : a.r;
+    for (int i = threadIdx.x; i < a.k * r; i += blockDim.x) s_basis[i] = a.basis[i];
     __syncthreads();
-    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
-    if (gw >= a.B * a.H * a.n) return;
-    const int64_t blk = gw % a.n, bh = gw / a.n;
-    const int64_t b = bh / a.H, h = bh % a.H;
-    const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh + blk * a.c_sn;
-    float sc[KM];
-#pragma unroll
-    for (int j = 0; j < KM; j++) {
-        sc[j] = 1.0f;
-        if (j < a.k && a.scales)
-            sc[j] = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
-    }
-    const int64_t obase = b * a.o_sb + h * a.o_sh;
-    for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
-        float c[KM][VEC];
-#pragma unroll
+    const int64_t total = a.B * a.H * a.n;
+    for (int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp; gw < total;
+         gw += (int64_t)gridDim.x * kWarpsPerCta) {
+        // block counts are < 2^31 (checked on the host): 32-bit index math
+        const unsigned bh = (unsigned)gw / (unsigned)a.n;
+        const int64_t blk = (int64_t)((unsigned)gw - bh * (unsigned)a.n);
+        const int64_t b = bh / (unsigned)a.H, h = bh % (unsigned)a.H;
+        const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh + blk * a.c_sn;
+        float sc[KM];
+    #pragma unroll
         for (int j = 0; j < KM; j++) {
-            if (j < a.k) {
-                load_vec_f32<CT, VEC>(cb + j * a.c_sj + d0, c[j]);
-                if (a.scales) {
-                    // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
-#pragma unroll
-                    for (int v = 0; v < VEC; v++) c[j][v] = __fmul_rn(c[j][v], sc[j]);
+            sc[j] = 1.0f;
+            if (j < a.k && a.scales)
+                sc[j] = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
+        }
+        const int64_t obase = b * a.o_sb + h * a.o_sh;
+        for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+            float c[KM][VEC];
+    #pragma unroll
+            for (int j = 0; j < KM; j++) {
+                if (j < a.k) {
+                    load_vec_f32<CT, VEC>(cb + j * a.c_sj + d0, c[j]);
+                    if (a.scales) {
+                        // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
+    #pragma unroll
+                        for (int v = 0; v < VEC; v++) c[j][v] = __fmul_rn(c[j][v], sc[j]);
+                    }
+                }
+            }
+            const int nrow = (int)min((int64_t)r, a.out_len - blk * r);
+    #pragma unroll
+            for (int i = 0; i < r; i++) {
+                if (i >= nrow) break;
+                const int64_t pos = blk * r + i;
+                float o[VEC];
+    #pragma unroll
+                for (int v = 0; v < VEC; v++) {
+                    float acc = 0.0f;
+    #pragma unroll
+                    for (int j = 0; j < KM; j++)
+                        if (j < a.k) acc = __fmaf_rn(c[j][v], s_basis[j * r + i], acc);
+                    o[v] = acc;
+                }
+                if constexpr (std::is_void<OT>::value) {
+    #pragma unroll
+                    for (int v = 0; v < VEC; v++)
+                        store_from_f32(a.out, obase + pos * a.o_ss + d0 + v, a.out_dtype, o[v]);
+                } else {
+                    store_vec_from_f32<OT, VEC>(static_cast<OT *>(a.out) + obase + pos * a.o_ss + d0, o);
                 }
             }
         }
-        for (int i = 0; i < a.r; i++) {
-            const int64_t pos = blk * a.r + i;
-            if (pos >= a.out_len) break;
+    }
+}
+
+// Fast path of the read path for head dim 128 (four channels per lane), block
+// length R in {8, 16}, k <= KM and vector output rows of OT: one warp per
+// block, basis by uniform loads.  Same operations in the same order as
+// jpeg_decode_kernel.
+template <typename CT, int R, int KM, typename OT>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+jpeg_decode_d128_kernel(DecArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= a.B * a.H * a.n) return;
+    const int d0 = lane * 4;
+    const unsigned bh = (unsigned)gw / (unsigned)a.n;  // < 2^31 blocks (host check)
+    const int64_t blk = (int64_t)((unsigned)gw - bh * (unsigned)a.n);
+    const int64_t b = bh / (unsigned)a.H, h = bh % (unsigned)a.H;
+    const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh + blk * a.c_sn + d0;
+    float c[KM][4];
 #pragma unroll
-            for (int v = 0; v < VEC; v++) {
-                float acc = 0.0f;
+    for (int j = 0; j < KM; j++) {
+        if (j < a.k) {
+            load_vec_f32<CT, 4>(cb + j * a.c_sj, c[j]);
+            if (a.scales) {
+                // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
+                const float sc = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
 #pragma unroll
-                for (int j = 0; j < KM; j++)
-                    if (j < a.k) acc = __fmaf_rn(c[j][v], s_basis[j * a.r + i], acc);
-                store_from_f32(a.out, obase + pos * a.o_ss + d0 + v, a.out_dtype, acc);
+                for (int v = 0; v < 4; v++) c[j][v] = __fmul_rn(c[j][v], sc);
             }
         }
+    }
+    OT *ob = static_cast<OT *>(a.out) + b * a.o_sb + h * a.o_sh + blk * R * a.o_ss + d0;
+    const int nrow = (int)min((int64_t)R, a.out_len - blk * R);
+#pragma unroll
+    for (int i = 0; i < R; i++) {
+        if (i >= nrow) break;
+        float o[4];
+#pragma unroll
+        for (int v = 0; v < 4; v++) o[v] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
+            if (j < a.k) {
+                const float m = __ldg(a.basis + j * R + i);
+#pragma unroll
+                for (int v = 0; v < 4; v++) o[v] = __fmaf_rn(c[j][v], m, o[v]);
+            }
+        }
+        store_vec_from_f32<OT, 4>(ob + i * a.o_ss, o);
     }
 }
 
@@ -268,6 +456,43 @@ png_encode_kernel(PngEncArgs a) {
     }
 }
 
+// png_filter with every delta kept (keep_ratio 1.0, keep_m = r - 1): four
+// channels per lane with vector loads and stores, R compile-time rows whose
+// loads are all in flight together.  Same arithmetic as png_encode_kernel.
+template <typename T, int R>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+png_encode_fast_kernel(PngEncArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= a.B * a.H * a.nblk) return;
+    const int64_t blk = gw % a.nblk, bh = gw / a.nblk;
+    const int64_t b = bh / a.H, h = bh % a.H;
+    const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * R * a.x_ss;
+    const int rows = (int)min((int64_t)R, a.S - blk * R);
+    float *db = a.deltas + b * a.d_sb + h * a.d_sh + blk * a.d_sn;
+    T *ab = static_cast<T *>(a.anchors) + b * a.a_sb + h * a.a_sh + blk * a.a_sn;
+    for (int64_t d0 = (int64_t)lane * 4; d0 < a.D; d0 += 128) {
+        float x[R][4];
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            if (i < rows) {
+                load_vec_f32<T, 4>(xb + i * a.x_ss + d0, x[i]);
+            } else {
+#pragma unroll
+                for (int v = 0; v < 4; v++) x[i][v] = 0.0f;  // zero padding past S
+            }
+        }
+        store_vec_from_f32<T, 4>(ab + d0, x[0]);  // anchor, input dtype (exact)
+#pragma unroll
+        for (int i = 1; i < R; i++) {
+            float dv[4];
+#pragma unroll
+            for (int v = 0; v < 4; v++) dv[v] = __fsub_rn(x[i][v], x[i - 1][v]);
+            store_vec_from_f32<float, 4>(db + (i - 1) * a.d_si + d0, dv);
+        }
+    }
+}
+
 struct PngDecArgs {
     const float *deltas;
     int64_t d_sb, d_sh, d_sn, d_si;
@@ -305,8 +530,49 @@ png_decode_kernel(PngDecArgs a) {
     }
 }
 
+// png_reconstruct fast path: four channels per lane, R compile-time rows,
+// all delta loads in flight together; same fp64 prefix as png_decode_kernel.
+// AT is the anchor (and output) element type.
+template <typename AT, int R>
+__global__ void __launch_bounds__(kWarpsPerCta * 32)
+png_decode_fast_kernel(PngDecArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+    if (gw >= a.B * a.H * a.n) return;
+    const int64_t blk = gw % a.n, bh = gw / a.n;
+    const int64_t b = bh / a.H, h = bh % a.H;
+    const float *db = a.deltas + b * a.d_sb + h * a.d_sh + blk * a.d_sn;
+    const AT *ab = static_cast<const AT *>(a.anchors) + b * a.a_sb + h * a.a_sh + blk * a.a_sn;
+    AT *ob = static_cast<AT *>(a.out) + b * a.o_sb + h * a.o_sh + blk * R * a.o_ss;
+    const int nrow = (int)min((int64_t)R, a.out_len - blk * R);
+    for (int64_t d0 = (int64_t)lane * 4; d0 < a.D; d0 += 128) {
+        float an[4], dl[R - 1][4];
+        load_vec_f32<AT, 4>(ab + d0, an);
+#pragma unroll
+        for (int i = 0; i < R - 1; i++) load_vec_f32<float, 4>(db + i * a.d_si + d0, dl[i]);
+        if (nrow > 0) store_vec_from_f32<AT, 4>(ob + d0, an);
+        double pre[4] = {0.0, 0.0, 0.0, 0.0};  // fp64 accumulation, as torch's CPU cumsum
+#pragma unroll
+        for (int i = 1; i < R; i++) {
+            float o[4];
+#pragma unroll
+            for (int v = 0; v < 4; v++) {
+                pre[v] += (double)dl[i - 1][v];
+                o[v] = __fadd_rn(an[v], __double2float_rn(pre[v]));
+            }
+            if (i < nrow) store_vec_from_f32<AT, 4>(ob + i * a.o_ss + d0, o);
+        }
+    }
+}
+
 inline unsigned grid_for(int64_t warps) {
     return (unsigned)((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+}
+
+// Grid of the grid-stride jpeg kernels (each warp walks many blocks, so the
+// per-CTA basis load is paid once): at most 8 CTAs per SM.
+inline unsigned grid_stride_for(int64_t warps) {
+    return (unsigned)std::min<int64_t>(grid_for(warps), (int64_t)num_sms() * 8);
 }
 
 template <typename F>
@@ -338,13 +604,15 @@ extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, 
     if (scales && scale_dtype != FC_F32 && scale_dtype != FC_F16) { set_error("jpeg_encode: scale dtype must be f32 or f16"); return FC_EINVAL; }
     const int64_t nblk = (S + r - 1) / r;
     if (B * H * nblk == 0) return FC_OK;
+    if (B * H * nblk >= ((int64_t)1 << 31)) { set_error("jpeg_encode: more than 2^31 blocks"); return FC_ENOTSUP; }
     if (!x || !basis || !out) { set_error("jpeg_encode: null pointer"); return FC_EINVAL; }
     const int es = dtype_size(x_dtype);
     // 4-element vectors when every row start and the head dim allow it
     bool v4 = (D % 4 == 0) && aligned(x, 4 * es) && (x_sb % 4 == 0) && (x_sh % 4 == 0) &&
               (x_ss % 4 == 0);
-    if (scales) v4 = v4 && aligned(out, 4) && (o_sb % 4 == 0) && (o_sh % 4 == 0) &&
-                     (o_sn % 4 == 0) && (o_sj % 4 == 0);
+    // codes (1 byte) or coefficients (x dtype) are written 4 at a time
+    v4 = v4 && aligned(out, scales ? 4 : 4 * es) && (o_sb % 4 == 0) && (o_sh % 4 == 0) &&
+         (o_sn % 4 == 0) && (o_sj % 4 == 0);
     EncArgs a{x, B, H, S, D, nblk, x_sb, x_sh, x_ss, basis, r, k, out, o_sb, o_sh, o_sn, o_sj,
               scales, scale_dtype, s_sb, s_sh, s_sn, err};
     const size_t smem = (size_t)kWarpsPerCta * kEncTile * D * sizeof(float);
@@ -355,11 +623,22 @@ extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, 
         if constexpr (std::is_same<T, int8_t>::value) {
             return FC_EINVAL;
         } else {
-            auto kern = v4 ? jpeg_encode_kernel<T, 4> : jpeg_encode_kernel<T, 1>;
+            if (v4 && D == 128 && (r == 8 || r == 16) && k <= 8) {
+                const unsigned g = grid_for((B * H * nblk + kEncBlocks - 1) / kEncBlocks);
+                if (r == 8 && k <= 4) jpeg_encode_d128_kernel<T, 8, 4><<<g, kWarpsPerCta * 32, 0, st>>>(a);
+                else if (r == 8) jpeg_encode_d128_kernel<T, 8, 8><<<g, kWarpsPerCta * 32, 0, st>>>(a);
+                else if (k <= 4) jpeg_encode_d128_kernel<T, 16, 4><<<g, kWarpsPerCta * 32, 0, st>>>(a);
+                else jpeg_encode_d128_kernel<T, 16, 8><<<g, kWarpsPerCta * 32, 0, st>>>(a);
+                return check_launch("jpeg_encode");
+            }
+            auto kern = !v4 ? jpeg_encode_kernel<T, 1, 0>
+                        : r == 8 ? jpeg_encode_kernel<T, 4, 8>
+                        : r == 16 ? jpeg_encode_kernel<T, 4, 16>
+                                  : jpeg_encode_kernel<T, 4, 0>;
             // the kernel also holds a static kMaxR x kMaxR basis table
             if (smem + sizeof(float) * kMaxR * kMaxR > 48 * 1024)
                 cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            kern<<<grid_for(B * H * nblk), kWarpsPerCta * 32, smem, st>>>(a);
+            kern<<<grid_stride_for(B * H * nblk), kWarpsPerCta * 32, smem, st>>>(a);
             return check_launch("jpeg_encode");
         }
     });
@@ -378,6 +657,7 @@ extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64
     if (r < 1 || r > kMaxR || k < 1 || k > r) { set_error("jpeg_decode: need 1 <= k <= r <= %d", kMaxR); return FC_EINVAL; }
     if (B < 0 || H < 0 || n < 0 || D <= 0 || out_len < 0 || out_len > n * r) { set_error("jpeg_decode: bad shape"); return FC_EINVAL; }
     if (B * H * n == 0 || out_len == 0) return FC_OK;
+    if (B * H * n >= ((int64_t)1 << 31)) { set_error("jpeg_decode: more than 2^31 blocks"); return FC_ENOTSUP; }
     if (!coef || !basis || !out) { set_error("jpeg_decode: null pointer"); return FC_EINVAL; }
     const int es = dtype_size(coef_dtype);
     const bool v4 = (D % 4 == 0) && aligned(coef, 4 * es) && (c_sb % 4 == 0) && (c_sh % 4 == 0) &&
@@ -385,17 +665,42 @@ extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64
     DecArgs a{coef, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales, scale_dtype, s_sb, s_sh, s_sn,
               basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const unsigned grid = grid_for(B * H * n);
+    const unsigned grid = grid_stride_for(B * H * n);
+    // vector stores of 4 outputs when the output rows allow them
+    const int oes = dtype_size(out_dtype);
+    const bool ov4 = v4 && aligned(out, 4 * oes) && (o_sb % 4 == 0) && (o_sh % 4 == 0) &&
+                     (o_ss % 4 == 0);
     return launch_typed(coef_dtype, [&](auto *tp) -> int {
         using CT = std::remove_pointer_t<decltype(tp)>;
-        if (k <= 4) {
-            if (v4) jpeg_decode_kernel<CT, 4, 4><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
-            else jpeg_decode_kernel<CT, 1, 4><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+        auto fast = [&](auto rr) {  // k <= 4, r in {8, 16}, vector loads and stores
+            constexpr int RR = decltype(rr)::value;
+            if (D == 128) {
+                const unsigned grid = grid_for(B * H * n);
+                switch (out_dtype) {
+                    case FC_F32: jpeg_decode_d128_kernel<CT, RR, 4, float><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
+                    case FC_BF16: jpeg_decode_d128_kernel<CT, RR, 4, __nv_bfloat16><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
+                    default: jpeg_decode_d128_kernel<CT, RR, 4, __half><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
+                }
+                return;
+            }
+            switch (out_dtype) {
+                case FC_F32: jpeg_decode_kernel<CT, 4, 4, RR, float><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
+                case FC_BF16: jpeg_decode_kernel<CT, 4, 4, RR, __nv_bfloat16><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
+                default: jpeg_decode_kernel<CT, 4, 4, RR, __half><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
+            }
+        };
+        if (k <= 4 && ov4 && r == 8) {
+            fast(std::integral_constant<int, 8>{});
+        } else if (k <= 4 && ov4 && r == 16) {
+            fast(std::integral_constant<int, 16>{});
+        } else if (k <= 4) {
+            if (v4) jpeg_decode_kernel<CT, 4, 4, 0, void><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            else jpeg_decode_kernel<CT, 1, 4, 0, void><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
         } else if (k <= 16) {
-            if (v4) jpeg_decode_kernel<CT, 4, 16><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
-            else jpeg_decode_kernel<CT, 1, 16><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            if (v4) jpeg_decode_kernel<CT, 4, 16, 0, void><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            else jpeg_decode_kernel<CT, 1, 16, 0, void><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
         } else {
-            jpeg_decode_kernel<CT, 1, kMaxR><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            jpeg_decode_kernel<CT, 1, kMaxR, 0, void><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
         }
         return check_launch("jpeg_decode");
     });
@@ -422,7 +727,17 @@ extern "C" int fc_png_encode(const void *x, int x_dtype, int64_t B, int64_t H, i
         if constexpr (std::is_same<T, int8_t>::value) {
             return FC_EINVAL;
         } else {
-            png_encode_kernel<T><<<grid_for(B * H * nblk), kWarpsPerCta * 32, 0, st>>>(a);
+            const int es = (int)sizeof(T);
+            const bool fast = keep_m == r - 1 && (r == 8 || r == 16) && D % 4 == 0 &&
+                              aligned(x, 4 * es) && x_sb % 4 == 0 && x_sh % 4 == 0 &&
+                              x_ss % 4 == 0 && aligned(deltas, 16) && d_sb % 4 == 0 &&
+                              d_sh % 4 == 0 && d_sn % 4 == 0 && d_si % 4 == 0 &&
+                              aligned(anchors, 4 * es) && a_sb % 4 == 0 && a_sh % 4 == 0 &&
+                              a_sn % 4 == 0;
+            const unsigned grid = grid_for(B * H * nblk);
+            if (fast && r == 8) png_encode_fast_kernel<T, 8><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            else if (fast) png_encode_fast_kernel<T, 16><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+            else png_encode_kernel<T><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
             return check_launch("png_encode");
         }
     });
@@ -441,7 +756,27 @@ extern "C" int fc_png_decode(const float *deltas, int64_t d_sb, int64_t d_sh, in
     if (!deltas || !anchors || !out) { set_error("png_decode: null pointer"); return FC_EINVAL; }
     PngDecArgs a{deltas, d_sb, d_sh, d_sn, d_si, anchors, a_dtype, a_sb, a_sh, a_sn,
                  B, H, n, r, D, out, out_len, o_sb, o_sh, o_ss};
-    png_decode_kernel<<<grid_for(B * H * n), kWarpsPerCta * 32, 0,
-                        static_cast<cudaStream_t>(stream)>>>(a);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = grid_for(B * H * n);
+    const int aes = dtype_size(a_dtype);
+    const bool fast = (r == 8 || r == 16) && D % 4 == 0 && aligned(deltas, 16) &&
+                      d_sb % 4 == 0 && d_sh % 4 == 0 && d_sn % 4 == 0 && d_si % 4 == 0 &&
+                      aligned(anchors, 4 * aes) && a_sb % 4 == 0 && a_sh % 4 == 0 &&
+                      a_sn % 4 == 0 && aligned(out, 4 * aes) && o_sb % 4 == 0 &&
+                      o_sh % 4 == 0 && o_ss % 4 == 0;
+    if (!fast) {
+        png_decode_kernel<<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+        return check_launch("png_decode");
+    }
+    auto go = [&](auto *tp) {
+        using AT = std::remove_pointer_t<decltype(tp)>;
+        if (r == 8) png_decode_fast_kernel<AT, 8><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+        else png_decode_fast_kernel<AT, 16><<<grid, kWarpsPerCta * 32, 0, st>>>(a);
+    };
+    switch (a_dtype) {
+        case FC_F32: go((float *)nullptr); break;
+        case FC_BF16: go((__nv_bfloat16 *)nullptr); break;
+        default: go((__half *)nullptr); break;
+    }
     return check_launch("png_decode");
 }

@@ -132,4 +132,32 @@ __device__ __forceinline__ void load_vec_f32(const T *p, float out[VEC]) {
     }
 }
 
+// Round VEC fp32 values to T (round-to-nearest-even, like store_from_f32) and
+// store them as one vector at p (aligned to VEC * sizeof(T) when that is 16,
+// 8 or 4 bytes; element stores otherwise).
+template <typename T, int VEC>
+__device__ __forceinline__ void store_vec_from_f32(T *p, const float v[VEC]) {
+    constexpr int BYTES = VEC * (int)sizeof(T);
+    if constexpr (VEC == 4 && std::is_same<T, float>::value) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if constexpr (VEC == 4 && BYTES == 8 && std::is_same<T, __nv_bfloat16>::value) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 w;
+        w.x = *reinterpret_cast<const uint32_t *>(&lo);
+        w.y = *reinterpret_cast<const uint32_t *>(&hi);
+        *reinterpret_cast<uint2 *>(p) = w;
+    } else if constexpr (VEC == 4 && BYTES == 8 && std::is_same<T, __half>::value) {
+        const __half2 lo = __floats2half2_rn(v[0], v[1]);
+        const __half2 hi = __floats2half2_rn(v[2], v[3]);
+        uint2 w;
+        w.x = *reinterpret_cast<const uint32_t *>(&lo);
+        w.y = *reinterpret_cast<const uint32_t *>(&hi);
+        *reinterpret_cast<uint2 *>(p) = w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < VEC; i++) store_from_f32(p, i, Elem<T>::code, v[i]);
+    }
+}
+
 }  // namespace fc
