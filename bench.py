@@ -356,7 +356,7 @@ def run_codec(args):
         config = {"workload": f"jpeg {'archive (dct_compress + quantize_coeffs)' if w == 'archive' else 'read (dequantize + dct_decompress)'}, "
                               "config 2 stream shape", "B": B, "H": H, "S": S, "D": D, "r": r,
                   "K": k, "in_dtype": "bf16", "codes": "int8 + fp32 scales"}
-        kernel = "jpeg_encode_kernel" if w == "archive" else "jpeg_decode_kernel"
+        kernel = "fc_jpeg_encode" if w == "archive" else "fc_jpeg_decode"
     else:
         # config 3: png lossless tier, fp32, r=16, keep 1.0
         B, H, S, D, r = 8, 8, 16384, 128, 16
@@ -373,7 +373,7 @@ def run_codec(args):
         nbytes = x.numel() * 4 + deltas.numel() * 4 + anchors.numel() * 4
         config = {"workload": f"png {'filter' if w == 'png-encode' else 'reconstruct'}, config 3",
                   "B": B, "H": H, "S": S, "D": D, "r": r, "keep_ratio": 1.0, "dtype": "fp32"}
-        kernel = "png_encode_kernel" if w == "png-encode" else "png_decode_kernel"
+        kernel = "fc_png_encode" if w == "png-encode" else "fc_png_decode"
     for _ in range(args.warmup):
         launch()
     stream = torch.cuda.current_stream(dev)
