@@ -96,7 +96,12 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 METRIC = ("decode-attn tokens/s & achieved HBM GB/s (% of peak) on int8 DCT KV, "
           "1/2/4/8 B200")
-CFG2 = dict(layers=36, B=16, Hq=32, Hk=8, D=128, S=32768, tail=5, r=8, K=4, rho=0.95)
+CFG2 = dict(layers=36, B=16, Hq=32, Hk=8, D=128, S=32768, tail=5, r=8, K=4, rho=0.95,
+            scale_dtype="fp32", config=2)
+# config 5 per GPU at 8-way batch sharding (global B=128): S=131072, K=2,
+# fp16 scales; 8 independent layer archives (~1.09 GB each) per step
+CFG5 = dict(layers=8, B=16, Hq=32, Hk=8, D=128, S=131072, tail=0, r=8, K=2, rho=0.95,
+            scale_dtype="fp16", config=5)
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -218,7 +223,8 @@ def build_layers(cfg, rank, device):
         seed = 1000 * rank + L
         k, v, q = synth_case(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"],
                              cfg["rho"], seed, device=device, dtype=torch.bfloat16)
-        c = fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"], quant_bits=8)
+        c = fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"], quant_bits=8,
+                          scale_dtype=torch.float16 if cfg["scale_dtype"] == "fp16" else torch.float32)
         ks, vs = fc._CodecStream(c), fc._CodecStream(c)
         ks.append(k)
         del k
@@ -323,7 +329,7 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
-CODEC_WORKLOADS = ("archive", "read", "png-encode", "png-decode")
+CODEC_WORKLOADS = ("archive", "read", "png-encode", "png-decode", "stream")
 
 
 def run_codec(args):
@@ -399,14 +405,85 @@ def run_codec(args):
     print(json.dumps(line), flush=True)
 
 
+def run_stream(args):
+    """--workload stream: config 4 -- 28 layers of a Qwen3-0.6B-shaped cache
+    (Hkv=8, D=128, bf16, jpeg r=8 K=2 int8), batch 64, one token appended per
+    layer per step; each step also reads layer 0's view incrementally.
+    Timed over 256-step windows at the start (from an empty cache) and at the
+    end of the 65536-token range (after a bulk prefill to 65280 tokens), with
+    CUDA events around every step (host launch overhead included)."""
+    import flashcodec_b200 as fc
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L, B, H, D, S_end, W = 28, 64, 8, 128, 65536, 256
+    g = torch.Generator(device=dev).manual_seed(4)
+    toks = [(torch.randn(B, H, 1, D, generator=g, device=dev).to(torch.bfloat16),
+             torch.randn(B, H, 1, D, generator=g, device=dev).to(torch.bfloat16)) for _ in range(L)]
+
+    def window(cache, steps):
+        stream = torch.cuda.current_stream(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for a, b in ev:
+            a.record(stream)
+            for i in range(L):
+                cache.append(toks[i][0], toks[i][1], i)
+            cache._keys[0].read()
+            b.record(stream)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) / steps * 1e3
+        return statistics.mean(a.elapsed_time(b) for a, b in ev), wall
+
+    def new_cache():
+        return fc.CodecKVCache("jpeg", block_size=8, keep_freqs=2, quant_bits=8)
+
+    c0 = new_cache()
+    for i in range(L):  # first token: allocate the streams
+        c0.append(toks[i][0], toks[i][1], i)
+    window(c0, 8)       # warm-up (kernels loaded, first archive)
+    del c0
+    c1 = new_cache()
+    start_ms, start_wall = window(c1, W)
+    del c1
+    torch.cuda.empty_cache()
+    c2 = new_cache()
+    S_pre = S_end - W
+    for i in range(L):
+        k = synth_stream(B, H, S_pre, D, 0.95, 2 * i, device=dev, dtype=torch.bfloat16)
+        c2.append(k, k, i)  # value content does not change the work
+        del k
+    c2._keys[0].read()
+    end_ms, end_wall = window(c2, W)
+    line = {"metric": "config 4 streaming step (append 28 layers + incremental read of one layer)",
+            "value": end_ms, "unit": "ms/step", "n_gpus": 1, "steps": W, "warmup": 8,
+            "ms_per_step": end_ms, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 4: Qwen3-0.6B-shaped streaming append/archive",
+                       "layers": L, "batch": B, "Hkv": H, "head_dim": D,
+                       "codec": "jpeg r=8 K=2 int8, fp32 scales",
+                       "window_start": {"context": [0, W], "ms_per_step": start_ms,
+                                        "wall_ms_per_step": start_wall},
+                       "window_end": {"context": [S_pre, S_end], "ms_per_step": end_ms,
+                                      "wall_ms_per_step": end_wall},
+                       "timing": "CUDA events around each step on the current stream"},
+            "gpu_launches": None}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(cfg, world):
-    return {"workload": ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K "
-                         "decode-attention launch per layer over the int8 DCT archive"),
+    name = ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K decode-attention "
+            "launch per layer over the int8 DCT archive") if cfg["config"] == 2 else (
+            "config 5: long-context decode, batch-sharded (16 sequences per GPU = global 128 "
+            "at 8 GPUs), S=131072, 8 layer archives, one split-K decode-attention launch per layer")
+    return {"workload": name,
             "layers": cfg["layers"], "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
             "Hq": cfg["Hq"], "Hkv": cfg["Hk"], "head_dim": cfg["D"], "context": cfg["S"],
-            "raw_tail": cfg["tail"], "codec": f"jpeg r={cfg['r']} K={cfg['K']} int8, fp32 scales",
+            "raw_tail": cfg["tail"],
+            "codec": f"jpeg r={cfg['r']} K={cfg['K']} int8, {cfg['scale_dtype']} scales",
             "kv_dtype": "bf16", "parallelism": f"batch-sharded x{world} (no collective)",
-            "l2": "no flush: the archive read each step (~20 GB per GPU) is >100x L2"}
+            "l2": "no flush: the archive read each step (>8 GB per GPU) is >60x L2"}
 
 
 def main():
@@ -415,9 +492,11 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="flashcodec_b200", choices=["flashcodec_b200", "reference"])
-    ap.add_argument("--layers", type=int, default=CFG2["layers"],
+    ap.add_argument("--config", type=int, default=2, choices=(2, 5),
+                    help="attention workload: config 2 (default, the headline) or config 5")
+    ap.add_argument("--layers", type=int, default=None,
                     help="layers (default 36; fewer only for profiling a small case)")
-    ap.add_argument("--batch", type=int, default=CFG2["B"],
+    ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 16; smaller only for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="attention", choices=("attention",) + CODEC_WORKLOADS,
@@ -427,9 +506,13 @@ def main():
     if args.workload != "attention":
         if args.impl == "reference":
             raise SystemExit("--impl reference times the attention workload")
-        run_codec(args)
+        if args.workload == "stream":
+            run_stream(args)
+        else:
+            run_codec(args)
         return
-    cfg = dict(CFG2, layers=args.layers, B=args.batch)
+    base = CFG2 if args.config == 2 else CFG5
+    cfg = dict(base, layers=args.layers or base["layers"], B=args.batch or base["B"])
     if args.impl == "reference":
         run_reference(args, cfg)
         return
@@ -441,7 +524,8 @@ def main():
     torch.cuda.set_device(dev)
     layers = build_layers(cfg, rank, dev)
     n = layers[0][0].n_blocks
-    per_launch = attn_bytes(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"], n, cfg["K"], cfg["tail"])
+    per_launch = attn_bytes(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"], n, cfg["K"], cfg["tail"],
+                            scale_b=2 if cfg["scale_dtype"] == "fp16" else 4)
     outs = [torch.empty_like(q) for _, _, q in layers]
 
     def step():
@@ -507,7 +591,7 @@ def main():
     e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e_steps, world)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg["config"] == 2:
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
         cpu = time_cpu_baseline(cpu_sample_from(layers, cfg), cfg, reps=5, threads=threads)
@@ -515,7 +599,7 @@ def main():
     if rank == 0:
         peak, kind = measured_peaks()
         achieved = per_launch / (kern_max * 1e-3) / 1e9
-        traffic = ncu_traffic()
+        traffic = ncu_traffic() if cfg["config"] == 2 and cfg["B"] == CFG2["B"] else None
         line = {
             "metric": METRIC, "value": world * cfg["B"] / (ms_max * 1e-3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
