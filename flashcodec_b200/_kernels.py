@@ -56,6 +56,14 @@ def as_bhsd(x: torch.Tensor) -> torch.Tensor:
     return x.reshape(1, lead, x.shape[-2], x.shape[-1])
 
 
+def _unit_last(*tensors) -> None:
+    """The kernels index the last dim with unit stride (the ABI carries the
+    strides of the other dims only)."""
+    for t in tensors:
+        if t is not None and t.dim() > 0 and t.shape[-1] > 1 and t.stride(-1) != 1:
+            raise ValueError("the last dimension must be contiguous (stride 1)")
+
+
 def _s(t, *dims):
     return [t.stride(d) for d in dims]
 
@@ -65,6 +73,7 @@ def jpeg_encode(x: torch.Tensor, basis: torch.Tensor, r: int, k: int, out: torch
                 scales: torch.Tensor | None = None, err: torch.Tensor | None = None) -> None:
     """x (B,H,S,D) -> out (B,H,n,k,D) [int8 codes with scales (B,H,n,k,1) | coefficients]."""
     require_cuda(x, basis, out, scales)
+    _unit_last(x, out)
     B, H, S, D = x.shape
     if (scales is None) != (out.dtype != torch.int8):
         raise ValueError("int8 output needs scales; float output takes none")
@@ -84,6 +93,7 @@ def jpeg_decode(coef: torch.Tensor, scales: torch.Tensor | None, basis: torch.Te
                 out: torch.Tensor, out_len: int) -> None:
     """coef (B,H,n,k,D) [+ scales (B,H,n,k,1)] -> out (B,H,>=out_len,D)."""
     require_cuda(coef, scales, basis, out)
+    _unit_last(coef, out)
     B, H, n, k, D = coef.shape
     st = _stream(coef.device)
     with torch.cuda.device(coef.device):
@@ -100,6 +110,7 @@ def png_encode(x: torch.Tensor, r: int, keep_m: int, deltas: torch.Tensor,
                anchors: torch.Tensor) -> None:
     """x (B,H,S,D) -> deltas (B,H,n,r-1,D) fp32, anchors (B,H,n,D) in x.dtype."""
     require_cuda(x, deltas, anchors)
+    _unit_last(x, deltas, anchors)
     B, H, S, D = x.shape
     st = _stream(x.device)
     with torch.cuda.device(x.device):
@@ -113,6 +124,7 @@ def png_decode(deltas: torch.Tensor, anchors: torch.Tensor, out: torch.Tensor,
                out_len: int) -> None:
     """deltas (B,H,n,r-1,D) fp32 + anchors (B,H,n,D) -> out (B,H,>=out_len,D)."""
     require_cuda(deltas, anchors, out)
+    _unit_last(deltas, anchors, out)
     B, H, n, rm1, D = deltas.shape
     st = _stream(deltas.device)
     with torch.cuda.device(deltas.device):

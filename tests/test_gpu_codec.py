@@ -107,6 +107,70 @@ def test_jpeg_odd_shapes_match_oracle(shape, r, k, dt):
     assert same(f32(rec), orc.jpeg_decode(ref, None, basis, r, "f32", out_len=shape[-2]))
 
 
+@pytest.mark.parametrize("shape,r,k,dt,q8", [
+    ((2, 3, 256, 128), 8, 4, torch.bfloat16, True),     # d128 archive, KM = 4
+    ((2, 3, 256, 128), 8, 8, torch.float32, True),      # KM = 8
+    ((1, 2, 517, 128), 16, 4, torch.float16, True),     # r = 16, partial last block
+    ((1, 2, 256, 128), 16, 8, torch.bfloat16, True),
+    ((2, 2, 203, 128), 8, 2, torch.float32, False),     # unquantized coefficients, padding
+    ((2, 2, 256, 128), 16, 3, torch.bfloat16, False),
+])
+def test_jpeg_fast_paths_match_oracle(shape, r, k, dt, q8):
+    """The head-dim-128 fast paths of the archive and read kernels against the
+    oracle, and against the general kernels (the same input at an address
+    off the vector alignment takes them), bit for bit."""
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as K
+    g = torch.Generator().manual_seed(11)
+    x = (torch.cumsum(torch.randn(*shape, generator=g) * 0.3, dim=-2) *
+         torch.exp(0.5 * torch.randn(1, shape[1], 1, shape[-1], generator=g))).to(dt)
+    tag = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}[dt]
+    basis = fc.dct_basis(r, k)
+    ref = orc.jpeg_encode(f32(x), r, k, basis.numpy(), tag)
+    B, H, S, D = shape
+    n = (S + r - 1) // r
+    xd = x.to(DEV)
+    # the same values one element past a vector boundary: the general kernel
+    buf = torch.empty(xd.numel() + 1, dtype=dt, device=DEV)
+    xs = buf[1:].view(shape)
+    xs.copy_(xd)
+    bd = basis.to(DEV).contiguous()
+    for src in (xd, xs):
+        if q8:
+            codes = torch.empty(B, H, n, k, D, dtype=torch.int8, device=DEV)
+            scales = torch.empty(B, H, n, k, 1, dtype=torch.float32, device=DEV)
+            K.jpeg_encode(src, bd, r, k, codes, scales)
+            rq, rs = orc.jpeg_quantize(ref, tag)
+            assert same(codes.cpu().numpy(), rq) and same(f32(scales), rs)
+            for odt in (torch.float32, torch.bfloat16, torch.float16):
+                rec = torch.empty(B, H, S, D, dtype=odt, device=DEV)
+                K.jpeg_decode(codes, scales, bd, r, rec, S)
+                otag = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}[odt]
+                want = orc.jpeg_decode(rq, rs, basis.numpy(), r, otag, out_len=S)
+                assert same(f32(rec), want), odt
+        else:
+            coef = torch.empty(B, H, n, k, D, dtype=dt, device=DEV)
+            K.jpeg_encode(src, bd, r, k, coef)
+            assert same(f32(coef), ref)
+            rec = torch.empty(B, H, S, D, dtype=dt, device=DEV)
+            K.jpeg_decode(coef, None, bd, r, rec, S)
+            assert same(f32(rec), orc.jpeg_decode(ref, None, basis.numpy(), r, tag, out_len=S))
+
+
+def test_png_fast_paths_match_oracle():
+    """png filter/reconstruct fast paths (keep 1.0, r in {8, 16}, 4-aligned
+    rows) against the oracle for fp32, bf16 and fp16, with a partial block."""
+    import flashcodec_b200 as fc
+    g = torch.Generator().manual_seed(5)
+    for dt, r in ((torch.float32, 16), (torch.bfloat16, 8), (torch.float16, 16)):
+        x = torch.cumsum(torch.randn(2, 3, 203, 128, generator=g), dim=-2).to(dt)
+        tag = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}[dt]
+        d, a = fc.png_filter(x.to(DEV), r, 1.0)
+        rd, ra = orc.png_encode(f32(x), r, 1.0)
+        assert same(f32(d), rd) and same(f32(a), ra)
+        assert same(f32(fc.png_reconstruct(d, a)), orc.png_decode(rd, ra, tag))
+
+
 def test_png_topm_and_odd_shapes_match_oracle():
     import flashcodec_b200 as fc
     g = torch.Generator().manual_seed(3)
@@ -176,3 +240,19 @@ def test_fp16_scales_exact_for_bf16_inputs():
                                          scale_dtype=torch.float16))
     tiny.append(torch.full((1, 1, 8, 128), 1e-9, device=DEV))   # scale below fp16 range
     assert tiny.scale_range_errors()
+
+
+def test_low_level_wrappers_refuse_strided_last_dim():
+    """The kernels take unit stride along the head dim; a view with another
+    stride is refused instead of being read wrongly."""
+    from flashcodec_b200 import _kernels as K
+    import flashcodec_b200 as fc
+    wide = torch.zeros(1, 2, 64, 256, device=DEV)
+    xs = wide[..., ::2]
+    codes = torch.empty(1, 2, 8, 2, 128, dtype=torch.int8, device=DEV)
+    scales = torch.empty(1, 2, 8, 2, 1, device=DEV)
+    with pytest.raises(ValueError):
+        K.jpeg_encode(xs, fc.dct_basis(8, 2).to(DEV), 8, 2, codes, scales)
+    with pytest.raises(ValueError):
+        K.png_encode(xs, 8, 7, torch.empty(1, 2, 8, 7, 128, device=DEV),
+                     torch.empty(1, 2, 8, 128, device=DEV))
