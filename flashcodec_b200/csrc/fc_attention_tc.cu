@@ -198,6 +198,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     constexpr int N = GT <= 4 ? 16 : 32;  // B columns: 4 limbs x GT heads, padded
     constexpr int PP = kR / S;            // positions of a block per lane
     constexpr int XF = 2 * GT + 1;        // exchange fields per tile (x 4 warps)
+    // Programmatic dependent launch: the next launch in the stream (when it
+    // is launched as a dependent) may be scheduled once every CTA of this one
+    // has started; it reads nothing before its griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -276,9 +280,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                          smem_addr(&s_tmem)),
                      "r"(kAlloc));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        // inputs, archive and workspace may be written by the previous grid
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0)
             for (; issued < min(kTcStages, 2 * T); issued++) issue(issued);
     } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         // q of the group's heads: per-head scale, int8 limbs (K-major B tile)
         const int d = tid;  // head_dim == 128 == epilogue threads
 #pragma unroll
@@ -701,6 +708,17 @@ bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows) {
 
 size_t align_to(size_t x, size_t al) { return (x + al - 1) / al * al; }
 
+// Launch as a programmatic dependent of the previous kernel in the stream
+// (overlaps this launch's scheduling and barrier/TMEM setup with the previous
+// grid's tail); FLASHCODEC_NO_PDL=1 turns it off for comparisons.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("FLASHCODEC_NO_PDL");
+        return !(e && atoi(e) != 0);
+    }();
+    return on;
+}
+
 // Dynamic shared memory already opted in, per kernel variant (GT x s) and device.
 constexpr int kMaxDevices = 64;
 std::atomic<int> g_smem_opted[16][kMaxDevices];
@@ -778,7 +796,17 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
                                  (int)cudaSharedmemCarveoutMaxShared);
             if (opted) opted->store((int)smem);
         }
-        kern<<<grid, kTcThreads, smem, st>>>(mk, mv, a);
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = grid;
+        lc.blockDim = dim3(kTcThreads);
+        lc.dynamicSmemBytes = smem;
+        lc.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = attr;
+        lc.numAttrs = pdl_enabled() ? 1 : 0;
+        cudaLaunchKernelEx(&lc, kern, mk, mv, a);
     };
     auto by_s = [&](auto gt, int gi) {
         constexpr int GT = decltype(gt)::value;
