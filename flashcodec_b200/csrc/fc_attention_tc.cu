@@ -304,15 +304,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         }
         epi_bar();
 #pragma unroll
+        for (int g = 0; g < GT; g++) {  // one limb split per head
+            int lq[kLimbs] = {0, 0, 0, 0};
+            if (g < G) limbs4(qv[g] / s_sq[g], lq);
+#pragma unroll
+            for (int l = 0; l < kLimbs; l++) bq[sw128_off(kLimbs * g + l, d)] = (unsigned char)(int8_t)lq[l];
+        }
+#pragma unroll
         for (int row = 0; row < N; row++) {
-            const int g = row / kLimbs, l = row % kLimbs;
-            int v = 0;
-            if (g < GT && g < G) {
-                int lq[4];
-                limbs4(qv[g] / s_sq[g], lq);
-                v = lq[l];
-            }
-            bq[sw128_off(row, d)] = (unsigned char)(int8_t)v;
+            if (row >= kLimbs * GT) bq[sw128_off(row, d)] = 0;
             bw[sw128_off(row, d)] = 0;
             bw[N * 128 + sw128_off(row, d)] = 0;
         }
