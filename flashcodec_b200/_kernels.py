@@ -181,6 +181,15 @@ def set_attn_kernel(which: str) -> str:
     return {v: k for k, v in codes.items()}[prev]
 
 
+def selftest_bounded_wait(status: torch.Tensor, epoch: int) -> None:
+    """Launch the bounded-wait self-test on status's device: it gives up after
+    the kernels' wait limit and records `epoch` in status (int32, 1 element)."""
+    require_cuda(status)
+    with torch.cuda.device(status.device):
+        rc = _lib.load().fc_selftest_bounded_wait(_p(status), int(epoch), _stream(status.device))
+    _lib.check(rc, "selftest_bounded_wait")
+
+
 def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
                 ws: torch.Tensor | None = None) -> None:
     """q (B,Hq,1,D); krows/vrows (B,Hk,n,s,D) or None; k/vscales (B,Hk,n,s,1)

@@ -778,6 +778,27 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
     }
 }
 
+namespace fc {
+// One CTA waits on an mbarrier that nothing arrives on (see
+// fc_selftest_bounded_wait): exercises the give-up path of the bounded wait.
+__global__ void selftest_wait_kernel(int *status, int epoch) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    mbar_wait_bounded(&bar, 0, status, epoch);
+}
+}  // namespace fc
+
+extern "C" int fc_selftest_bounded_wait(int *status, int epoch, void *stream) {
+    clear_error();
+    if (!status || epoch <= 0) { set_error("selftest_bounded_wait: null status or epoch <= 0"); return FC_EINVAL; }
+    selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, epoch);
+    return check_launch("selftest_bounded_wait");
+}
+
 extern "C" int fc_set_attn_kernel(int which) {
     if (which != FC_ATTN_AUTO && which != FC_ATTN_CUDA_CORE && which != FC_ATTN_TENSOR_CORE)
         return -1;

@@ -230,7 +230,8 @@ FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t
 
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
  * AUTO uses the tcgen05 int8 tensor-core kernel whenever the archive allows
- * it (contiguous (B, Hk, cap, s, 128) int8 codes, s | 32, Hq/Hk <= 8) and the
+ * it (contiguous (B, Hk, cap, s, 128) int8 codes, block size 8 with
+ * s in {1, 2, 4, 8} stored rows per block, Hq/Hk <= 8) and the
  * CUDA-core kernel otherwise.  CUDA_CORE forces the CUDA-core kernel;
  * TENSOR_CORE makes unsupported layouts fail with FC_ENOTSUP instead of
  * falling back.  Returns the previous setting, or -1 for an unknown value.
@@ -239,6 +240,15 @@ FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t
 #define FC_ATTN_CUDA_CORE 1
 #define FC_ATTN_TENSOR_CORE 2
 FC_API int fc_set_attn_kernel(int which);
+
+/* Self-test of the kernels' bounded waits (failure detection without a GPU
+ * fault): one CTA waits on an mbarrier that nothing arrives on, gives up
+ * after the wait limit every attention-kernel wait uses (100 ms of
+ * %globaltimer time), records `epoch` in the device int *status the way a
+ * timed-out attention launch records its epoch, and exits; the context stays
+ * usable.  Returns FC_OK when the launch was issued.  No counterpart in the
+ * reference. */
+FC_API int fc_selftest_bounded_wait(int *status, int epoch, void *stream);
 
 #ifdef __cplusplus
 }

@@ -228,3 +228,57 @@ def test_tensor_core_refuses_unsupported_layout(kernel_choice):
     kernel_choice("tensor-core")
     with pytest.raises(NotImplementedError):
         fc.codec_decode_attention(q.to(DEV), ks, vs)
+
+
+def test_bounded_wait_gives_up_and_reports():
+    """Failure detection without a GPU fault: a wait on an mbarrier that
+    nothing arrives on gives up after the kernels' 100 ms limit, records the
+    epoch in the status word, and the context stays usable afterwards."""
+    import time
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as K
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    K.selftest_bounded_wait(status, 12345)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    assert status.item() == 12345
+    assert 0.09 <= dt < 5.0, dt
+    k, v, q = bench.synth_case(1, 4, 2, 8 * 30 + 3, 128, 0.95, 6)
+    ks, vs = build("jpeg", dict(keep_freqs=2, quant_bits=8), k.to(DEV), v.to(DEV))
+    out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+    check_close(out, oracle_attention(q, ks, vs), torch.float32)
+    assert K.attn_status(q.to(DEV).device) == 0
+
+
+def test_config5_full_size_kernels_agree():
+    """Config 5 at full per-GPU size (16 sequences, S=131072, K=2, fp16
+    scales): the tensor-core and CUDA-core kernels agree, and sequence 0
+    matches the fp64 oracle."""
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as Kn
+    B, Hq, Hk, S, D = 16, 32, 8, 131072, 128
+    k, v, q = bench.synth_case(B, Hq, Hk, S + 3, D, 0.95, 55, device=DEV, dtype=torch.bfloat16)
+    kw = dict(keep_freqs=2, quant_bits=8, scale_dtype=torch.float16)
+    ks, vs = build("jpeg", kw, k, v)
+    del k, v
+    prev = Kn.set_attn_kernel("tensor-core")
+    try:
+        out_tc = fc.codec_decode_attention(q, ks, vs)
+        Kn.set_attn_kernel("cuda-core")
+        out_cc = fc.codec_decode_attention(q, ks, vs)
+    finally:
+        Kn.set_attn_kernel(prev)
+    diff = (out_tc.float() - out_cc.float()).abs()
+    assert diff.max().item() <= 2e-3 + 2.0 ** -8 * out_cc.float().abs().max().item()
+    # sequence 0 against the oracle (archive rows read back for b = 0)
+    n = ks.n_blocks
+    A = f32(fc.block_basis(ks.codec, ks.block_size))
+    rows = {}
+    for nm, st in (("k", ks), ("v", vs)):
+        rows[nm] = orc.stored_rows("jpeg", codes=st._coeffs[:1, :, :n].cpu().numpy().astype(np.float32),
+                                   scales=f32(st._scales[:1, :, :n]))
+        rows[nm + "raw"] = f32(st.raw[:1])
+    ref = orc.decode_attention(f32(q[:1]), rows["k"], rows["v"], rows["kraw"], rows["vraw"], A)
+    check_close(out_tc[:1], ref, torch.bfloat16)
