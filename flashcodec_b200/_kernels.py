@@ -181,6 +181,35 @@ def set_attn_kernel(which: str) -> str:
     return {v: k for k, v in codes.items()}[prev]
 
 
+def decode_attn_png(q, kanc, vanc, kdel, vdel, kraw, vraw, A, scale, out) -> None:
+    """png archive read in place: anchors (B,Hk,n,D) as row 0 of every block,
+    fp32 deltas (B,Hk,n,r-1,D) as rows 1..r-1; A (r,r) tril(ones)."""
+    require_cuda(q, kanc, vanc, kdel, vdel, kraw, vraw, A, out)
+    _unit_last(kanc, vanc, kdel, vdel)
+    if kanc.stride() != vanc.stride() or kdel.stride() != vdel.stride():
+        raise ValueError("K and V png archives must share one layout")
+    B, Hq, _, D = q.shape
+    Hk, n, rm1 = kdel.shape[1], kdel.shape[2], kdel.shape[3]
+    r = rm1 + 1
+    t = kraw.shape[2] if kraw is not None else 0
+    ws = workspace(q.device, attn_workspace_bytes(B, Hq, Hk, D, n, r, r, t))
+    z3 = (0, 0, 0)
+    st = _stream(q.device)
+    with torch.cuda.device(q.device):
+        rc = _lib.load().fc_decode_attn_png(
+            _p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1), Hk, n, r,
+            _p(kanc), _p(vanc), dtype_code(kanc), *_s(kanc, 0, 1, 2),
+            _p(kdel), _p(vdel), *_s(kdel, 0, 1, 2, 3),
+            _p(kraw), *(_s(kraw, 0, 1, 2) if kraw is not None else z3),
+            _p(vraw), *(_s(vraw, 0, 1, 2) if vraw is not None else z3),
+            dtype_code(kraw) if kraw is not None else 0, t,
+            _p(A), float(scale), _p(out), dtype_code(out), out.stride(0), out.stride(1),
+            _p(ws), ws.numel(), st)
+    if rc != _lib.FC_OK:
+        reset_workspace(q.device)
+    _lib.check(rc, "decode_attn_png")
+
+
 def selftest_bounded_wait(status: torch.Tensor, epoch: int) -> None:
     """Launch the bounded-wait self-test on status's device: it gives up after
     the kernels' wait limit and records `epoch` in status (int32, 1 element)."""

@@ -47,10 +47,7 @@ def _rows(stream):
     if c.name == "jpeg":
         rows = stream._coeffs[:, :, :n]
         return rows, (stream._scales[:, :, :n] if c.quantized else None)
-    # png: [anchor; deltas] as fp32 rows.  Assembled on the device per call;
-    # the kernel itself reads any row layout.
-    return torch.cat([stream._anchors[:, :, :n].unsqueeze(-2).float(),
-                      stream._deltas[:, :, :n]], dim=-2), None
+    raise AssertionError("png archives are read in place by fc_decode_attn_png")
 
 
 def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="auto"):
@@ -83,9 +80,17 @@ def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="au
     Hk = (ks._raw_buf if ks._raw_buf is not None else
           (ks._coeffs if ks.codec.name == "jpeg" else ks._deltas)).shape[1]
     assert Hq % Hk == 0, f"query heads ({Hq}) must be a multiple of kv heads ({Hk})"
+    out = torch.empty_like(query)
+    n = ks.n_blocks
+    if ks.codec.name == "png" and n > 0:
+        # anchors and deltas read where the archive keeps them (no row assembly)
+        A = _device_A(ks.codec, ks.block_size, query.device)
+        K.decode_attn_png(query, ks._anchors[:, :, :n], vs._anchors[:, :, :n],
+                          ks._deltas[:, :, :n], vs._deltas[:, :, :n], ks.raw, vs.raw, A,
+                          scale, out)
+        return out
     krows, kscales = _rows(ks)
     vrows, vscales = _rows(vs)
     A = _device_A(ks.codec, ks.block_size, query.device) if krows is not None else None
-    out = torch.empty_like(query)
     K.decode_attn(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale, out)
     return out

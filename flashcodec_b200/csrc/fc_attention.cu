@@ -68,6 +68,11 @@ struct AttnArgs {
     int64_t ks_sb, ks_sh, ks_sn, vs_sb, vs_sh, vs_sn;
     const void *kraw, *vraw;
     int raw_dtype;
+    // png archives: row 0 of every block from these anchors (own dtype and
+    // strides), rows 1..r-1 from krows/vrows (the fp32 deltas); null otherwise
+    const void *kanc, *vanc;
+    int anc_dtype;
+    int64_t a_sb, a_sh, a_sn;
     int64_t kr_sb, kr_sh, kr_st, vr_sb, vr_sh, vr_st;
     int n_raw;
     const float *A;
@@ -205,7 +210,7 @@ attn_kernel(AttnArgs a) {
             for (int off = lpr >> 1; off > 0; off >>= 1)
                 part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
     };
-    auto row_dot_raw = [&](const void *base, int64_t off, bool valid, float part[GT]) {
+    auto row_dot_raw = [&](const void *base, int64_t off, bool valid, float part[GT], int dt) {
 #pragma unroll
         for (int g = 0; g < GT; g++) part[g] = 0.0f;
         if (valid) {
@@ -215,7 +220,7 @@ attn_kernel(AttnArgs a) {
                 for (int v = 0; v < VEC; v++) {
                     const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
                     if (d < a.D) {
-                        const float x = load_as_f32(base, off + d, a.raw_dtype);
+                        const float x = load_as_f32(base, off + d, dt);
 #pragma unroll
                         for (int g = 0; g < GT; g++) part[g] = fmaf(qr[g][c][v], x, part[g]);
                     }
@@ -257,7 +262,12 @@ attn_kernel(AttnArgs a) {
             const bool valid = row < krows_total;
             const int blk = valid ? row / s : 0, j = valid ? row % s : 0;
             float part[GT];
-            row_dot_typed(kbase + (int64_t)blk * a.k_sn + (int64_t)j * a.k_sj, valid, part);
+            if (a.kanc && j == 0)
+                row_dot_raw(a.kanc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn, valid, part,
+                            a.anc_dtype);
+            else
+                row_dot_typed(kbase + (int64_t)blk * a.k_sn + (int64_t)(j - (a.kanc ? 1 : 0)) * a.k_sj,
+                              valid, part);
             if (valid && li == 0) {
                 const float ks = sks[row];
 #pragma unroll
@@ -270,7 +280,7 @@ attn_kernel(AttnArgs a) {
         const int t = base + warp * rpw + lr;
         const bool valid = t < nraw;
         float part[GT];
-        row_dot_raw(a.kraw, b * a.kr_sb + hk * a.kr_sh + (int64_t)t * a.kr_st, valid, part);
+        row_dot_raw(a.kraw, b * a.kr_sb + hk * a.kr_sh + (int64_t)t * a.kr_st, valid, part, a.raw_dtype);
         if (valid && li == 0) {
 #pragma unroll
             for (int g = 0; g < GT; g++) ssc[(krows_total + t) * GT + g] = part[g];
@@ -349,6 +359,24 @@ attn_kernel(AttnArgs a) {
         }
     };
 
+    // one row of run-time dtype (png anchors)
+    auto accum_any = [&](const void *base, int64_t off, int dt, int wrow) {
+        float w[GT];
+#pragma unroll
+        for (int g = 0; g < GT; g++) w[g] = ssc[wrow * GT + g];
+#pragma unroll
+        for (int c = 0; c < NCH; c++)
+#pragma unroll
+            for (int v = 0; v < VEC; v++) {
+                const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
+                if (d < a.D) {
+                    const float x = load_as_f32(base, off + d, dt);
+#pragma unroll
+                    for (int g = 0; g < GT; g++) acc[g][c][v] = fmaf(w[g], x, acc[g][c][v]);
+                }
+            }
+    };
+
     if (BULK) {
         for (int t = ntiles; t < ttot; t++) {
             const bool ok = mbar_wait_bounded(bars + (t % kStages), (t / kStages) & 1, a.status,
@@ -369,7 +397,11 @@ attn_kernel(AttnArgs a) {
             const int row = base + warp * rpw + lr;
             if (row < krows_total) {
                 const int blk = row / s, j = row % s;
-                accum_typed(vbase + (int64_t)blk * a.v_sn + (int64_t)j * a.v_sj, row);
+                if (a.vanc && j == 0)
+                    accum_any(a.vanc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn, a.anc_dtype, row);
+                else
+                    accum_typed(vbase + (int64_t)blk * a.v_sn + (int64_t)(j - (a.vanc ? 1 : 0)) * a.v_sj,
+                                row);
             }
         }
     }
@@ -638,7 +670,15 @@ extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
     return w;
 }
 
-extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+// png archive rows of fc_decode_attn_png: the anchors stand for row 0 of every
+// block (K and V anchors share one layout).
+struct PngAnchors {
+    const void *k, *v;
+    int dtype;
+    int64_t sb, sh, sn;
+};
+
+static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
                               int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int s,
                               int r, int rows_dtype, const void *k_rows, int64_t k_sb,
                               int64_t k_sh, int64_t k_sn, int64_t k_sj, const void *v_rows,
@@ -650,7 +690,8 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
                               int64_t vr_st, int raw_dtype, int64_t n_raw, const float *A,
                               float softmax_scale, void *out, int out_dtype, int64_t o_sb,
                               int64_t o_sh, void *workspace, size_t workspace_bytes,
-                              void *stream) {
+                              void *stream,
+                            const PngAnchors *png) {
     clear_error();
     if (B < 0 || Hq <= 0 || Hk <= 0 || D <= 0) { set_error("decode_attn: bad shape"); return FC_EINVAL; }
     if (Hq % Hk != 0) { set_error("decode_attn: Hq (%lld) must be a multiple of Hk (%lld)", (long long)Hq, (long long)Hk); return FC_EINVAL; }
@@ -668,7 +709,8 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
     if (!q || !out || (n_blocks > 0 && (!k_rows || !v_rows || !A))) { set_error("decode_attn: null pointer"); return FC_EINVAL; }
     if (n_blocks == 0) { s = 1; r = std::max<int>(r, 1); rows_dtype = FC_F32; }
 
-    const int sel = g_attn_kernel.load();
+    // png rows come from two tensors: the CUDA-core kernel's direct-load path
+    const int sel = png ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
     if (n_blocks > 0 && sel != FC_ATTN_CUDA_CORE) {
         const int64_t G = Hq / Hk, row = (int64_t)s * D;
         const bool contig = tc_supported(D, s, r, G, rows_dtype) && k_sj == D && k_sn == row &&
@@ -720,9 +762,10 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
         }
     }
     const int es = dtype_size(rows_dtype);
-    const int vm = n_blocks > 0 ? pick_vec_mode(D, es, k_rows, v_rows, k_sb, k_sh, k_sn, k_sj,
-                                                v_sb, v_sh, v_sn, v_sj, s)
-                                : 0;
+    int vm = n_blocks > 0 ? pick_vec_mode(D, es, k_rows, v_rows, k_sb, k_sh, k_sn, k_sj,
+                                          v_sb, v_sh, v_sn, v_sj, s)
+                          : 0;
+    if (png) vm = std::min(vm, 1);  // rows of a block are not one contiguous run
     Plan p = make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm);
     if (p.smem > 200 * 1024) { set_error("decode_attn: shared memory plan too large"); return FC_ENOTSUP; }
     if (!workspace || workspace_bytes < p.ws) {
@@ -742,6 +785,10 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
     a.ks_sb = ks_sb; a.ks_sh = ks_sh; a.ks_sn = ks_sn;
     a.vs_sb = vs_sb; a.vs_sh = vs_sh; a.vs_sn = vs_sn;
     a.kraw = k_raw; a.vraw = v_raw; a.raw_dtype = raw_dtype;
+    if (png) {
+        a.kanc = png->k; a.vanc = png->v; a.anc_dtype = png->dtype;
+        a.a_sb = png->sb; a.a_sh = png->sh; a.a_sn = png->sn;
+    }
     a.kr_sb = kr_sb; a.kr_sh = kr_sh; a.kr_st = kr_st;
     a.vr_sb = vr_sb; a.vr_sh = vr_sh; a.vr_st = vr_st;
     a.n_raw = (int)n_raw;
@@ -776,6 +823,50 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
         case FC_F16: return launch_rt<__half>(p, a, grid, st);
         default: return launch_rt<float>(p, a, grid, st);
     }
+}
+
+extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                              int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int s,
+                              int r, int rows_dtype, const void *k_rows, int64_t k_sb,
+                              int64_t k_sh, int64_t k_sn, int64_t k_sj, const void *v_rows,
+                              int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t v_sj,
+                              const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                              const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                              int scale_dtype, const void *k_raw, int64_t kr_sb, int64_t kr_sh,
+                              int64_t kr_st, const void *v_raw, int64_t vr_sb, int64_t vr_sh,
+                              int64_t vr_st, int raw_dtype, int64_t n_raw, const float *A,
+                              float softmax_scale, void *out, int out_dtype, int64_t o_sb,
+                              int64_t o_sh, void *workspace, size_t workspace_bytes,
+                              void *stream) {
+    return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype, k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj, k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn, scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st, raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int fc_decode_attn_png(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                  int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int r,
+                                  const void *k_anchors, const void *v_anchors, int anchor_dtype,
+                                  int64_t a_sb, int64_t a_sh, int64_t a_sn,
+                                  const float *k_deltas, const float *v_deltas, int64_t d_sb,
+                                  int64_t d_sh, int64_t d_sn, int64_t d_si,
+                                  const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
+                                  const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+                                  int raw_dtype, int64_t n_raw, const float *A,
+                                  float softmax_scale, void *out, int out_dtype, int64_t o_sb,
+                                  int64_t o_sh, void *workspace, size_t workspace_bytes,
+                                  void *stream) {
+    clear_error();
+    if (n_blocks > 0 && (r < 2 || !k_anchors || !v_anchors || !k_deltas || !v_deltas ||
+                         !is_float_dtype(anchor_dtype))) {
+        set_error("decode_attn_png: need r >= 2, anchors of f32/bf16/f16 and fp32 deltas");
+        return FC_EINVAL;
+    }
+    const PngAnchors png{k_anchors, v_anchors, anchor_dtype, a_sb, a_sh, a_sn};
+    // rows j >= 1 of a block are deltas row j - 1: s = r stored rows, A = tril(ones)
+    return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, r, r, FC_F32,
+                            k_deltas, d_sb, d_sh, d_sn, d_si, v_deltas, d_sb, d_sh, d_sn, d_si,
+                            nullptr, 0, 0, 0, nullptr, 0, 0, 0, FC_F32, k_raw, kr_sb, kr_sh, kr_st,
+                            v_raw, vr_sb, vr_sh, vr_st, raw_dtype, n_raw, A, softmax_scale, out,
+                            out_dtype, o_sb, o_sh, workspace, workspace_bytes, stream,
+                            n_blocks > 0 ? &png : nullptr);
 }
 
 namespace fc {

@@ -190,6 +190,31 @@ FC_API int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int
                    void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Decode attention over a png archive read in place: replaces the
+ * [anchor; deltas] row assembly of flashcodec/attention.py:59-61 (the rows the
+ * png path of codec_decode_attention, attention.py:64-140, materialises before
+ * its einsums).  Row 0 of every block is the anchor (k_anchors / v_anchors,
+ * (B, Hk, n_blocks, D) of anchor_dtype, strides a_*, shared by K and V), rows
+ * 1..r-1 are the fp32 deltas ((B, Hk, n_blocks, r-1, D), strides d_*, shared
+ * by K and V); A is the (r, r) tril(ones) synthesis matrix.  Everything else
+ * as fc_decode_attn, with s = r and the same workspace size
+ * (fc_decode_attn_workspace_size(B, Hq, Hk, D, n_blocks, r, r, n_raw)).
+ * Runs the CUDA-core kernel whatever fc_set_attn_kernel selects.
+ */
+FC_API int fc_decode_attn_png(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                   int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int r,
+                   const void *k_anchors, const void *v_anchors, int anchor_dtype,
+                   int64_t a_sb, int64_t a_sh, int64_t a_sn,
+                   const float *k_deltas, const float *v_deltas,
+                   int64_t d_sb, int64_t d_sh, int64_t d_sn, int64_t d_si,
+                   const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
+                   const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+                   int raw_dtype, int64_t n_raw,
+                   const float *A, float softmax_scale,
+                   void *out, int out_dtype, int64_t o_sb, int64_t o_sh,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * Decode attention that allocates nothing.  No counterpart in the reference:
  * an addition of this library for callers that cannot allocate device
  * memory -- engines that hand all of HBM to their KV block pool at start-up

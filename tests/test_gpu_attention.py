@@ -282,3 +282,19 @@ def test_config5_full_size_kernels_agree():
         rows[nm + "raw"] = f32(st.raw[:1])
     ref = orc.decode_attention(f32(q[:1]), rows["k"], rows["v"], rows["kraw"], rows["vraw"], A)
     check_close(out_tc[:1], ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dt,r,keep,tail", [
+    (torch.bfloat16, 8, 1.0, 3),     # bf16 anchors, fp32 deltas
+    (torch.float32, 16, 1.0, 0),
+    (torch.float16, 8, 0.5, 5),      # Top-M pruned deltas
+])
+def test_png_attention_reads_archive_in_place(dt, r, keep, tail):
+    """png attention from the archive's own anchor and delta tensors (no row
+    assembly) against the fp64 oracle."""
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(2, 8, 4, r * 40 + tail, 64, 0.98, 17, dtype=dt)
+    ks, vs = build("png", dict(keep_ratio=keep), k.to(DEV), v.to(DEV), r=r)
+    out = fc.codec_decode_attention(q.to(DEV), ks, vs)
+    assert out.dtype == dt
+    check_close(out, oracle_attention(q, ks, vs), dt)
