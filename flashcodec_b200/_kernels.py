@@ -210,6 +210,31 @@ def decode_attn_png(q, kanc, vanc, kdel, vdel, kraw, vraw, A, scale, out) -> Non
     _lib.check(rc, "decode_attn_png")
 
 
+def gather_batch(src: torch.Tensor, idx: torch.Tensor, live: int) -> torch.Tensor:
+    """New tensor like src (B_src, H, L, ...) with batch rows src[idx[b]]:
+    the first `live` entries of dim 2 are gathered (the rest is left
+    uninitialised, as beyond a stream's live length).  idx: int64 on
+    src.device, values in [0, B_src)."""
+    require_cuda(src, idx)
+    if not src.is_contiguous():
+        raise ValueError("gather_batch needs a contiguous source")
+    B_src, H = src.shape[0], src.shape[1]
+    if idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= B_src):
+        raise IndexError(f"batch index out of range for {B_src} rows")
+    dst = torch.empty((idx.numel(),) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    row = src[0, 0, 0].numel() * src.element_size() if src.dim() > 2 else src.element_size()
+    slab = live * row
+    st = _stream(src.device)
+    with torch.cuda.device(src.device):
+        rc = _lib.load().fc_gather_batch(
+            _p(src), B_src, _p(dst), idx.numel(), H, slab,
+            src.stride(0) * src.element_size(), src.stride(1) * src.element_size(),
+            dst.stride(0) * dst.element_size(), dst.stride(1) * dst.element_size(),
+            _p(idx), st)
+    _lib.check(rc, "gather_batch")
+    return dst
+
+
 def selftest_bounded_wait(status: torch.Tensor, epoch: int) -> None:
     """Launch the bounded-wait self-test on status's device: it gives up after
     the kernels' wait limit and records `epoch` in status (int32, 1 element)."""

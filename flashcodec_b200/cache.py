@@ -285,43 +285,26 @@ class _CodecStream:
             self._raw_len = tail
 
     def select_batch(self, idx):
-        """Gather rows of the batch dim (beam search; flashcodec/cache.py:259-301)."""
+        """Gather rows of the batch dim (beam search; flashcodec/cache.py:259-301).
+        Every live prefix (archive, reconstruction, raw tail) is gathered into
+        a new buffer by fc_gather_batch, one read and one write per byte;
+        indices outside the batch raise IndexError."""
         if self._raw_len == 0 and self.n_blocks == 0 and self._rec is None:
             return
         like = (self._raw_buf if self._raw_buf is not None else
                 (self._coeffs if self.codec.name == "jpeg" else self._deltas))
-        idx = idx.to(like.device)
+        idx = idx.to(device=like.device, dtype=torch.int64).contiguous()
         r = self.block_size
         if self._raw_buf is not None:
-            self._raw_buf = self._raw_buf.index_select(0, idx)
-        if idx.numel() == like.shape[0]:
-            if self.n_blocks:
-                for t in self._archive_tensors():
-                    t[:, :, :self.n_blocks] = t[:, :, :self.n_blocks].index_select(0, idx)
-            if self._rec is not None and self._rec_blocks:
-                done = self._rec_blocks * r
-                # a new buffer: read() may have handed out views of the old one
-                new_r = torch.empty_like(self._rec)
-                new_r[:, :, :done] = self._rec[:, :, :done].index_select(0, idx)
-                self._rec = new_r
-            return
-        B, H, D = idx.numel(), like.shape[1], like.shape[-1]
+            self._raw_buf = K.gather_batch(self._raw_buf, idx, self._raw_buf.shape[2])
         if self._capacity:
-            for attr, shape, dtype in self._archive_spec(self._capacity, B, H, D):
-                old = getattr(self, attr)
-                new = torch.empty(shape, dtype=dtype, device=like.device)
-                if self.n_blocks:
-                    new[:, :, :self.n_blocks] = old[:, :, :self.n_blocks].index_select(0, idx)
-                setattr(self, attr, new)
+            for attr, _, _ in self._archive_spec(self._capacity, *like.shape[:2], like.shape[-1]):
+                setattr(self, attr, K.gather_batch(getattr(self, attr), idx, self.n_blocks))
         if self._rec is not None:
-            new_r = torch.empty((B, H, self._rec_capacity, D), dtype=self._rec.dtype,
-                                device=like.device)
-            if self._rec_blocks:
-                done = self._rec_blocks * r
-                new_r[:, :, :done] = self._rec[:, :, :done].index_select(0, idx)
-            self._rec = new_r
+            # a new buffer also keeps views handed out by read() intact
+            self._rec = K.gather_batch(self._rec, idx, self._rec_blocks * r)
         if self.meta is not None:
-            self.meta = (B,) + self.meta[1:]
+            self.meta = (idx.numel(),) + self.meta[1:]
 
     def _archive_tensors(self):
         """Live archive tensors (flashcodec/cache.py:303-308)."""

@@ -253,6 +253,18 @@ FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t
                    const float *A, float softmax_scale,
                    void *out, int out_dtype, int64_t o_sb, int64_t o_sh, void *stream);
 
+/* Batch gather for beam-search reordering: replaces the index_select +
+ * copy-back of every stream tensor in _CodecStream.select_batch
+ * (flashcodec/cache.py:259-301).  For each destination (b, h) in B x H, copies
+ * `slab_bytes` bytes from src + idx[b]*src_sb + h*src_sh to
+ * dst + b*dst_sb + h*dst_sh (strides in bytes; a slab is the live prefix of
+ * one (batch, head) row of an archive, reconstruction or raw-tail tensor).
+ * idx: B device int64 values in [0, B_src) (the caller checks them; the kernel
+ * skips any outside); dst must not overlap src; B * H <= 65535. */
+FC_API int fc_gather_batch(const void *src, int64_t B_src, void *dst, int64_t B, int64_t H,
+                           int64_t slab_bytes, int64_t src_sb, int64_t src_sh,
+                           int64_t dst_sb, int64_t dst_sh, const int64_t *idx, void *stream);
+
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
  * AUTO uses the tcgen05 int8 tensor-core kernel whenever the archive allows
  * it (contiguous (B, Hk, cap, s, 128) int8 codes, block size 8 with

@@ -211,3 +211,28 @@ def test_streaming_decode_one_token_per_step():
     assert torch.equal(one._keys[0]._coeffs[:, :, :n], c._keys[0]._coeffs[:, :, :n])
     assert torch.equal(one._values[0]._scales[:, :, :n], c._values[0]._scales[:, :, :n])
     assert torch.equal(one._keys[0].raw, c._keys[0].raw)
+
+
+def test_reorder_gathers_archive_bitwise_and_checks_indices():
+    """select_batch (fc_gather_batch) moves every live prefix bit for bit,
+    with repeated indices (beam search), and refuses indices outside the batch
+    before touching anything."""
+    import flashcodec_b200 as fc
+    g = torch.Generator().manual_seed(8)
+    kb = torch.randn(3, H, S + 5, D, generator=g).to(torch.bfloat16).to(DEV)
+    vb = torch.randn(3, H, S + 5, D, generator=g).to(torch.bfloat16).to(DEV)
+    for mode, kw in (("jpeg", dict(keep_freqs=2, quant_bits=8)), ("png", dict(keep_ratio=1.0))):
+        c = fc.CodecKVCache(mode=mode, block_size=R, **kw)
+        c.append(kb, vb, 0)
+        ks = c._keys[0]
+        n = ks.n_blocks
+        before = [t[:, :, :n].clone() for t in ks._archive_tensors()] + [ks.raw.clone()]
+        idx = torch.tensor([2, 2, 0, 1])
+        c.reorder_cache(idx)
+        i = idx.to(DEV)
+        after = [t[:, :, :n] for t in ks._archive_tensors()] + [ks.raw]
+        for x, y in zip(before, after):
+            assert torch.equal(y, x.index_select(0, i))
+        with pytest.raises(IndexError):
+            c.reorder_cache(torch.tensor([0, 7]))
+        assert ks.raw.shape[0] == 4
