@@ -100,3 +100,28 @@ def test_workspace_size_is_host_only(lib):
     # of the 553 MB archive of this shape (config 2, one layer)
     assert n < 0.05 * 553_648_128
     assert lib.fc_decode_attn_workspace_size(1, 3, 2, 64, 8, 2, 8, 0) == 0
+
+
+def test_new_entry_points_validate_on_the_host(lib):
+    """fc_decode_attn_png, fc_gather_batch and fc_selftest_bounded_wait refuse
+    bad arguments before any CUDA call."""
+    from flashcodec_b200 import _lib
+    P = ctypes.c_void_p
+    d = P(0x1000)
+    # png attention: r < 2, and missing anchors
+    for r, kanc in ((1, d), (8, None)):
+        rc = lib.fc_decode_attn_png(d, _lib.FC_F32, 1, 4, 64, 256, 64, 2, 4, r,
+                                    kanc, d, _lib.FC_F32, 0, 0, 0, d, d, 0, 0, 0, 0,
+                                    None, 0, 0, 0, None, 0, 0, 0, _lib.FC_F32, 0,
+                                    d, 0.125, d, _lib.FC_F32, 256, 64, None, 0, None)
+        assert rc == _lib.FC_EINVAL
+    # gather: null index, destination equal to the source, nothing to do
+    assert lib.fc_gather_batch(d, 2, P(0x2000), 2, 2, 64, 256, 64, 256, 64, None,
+                               None) == _lib.FC_EINVAL
+    assert lib.fc_gather_batch(d, 2, d, 2, 2, 64, 256, 64, 256, 64, P(0x3000),
+                               None) == _lib.FC_EINVAL
+    assert lib.fc_gather_batch(d, 2, P(0x2000), 0, 2, 64, 256, 64, 256, 64, P(0x3000),
+                               None) == _lib.FC_OK
+    # self-test: null status, epoch <= 0
+    assert lib.fc_selftest_bounded_wait(None, 1, None) == _lib.FC_EINVAL
+    assert lib.fc_selftest_bounded_wait(d, 0, None) == _lib.FC_EINVAL
