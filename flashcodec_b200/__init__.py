@@ -16,11 +16,31 @@ from .attention import block_basis, codec_decode_attention
 from .cache import CodecKVCache, _CodecStream, make_codec
 from .codecs import (JPEGCodec, PNGCodec, dct_basis, dct_compress, dct_decompress,
                      dequantize_coeffs, png_filter, png_reconstruct, quantize_coeffs)
+from .patch import (apply_flash_codec, find_attention_modules, remove_flash_codec,
+                    undo_flash_codec)
+from .patch_attention import (apply_codec_attention, codec_attention_stats,
+                              remove_codec_attention)
 
 __version__ = "0.1.0"
 
+_LAZY = ("FlashCodecCache", "FlashCodecLayer", "HAS_HF_CACHE")
+
+
+def __getattr__(name):
+    """transformers-backed names load on first use (flashcodec/__init__.py:15-16
+    imports them eagerly; importing transformers takes seconds)."""
+    if name in _LAZY:
+        from . import hf_cache
+        return getattr(hf_cache, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
+
+
 __all__ = [
-    "CodecKVCache", "make_codec", "JPEGCodec", "PNGCodec",
+    "apply_flash_codec", "remove_flash_codec", "undo_flash_codec",
+    "find_attention_modules",
+    "apply_codec_attention", "remove_codec_attention", "codec_attention_stats",
+    "CodecKVCache", "FlashCodecCache", "FlashCodecLayer", "make_codec",
+    "HAS_HF_CACHE", "JPEGCodec", "PNGCodec",
     "codec_decode_attention", "block_basis",
     "dct_basis", "dct_compress", "dct_decompress",
     "quantize_coeffs", "dequantize_coeffs",

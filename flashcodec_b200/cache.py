@@ -432,3 +432,12 @@ class CodecKVCache:
     def __repr__(self):
         return (f"CodecKVCache(mode={self.mode!r}, codec={self.codec}, "
                 f"layers={sorted(set(self._keys) | set(self._values))})")
+
+
+def __getattr__(name):
+    """The transformers-backed classes load on first use (importing
+    transformers takes seconds)."""
+    if name in ("FlashCodecCache", "FlashCodecLayer", "HAS_HF_CACHE"):
+        from . import hf_cache
+        return getattr(hf_cache, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
