@@ -112,6 +112,21 @@ def attn_bytes(B, Hq, Hk, D, n, K, tail, code_b=1, scale_b=4, io_b=2):
             + 2 * B * Hk * tail * D * io_b + 2 * B * Hq * D * io_b)
 
 
+def codec_attn_bytes(cfg, n):
+    """Algorithmic bytes of one launch for the archive format in cfg:
+    jpeg-int8 (codes + scales), jpeg-fp (bf16 coefficients, quant_bits=0) or
+    png (bf16 anchor + fp32 deltas per block)."""
+    codec = cfg.get("codec", "jpeg-int8")
+    B, Hq, Hk, D, tail = cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"], cfg["tail"]
+    if codec == "jpeg-int8":
+        return attn_bytes(B, Hq, Hk, D, n, cfg["K"], tail,
+                          scale_b=2 if cfg["scale_dtype"] == "fp16" else 4)
+    if codec == "jpeg-fp":
+        return attn_bytes(B, Hq, Hk, D, n, cfg["K"], tail, code_b=2, scale_b=0)
+    per_block = D * 2 + (cfg["r"] - 1) * D * 4
+    return 2 * B * Hk * n * per_block + 2 * B * Hk * tail * D * 2 + 2 * B * Hq * D * 2
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -223,8 +238,14 @@ def build_layers(cfg, rank, device):
         seed = 1000 * rank + L
         k, v, q = synth_case(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"],
                              cfg["rho"], seed, device=device, dtype=torch.bfloat16)
-        c = fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"], quant_bits=8,
-                          scale_dtype=torch.float16 if cfg["scale_dtype"] == "fp16" else torch.float32)
+        codec = cfg.get("codec", "jpeg-int8")
+        if codec == "png":
+            c = fc.make_codec("png", block_size=cfg["r"], keep_ratio=1.0)
+        else:
+            c = fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"],
+                              quant_bits=8 if codec == "jpeg-int8" else 0,
+                              scale_dtype=torch.float16 if cfg["scale_dtype"] == "fp16"
+                              else torch.float32)
         ks, vs = fc._CodecStream(c), fc._CodecStream(c)
         ks.append(k)
         del k
@@ -477,11 +498,21 @@ def workload_config(cfg, world):
             "launch per layer over the int8 DCT archive") if cfg["config"] == 2 else (
             "config 5: long-context decode, batch-sharded (16 sequences per GPU = global 128 "
             "at 8 GPUs), S=131072, 8 layer archives, one split-K decode-attention launch per layer")
+    codec = cfg.get("codec", "jpeg-int8")
+    if codec == "jpeg-fp":
+        name = name.replace("int8 DCT archive", "unquantized DCT archive (bf16 coefficients)")
+        desc = f"jpeg r={cfg['r']} K={cfg['K']} quant_bits=0, bf16 coefficients"
+    elif codec == "png":
+        name = name.replace("int8 DCT archive", "png archive (bf16 anchors + fp32 deltas)")
+        name = name.replace("36 layers", f"{cfg['layers']} layers")
+        desc = f"png r={cfg['r']} keep_ratio=1.0"
+    else:
+        desc = f"jpeg r={cfg['r']} K={cfg['K']} int8, {cfg['scale_dtype']} scales"
     return {"workload": name,
             "layers": cfg["layers"], "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
             "Hq": cfg["Hq"], "Hkv": cfg["Hk"], "head_dim": cfg["D"], "context": cfg["S"],
             "raw_tail": cfg["tail"],
-            "codec": f"jpeg r={cfg['r']} K={cfg['K']} int8, {cfg['scale_dtype']} scales",
+            "codec": desc,
             "kv_dtype": "bf16", "parallelism": f"batch-sharded x{world} (no collective)",
             "l2": "no flush: the archive read each step (>8 GB per GPU) is >60x L2"}
 
@@ -498,6 +529,10 @@ def main():
                     help="layers (default 36; fewer only for profiling a small case)")
     ap.add_argument("--batch", type=int, default=None,
                     help="sequences per GPU (default 16; smaller only for profiling)")
+    ap.add_argument("--codec", default="jpeg-int8", choices=("jpeg-int8", "jpeg-fp", "png"),
+                    help="archive format of the attention workload: jpeg-int8 (default, the "
+                         "headline), jpeg-fp (quant_bits=0, bf16 coefficients) or png "
+                         "(r=8, lossless; 4 layers by default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="attention", choices=("attention",) + CODEC_WORKLOADS,
                     help="attention (default, config 2) or one codec kernel's HBM throughput")
@@ -512,7 +547,13 @@ def main():
             run_codec(args)
         return
     base = CFG2 if args.config == 2 else CFG5
-    cfg = dict(base, layers=args.layers or base["layers"], B=args.batch or base["B"])
+    cfg = dict(base, layers=args.layers or base["layers"], B=args.batch or base["B"],
+               codec=args.codec)
+    if args.codec != "jpeg-int8":
+        if args.impl == "reference" or args.gpus != 1:
+            raise SystemExit("--codec other than jpeg-int8 is a 1-GPU secondary line")
+        if args.codec == "png" and not args.layers:
+            cfg["layers"] = 4        # ~4 GB of fp32 deltas per layer
     if args.impl == "reference":
         run_reference(args, cfg)
         return
@@ -524,8 +565,7 @@ def main():
     torch.cuda.set_device(dev)
     layers = build_layers(cfg, rank, dev)
     n = layers[0][0].n_blocks
-    per_launch = attn_bytes(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"], n, cfg["K"], cfg["tail"],
-                            scale_b=2 if cfg["scale_dtype"] == "fp16" else 4)
+    per_launch = codec_attn_bytes(cfg, n)
     outs = [torch.empty_like(q) for _, _, q in layers]
 
     def step():
@@ -588,7 +628,8 @@ def main():
     e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e_steps, world)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg["config"] == 2:
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and cfg["config"] == 2
+            and cfg["codec"] == "jpeg-int8"):
         threads = os.cpu_count() or 1
         torch.set_num_threads(threads)
         cpu = time_cpu_baseline(cpu_sample_from(layers, cfg), cfg, reps=5, threads=threads)
@@ -596,9 +637,12 @@ def main():
     if rank == 0:
         peak, kind = measured_peaks()
         achieved = per_launch / (kern_max * 1e-3) / 1e9
-        traffic = ncu_traffic() if cfg["config"] == 2 and cfg["B"] == CFG2["B"] else None
+        traffic = (ncu_traffic() if cfg["config"] == 2 and cfg["B"] == CFG2["B"]
+                   and cfg["codec"] == "jpeg-int8" else None)
         line = {
-            "metric": METRIC, "value": world * cfg["B"] / (ms_max * 1e-3), "unit": "tokens/s",
+            "metric": METRIC if cfg["codec"] == "jpeg-int8" else
+            f"decode-attn tokens/s & achieved HBM GB/s (% of peak) on {cfg['codec']} KV, 1 B200",
+            "value": world * cfg["B"] / (ms_max * 1e-3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic", "config": workload_config(cfg, world),

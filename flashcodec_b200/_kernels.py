@@ -235,6 +235,56 @@ def gather_batch(src: torch.Tensor, idx: torch.Tensor, live: int) -> torch.Tenso
     return dst
 
 
+def _rows3(x: torch.Tensor, name: str) -> torch.Tensor:
+    """(B, H, D) view of a one-token (B, H, D) or (B, H, 1, D) tensor."""
+    if x.dim() == 4:
+        if x.shape[2] != 1:
+            raise ValueError(f"{name}: one token per sequence expected, got {tuple(x.shape)}")
+        x = x[:, :, 0]
+    if x.dim() != 3:
+        raise ValueError(f"{name}: expected (B, H, D) or (B, H, 1, D), got {tuple(x.shape)}")
+    if x.shape[-1] > 1 and x.stride(-1) != 1:
+        raise ValueError(f"{name}: the head dim must have unit stride")
+    return x
+
+
+def rope_kv_append(q, k, v, cos, sin, q_out, k_out, v_out=None) -> None:
+    """Rotary embedding of one token's q and k (rotate-half form) written to
+    q_out and k_out, and v copied to v_out, in one launch (fc_rope_kv_append).
+    q/q_out (B,Hq[,1],D); k, v, k_out, v_out (B,Hk[,1],D) (outputs may be
+    strided views such as a raw-tail slot); cos/sin (B or 1, [1, [1,]] D).
+    All one dtype; v and v_out are optional together."""
+    require_cuda(q, k, v, cos, sin, q_out, k_out, v_out)
+    q, q_out = _rows3(q, "q"), _rows3(q_out, "q_out")
+    k, k_out = _rows3(k, "k"), _rows3(k_out, "k_out")
+    if (v is None) != (v_out is None):
+        raise ValueError("v and v_out go together")
+    if v is not None:
+        v, v_out = _rows3(v, "v"), _rows3(v_out, "v_out")
+    B, Hq, D = q.shape
+    Hk = k.shape[1]
+    tensors = [q, k, cos, sin, q_out, k_out] + ([v, v_out] if v is not None else [])
+    if len({t.dtype for t in tensors}) != 1:
+        raise ValueError("rope_kv_append: every tensor must have one dtype")
+    if q_out.shape != q.shape or k_out.shape != k.shape or k.shape[0] != B or k.shape[2] != D \
+            or (v is not None and (v.shape != k.shape or v_out.shape != k.shape)):
+        raise ValueError("rope_kv_append: shape mismatch")
+    cs = [c.reshape(-1, c.shape[-1]) for c in (cos, sin)]
+    if cs[0].shape != cs[1].shape or cs[0].shape[-1] != D or cs[0].shape[0] not in (1, B) \
+            or cs[0].stride(-1) != 1 or cs[0].stride(0) != cs[1].stride(0):
+        raise ValueError("rope_kv_append: cos/sin must be (B or 1, D) rows of the head dim")
+    cs_sb = cs[0].stride(0) if cs[0].shape[0] == B and B > 1 else 0
+    z = (None, 0, 0, None, 0, 0)
+    vv = (_p(v), v.stride(0), v.stride(1), _p(v_out), v_out.stride(0), v_out.stride(1)) \
+        if v is not None else z
+    with torch.cuda.device(q.device):
+        rc = _lib.load().fc_rope_kv_append(
+            _p(q), q.stride(0), q.stride(1), _p(q_out), q_out.stride(0), q_out.stride(1), Hq,
+            _p(k), k.stride(0), k.stride(1), _p(k_out), k_out.stride(0), k_out.stride(1),
+            *vv, Hk, _p(cs[0]), _p(cs[1]), cs_sb, dtype_code(q), B, D, _stream(q.device))
+    _lib.check(rc, "rope_kv_append")
+
+
 def selftest_bounded_wait(status: torch.Tensor, epoch: int) -> None:
     """Launch the bounded-wait self-test on status's device: it gives up after
     the kernels' wait limit and records `epoch` in status (int32, 1 element)."""

@@ -330,6 +330,41 @@ class _CodecStream:
         return bool(self._scale_err is not None and int(self._scale_err.item()) != 0)
 
 
+def append_rotary(key_stream, value_stream, q, k, v, cos, sin):
+    """One decode token of one layer: rotary embedding of q and k and the
+    append of (rotated k, v) to the layer's streams in one launch
+    (fc_rope_kv_append writes straight into the raw-tail slot); a block that
+    this token completes is archived as ``append`` would archive it.
+
+    q (B,Hq,1,D), k and v (B,Hk,1,D) before the rotation; cos/sin (B or 1,
+    [1,] D) in the same dtype (rotate-half form, transformers'
+    ``apply_rotary_pos_emb``).  Returns the rotated q (B,Hq,1,D); the streams
+    end up bit-identical to ``rope`` followed by two ``append`` calls."""
+    ks, vs = key_stream, value_stream
+    K.require_cuda(q, k, v)
+    for st, x in ((ks, k), (vs, v)):
+        if st.meta is None:
+            st.meta = (x.shape[0], x.shape[1], x.shape[-1], x.element_size())
+            st.dtype = x.dtype
+    if k.dtype != ks.dtype or v.dtype != vs.dtype or ks._raw_len != vs._raw_len \
+            or ks.block_size != vs.block_size:
+        raise ValueError("append_rotary: the key and value streams must match the tokens "
+                         "and each other")
+    ks._ensure_raw(k)
+    vs._ensure_raw(v)
+    t = ks._raw_len
+    q_out = torch.empty_like(q)
+    K.rope_kv_append(q, k, v, cos, sin, q_out, ks._raw_buf[:, :, t], vs._raw_buf[:, :, t])
+    ks._raw_len = vs._raw_len = t + 1
+    if t + 1 == ks.block_size:
+        for st in (ks, vs):
+            st._grow(st.n_blocks + 1, st._raw_buf)
+            st._archive_from(st._raw_buf, 1)
+            st.n_archived += st.block_size
+            st._raw_len = 0
+    return q_out
+
+
 class CodecKVCache:
     """Codec KV cache, multi-layer, duck-typed as a HuggingFace Cache
     (flashcodec/cache.py:328-440).

@@ -8,6 +8,12 @@ the layer's codec streams and computes attention with one
 ``codec_decode_attention`` launch (fc_decode_attn): the (S, D) view is never
 reconstructed during decode.
 
+The rotary embedding and the append run as one fc_rope_kv_append launch
+once the model's rotary function has been checked, on its first decode step,
+to give bit-identical results to the fused kernel (``_fused_rope``); the
+reference runs them as separate torch ops and appends
+(flashcodec/patch_attention.py:82-94).
+
 Taken when (anything else runs the original forward, silently, as in
 flashcodec/patch_attention.py:51-63):
 
@@ -26,7 +32,11 @@ import importlib
 
 import torch
 
+from . import _kernels as K
+from .cache import append_rotary
+
 _ROPE = {}
+_ROPE_EXACT = {}       # (rotary function, dtype) -> the fused kernel matches it bitwise
 
 
 def _rope_fn(module):
@@ -41,6 +51,32 @@ def _rope_fn(module):
             fn = None
         _ROPE[name] = fn or False
     return fn or None
+
+
+def _fused_rope(rope, q, k, v, cos, sin, key_stream):
+    """Whether this step's rotary embedding and append may run as one
+    fc_rope_kv_append launch.  The first time a model's rotary function is
+    seen, the kernel's rotation is compared bitwise with the function's
+    output on that step's q and k (the step itself then takes the unfused
+    path); functions that differ (partial rotary, interleaved pairs, another
+    rounding) keep the unfused path for good."""
+    D = q.shape[-1]
+    if not (q.dtype == k.dtype == v.dtype == cos.dtype == sin.dtype
+            and q.dtype in (torch.float32, torch.bfloat16, torch.float16)
+            and (key_stream.dtype is None or key_stream.dtype == k.dtype)
+            and D % 2 == 0 and cos.shape == sin.shape and cos.shape[-1] == D
+            and cos.numel() // D in (1, q.shape[0])):
+        return False
+    key = (rope, q.dtype)
+    ok = _ROPE_EXACT.get(key)
+    if ok is None:
+        q_ref, k_ref = rope(q, k, cos, sin)
+        q_f, k_f = torch.empty_like(q_ref), torch.empty_like(k_ref)
+        K.rope_kv_append(q, k, None, cos, sin, q_f, k_f)
+        ok = bool(torch.equal(q_f, q_ref) and torch.equal(k_f, k_ref))
+        _ROPE_EXACT[key] = ok
+        return False
+    return ok
 
 
 def _codec_layer(module, past_key_values):
@@ -83,7 +119,7 @@ def _decode_forward(module, orig, hidden_states, position_embeddings=None,
     if hasattr(module, "k_norm"):
         k = module.k_norm(k)
     cos, sin = position_embeddings
-    q, k = rope(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+    q, k = q.transpose(1, 2), k.transpose(1, 2)
 
     if not layer.is_initialized:
         layer.lazy_initialization(k, v)
@@ -92,8 +128,12 @@ def _decode_forward(module, orig, hidden_states, position_embeddings=None,
         if st._rec is not None:
             st.discard_view()
     layer.keys = layer.values = None
-    ks.append(k)
-    vs.append(v)
+    if _fused_rope(rope, q, k, v, cos, sin, ks):
+        q = append_rotary(ks, vs, q, k, v, cos, sin)
+    else:
+        q, k = rope(q, k, cos, sin)
+        ks.append(k)
+        vs.append(v)
     from .attention import codec_decode_attention
     out = codec_decode_attention(q, ks, vs, scale=module.scaling)
     out = out.transpose(1, 2).reshape(*lead, -1)

@@ -265,6 +265,27 @@ FC_API int fc_gather_batch(const void *src, int64_t B_src, void *dst, int64_t B,
                            int64_t slab_bytes, int64_t src_sb, int64_t src_sh,
                            int64_t dst_sb, int64_t dst_sh, const int64_t *idx, void *stream);
 
+/* Decode-step rotary embedding fused with the cache append: replaces, for one
+ * new token, transformers' apply_rotary_pos_emb on q and k followed by the two
+ * stream appends (flashcodec/patch_attention.py:82-94, cache.py:143-159).
+ * q (B, Hq, D) -> q_out; k (B, Hk, D) -> rotated into k_out; v (B, Hk, D)
+ * copied unchanged into v_out (v and v_out may both be null: rotation only).
+ * x_out = x*cos + rotate_half(x)*sin with rotate_half(x) = [-x2, x1] over the
+ * two halves of D; cos and sin are (B, D) rows (batch stride cs_sb).  All
+ * tensors have element type `dtype` (fp32, bf16 or fp16) and unit stride
+ * along D; strides are in elements.  Each product and the sum are rounded to
+ * `dtype` as torch's elementwise ops round them, so the result is
+ * bit-identical to the unfused expression.  Outputs must not alias inputs;
+ * D must be even. */
+FC_API int fc_rope_kv_append(const void *q, int64_t q_sb, int64_t q_sh, void *q_out,
+                             int64_t qo_sb, int64_t qo_sh, int64_t Hq,
+                             const void *k, int64_t k_sb, int64_t k_sh, void *k_out,
+                             int64_t ko_sb, int64_t ko_sh,
+                             const void *v, int64_t v_sb, int64_t v_sh, void *v_out,
+                             int64_t vo_sb, int64_t vo_sh, int64_t Hk,
+                             const void *cos, const void *sin, int64_t cs_sb,
+                             int dtype, int64_t B, int64_t D, void *stream);
+
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
  * AUTO uses the tcgen05 int8 tensor-core kernel whenever the archive allows
  * it (contiguous (B, Hk, cap, s, 128) int8 codes, block size 8 with

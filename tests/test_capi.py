@@ -125,3 +125,23 @@ def test_new_entry_points_validate_on_the_host(lib):
     # self-test: null status, epoch <= 0
     assert lib.fc_selftest_bounded_wait(None, 1, None) == _lib.FC_EINVAL
     assert lib.fc_selftest_bounded_wait(d, 0, None) == _lib.FC_EINVAL
+
+
+def test_rope_kv_append_validates_on_the_host(lib):
+    """fc_rope_kv_append refuses odd head dims, integer dtypes, a v without
+    v_out and aliased outputs before any CUDA call; empty work is a no-op."""
+    from flashcodec_b200 import _lib
+    P = ctypes.c_void_p
+    q, qo, k, ko, v, vo, c, s = (P(0x1000 * (i + 1)) for i in range(8))
+
+    def call(B=2, D=64, dt=_lib.FC_BF16, q_out=qo, v_=v, v_out=vo, Hq=4, Hk=2):
+        return lib.fc_rope_kv_append(q, 256, 64, q_out, 256, 64, Hq, k, 128, 64, ko, 128, 64,
+                                     v_, 128, 64, v_out, 128, 64, Hk, c, s, 64, dt, B, D, None)
+
+    assert call(D=63) == _lib.FC_EINVAL
+    assert b"odd" in lib.fc_last_error_string()
+    assert call(dt=_lib.FC_I8) == _lib.FC_EINVAL
+    assert call(v_out=None) == _lib.FC_EINVAL
+    assert call(q_out=q) == _lib.FC_EINVAL
+    assert call(B=-1) == _lib.FC_EINVAL
+    assert call(B=0) == _lib.FC_OK

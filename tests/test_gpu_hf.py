@@ -187,6 +187,13 @@ def test_i_materialization_free_generation(count_decode):
     assert fc.codec_attention_stats(model) == n_layers
     assert torch.equal(gen(model), ref)
     assert len(count_decode) == n_layers * (NEW - 1)
+    # the model's rotary function was checked once and the fused
+    # rotary + append kernel took over the later decode steps
+    from transformers.models.llama import modeling_llama
+
+    from flashcodec_b200 import patch_attention
+    assert patch_attention._ROPE_EXACT[(modeling_llama.apply_rotary_pos_emb,
+                                        torch.float32)] is True
     cache = model._flashcodec["caches"][-1]
     assert cache.get_seq_length() == PROMPT_LEN + NEW - 1
     for layer in cache.layers:
