@@ -350,7 +350,7 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
-CODEC_WORKLOADS = ("archive", "read", "png-encode", "png-decode", "stream")
+CODEC_WORKLOADS = ("archive", "read", "png-encode", "png-decode", "stream", "decode-step")
 
 
 def run_codec(args):
@@ -493,6 +493,99 @@ def run_stream(args):
     print(json.dumps(line), flush=True)
 
 
+def run_decode_step(args):
+    """--workload decode-step: the attention half of one model decode step on
+    config 2 (36 layers, B=16, Hq=32, Hkv=8, D=128, 32768 archived tokens,
+    jpeg r=8 K=4 int8): per layer the rotary embedding of the new q and k,
+    the append of k and v (archiving each block as it completes) and the
+    archive decode attention.  Fused = fc_rope_kv_append + fc_decode_attn
+    (what the patched attention module runs); unfused = transformers'
+    apply_rotary_pos_emb + two stream appends + fc_decode_attn (the
+    reference's sequence, flashcodec/patch_attention.py:82-98, on this
+    package's kernels).  CUDA events around each step, host launch overhead
+    included; the archives are pre-grown so no capacity doubling lands in the
+    timed steps."""
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as K
+    from flashcodec_b200.cache import append_rotary
+    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = dict(CFG2, layers=args.layers or CFG2["layers"], B=args.batch or CFG2["B"])
+    layers = build_layers(cfg, 0, dev)
+    B, Hq, Hk, D = cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"]
+    steps = args.steps
+    for ks, vs, _ in layers:
+        for st in (ks, vs):
+            st._grow(st.n_blocks + 2 * (steps + args.warmup) // cfg["r"] + 2, st._raw_buf)
+    g = torch.Generator(device=dev).manual_seed(11)
+
+    def hf(h):
+        return torch.randn(B, 1, h, D, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+
+    toks = [(hf(Hq), hf(Hk), hf(Hk)) for _ in layers]
+    pos = torch.arange(B, device=dev, dtype=torch.float32)[:, None] + cfg["S"]
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float32) / D))
+    ang = torch.cat([pos * inv, pos * inv], dim=-1)[:, None, :]
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+
+    def fused():
+        for (ks, vs, _), (q, k, v) in zip(layers, toks):
+            qr = append_rotary(ks, vs, q, k, v, cos, sin)
+            fc.codec_decode_attention(qr, ks, vs)
+
+    def unfused():
+        for (ks, vs, _), (q, k, v) in zip(layers, toks):
+            qr, kr = apply_rotary_pos_emb(q, k, cos, sin)
+            ks.append(kr)
+            vs.append(v)
+            fc.codec_decode_attention(qr, ks, vs)
+
+    def timed(fn):
+        stream = torch.cuda.current_stream(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        torch.cuda.synchronize()
+        for a, b in ev:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in ev)
+
+    for _ in range(args.warmup):
+        fused()
+        unfused()
+    sampler = ClockSampler([0])
+    sampler.start()
+    time.sleep(0.5)
+    t0 = time.time()
+    ms_f = timed(fused)
+    ms_u = timed(unfused)
+    clocks = sampler.stop(t0, time.time())
+    assert K.attn_status(dev) == 0, "a bounded wait in the attention kernel gave up"
+    L = len(layers)
+    per_attn = codec_attn_bytes(cfg, layers[0][0].n_blocks)
+    line = {"metric": "decode-step tokens/s (rotary + append + archive decode attention, "
+                      f"{L} layers)",
+            "value": B / (ms_f * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms_f, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 2 decode step, attention side: rotary embedding of "
+                                   "q/k, KV append (archive on block completion), decode "
+                                   "attention, per layer",
+                       "layers": L, "batch": B, "Hq": Hq, "Hkv": Hk, "head_dim": D,
+                       "context": cfg["S"], "codec": "jpeg r=8 K=4 int8, fp32 scales",
+                       "l2": "no flush: the archives read each step (~20 GB) are >100x L2"},
+            "unfused": {"ms_per_step": ms_u, "tokens_per_s": B / (ms_u * 1e-3),
+                        "sequence": "apply_rotary_pos_emb + 2 appends + attention"},
+            "speedup_vs_unfused": ms_u / ms_f,
+            "attention_bytes_per_step": per_attn * L,
+            "gpu_launches": steps * L * 2 + steps * L * 2 // cfg["r"],
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def workload_config(cfg, world):
     name = ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K decode-attention "
             "launch per layer over the int8 DCT archive") if cfg["config"] == 2 else (
@@ -543,6 +636,8 @@ def main():
             raise SystemExit("--impl reference times the attention workload")
         if args.workload == "stream":
             run_stream(args)
+        elif args.workload == "decode-step":
+            run_decode_step(args)
         else:
             run_codec(args)
         return
