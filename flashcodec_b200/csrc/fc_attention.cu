@@ -187,28 +187,126 @@ attn_kernel(AttnArgs a) {
             }
     __syncthreads();
 
-    // ---- dot products of one row with every head's q, reduced over the row's lanes
-    auto row_dot_typed = [&](const RT *p, bool valid, float part[GT]) {
+    // ---- row loaders: the VEC channels of each chunk this lane covers, as fp32
+    // (zeros past D)
+    auto load_typed = [&](const RT *p, float x[NCH][VEC]) {
 #pragma unroll
-        for (int g = 0; g < GT; g++) part[g] = 0.0f;
-        if (valid) {
+        for (int c = 0; c < NCH; c++) {
+            const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
+            if (d0 < a.D) {
+                load_vec_f32<RT, VEC>(p + d0, x[c]);
+            } else {
 #pragma unroll
-            for (int c = 0; c < NCH; c++) {
-                const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
-                if (d0 < a.D) {
-                    float x[VEC];
-                    load_vec_f32<RT, VEC>(p + d0, x);
+                for (int v = 0; v < VEC; v++) x[c][v] = 0.0f;
+            }
+        }
+    };
+    // a row of run-time element type (png anchors), `off` elements from base
+    auto load_any = [&](const void *base, int64_t off, int dt, float x[NCH][VEC]) {
 #pragma unroll
-                    for (int g = 0; g < GT; g++)
+        for (int c = 0; c < NCH; c++) {
+            const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
+            if (d0 < a.D) {
+                switch (dt) {
+                    case FC_F32:
+                        load_vec_f32<float, VEC>(static_cast<const float *>(base) + off + d0, x[c]);
+                        break;
+                    case FC_BF16:
+                        load_vec_f32<__nv_bfloat16, VEC>(
+                            static_cast<const __nv_bfloat16 *>(base) + off + d0, x[c]);
+                        break;
+                    case FC_F16:
+                        load_vec_f32<__half, VEC>(static_cast<const __half *>(base) + off + d0, x[c]);
+                        break;
+                    default:
+                        load_vec_f32<int8_t, VEC>(static_cast<const int8_t *>(base) + off + d0, x[c]);
+                        break;
+                }
+            } else {
 #pragma unroll
-                        for (int v = 0; v < VEC; v++) part[g] = fmaf(qr[g][c][v], x[v], part[g]);
+                for (int v = 0; v < VEC; v++) x[c][v] = 0.0f;
+            }
+        }
+    };
+    // stored row `row` of this split read in place: png row 0 from the anchors,
+    // every other row from the row tensor (rows 1..r-1 = deltas 0..r-2)
+    auto load_direct = [&](const RT *rbase, const void *anc, int64_t sn, int64_t sj, int row,
+                           float x[NCH][VEC]) {
+        const int blk = row / s, j = row - blk * s;
+        if (anc && j == 0)
+            load_any(anc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn, a.anc_dtype, x);
+        else
+            load_typed(rbase + (int64_t)blk * sn + (int64_t)(j - (anc ? 1 : 0)) * sj, x);
+    };
+
+    // ---- scores of U rows per lane group at a time.  The loads of all U rows
+    // are issued before any arithmetic (U rows of memory in flight per warp).
+    // The U x GT partial dot products of each lane are then reduced over the
+    // row's lanes by one transposing butterfly: at each level a lane keeps half
+    // of its partials and adds the other lane's copy of that half, so a level
+    // costs half as many shuffles as the one before instead of GT per row;
+    // afterwards lane li holds the complete sums of entries [off, off + held)
+    // of the list (u, g) -> u * GT + g.
+    // U: about 32 loaded values per lane (8 rows of fp32, 4 of bf16, 2 of int8),
+    // at most 32 partials per lane
+    constexpr int UL = (32 / (NCH * VEC)) < 1 ? 1 : (32 / (NCH * VEC));
+    constexpr int U = (UL > 8 ? 8 : UL) * GT > 32 ? 32 / GT : (UL > 8 ? 8 : UL);
+    constexpr int M = U * GT;
+    auto dots = [&](float x[U][NCH][VEC], float v[M]) {
+#pragma unroll
+        for (int u = 0; u < U; u++)
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                float acc_d = 0.0f;
+#pragma unroll
+                for (int c = 0; c < NCH; c++)
+#pragma unroll
+                    for (int e = 0; e < VEC; e++) acc_d = fmaf(qr[g][c][e], x[u][c][e], acc_d);
+                v[u * GT + g] = acc_d;
+            }
+    };
+    auto butterfly = [&](float v[M]) {
+        int off = 0;
+#pragma unroll
+        for (int lv = 0; lv < 5; lv++) {
+            if (lv < a.lprl) {
+                const int o = lpr >> (lv + 1);
+                const int m = M >> lv;
+                if (m > 1) {
+                    const bool upper = (li & o) != 0;
+#pragma unroll
+                    for (int i = 0; i < M / 2; i++) {
+                        if (i < m / 2) {
+                            const float send = upper ? v[i] : v[i + m / 2];
+                            const float keep = upper ? v[i + m / 2] : v[i];
+                            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                        }
+                    }
+                    if (upper) off += m / 2;
+                } else {
+                    v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
                 }
             }
         }
+        return off;
+    };
+    // entries a lane holds after the butterfly, and whether it writes them
+    // (when the row has more lanes than entries, lanes repeat; the first writes)
+    const int held = max(M >> a.lprl, 1);
+    const bool writer = lpr <= M || (li & (lpr / M - 1)) == 0;
+    auto store_scores = [&](const float v[M], int off, int base, int limit, int gbase) {
+        if (!writer) return;
 #pragma unroll
-        for (int g = 0; g < GT; g++)
-            for (int off = lpr >> 1; off > 0; off >>= 1)
-                part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+        for (int i = 0; i < M; i++) {
+            if (i < held) {
+                const int e = off + i, u = e / GT, g = e % GT;
+                const int row = base + u * rows_per_pass + warp * rpw + lr;
+                if (row < limit) {
+                    const int grow = gbase + row;
+                    ssc[grow * GT + g] = v[i] * sks[grow];
+                }
+            }
+        }
     };
     auto row_dot_raw = [&](const void *base, int64_t off, bool valid, float part[GT], int dt) {
 #pragma unroll
@@ -241,38 +339,47 @@ attn_kernel(AttnArgs a) {
             if (__syncthreads_or(!ok)) { drain(t); return; }
             const RT *tile = reinterpret_cast<const RT *>(ring + (t % kStages) * kStageBytes);
             const int trows = min(a.tb, nb - t * a.tb) * s;
-            for (int base = 0; base < trows; base += rows_per_pass) {
-                const int row = base + warp * rpw + lr;
-                const bool valid = row < trows;
-                float part[GT];
-                row_dot_typed(tile + (int64_t)row * row_elems, valid, part);
-                if (valid && li == 0) {
-                    const int grow = t * a.tb * s + row;
-                    const float ks = sks[grow];
+            for (int base = 0; base < trows; base += rows_per_pass * U) {
+                float x[U][NCH][VEC];
 #pragma unroll
-                    for (int g = 0; g < GT; g++) ssc[grow * GT + g] = part[g] * ks;
+                for (int u = 0; u < U; u++) {
+                    const int row = base + u * rows_per_pass + warp * rpw + lr;
+                    if (row < trows) {
+                        load_typed(tile + (int64_t)row * row_elems, x[u]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < NCH; c++)
+#pragma unroll
+                            for (int e = 0; e < VEC; e++) x[u][c][e] = 0.0f;
+                    }
                 }
+                float v[M];
+                dots(x, v);
+                const int off = butterfly(v);
+                store_scores(v, off, base, trows, t * a.tb * s);
             }
             __syncthreads();
             if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
     } else {
-        for (int base = 0; base < krows_total; base += rows_per_pass) {
-            const int row = base + warp * rpw + lr;
-            const bool valid = row < krows_total;
-            const int blk = valid ? row / s : 0, j = valid ? row % s : 0;
-            float part[GT];
-            if (a.kanc && j == 0)
-                row_dot_raw(a.kanc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn, valid, part,
-                            a.anc_dtype);
-            else
-                row_dot_typed(kbase + (int64_t)blk * a.k_sn + (int64_t)(j - (a.kanc ? 1 : 0)) * a.k_sj,
-                              valid, part);
-            if (valid && li == 0) {
-                const float ks = sks[row];
+        for (int base = 0; base < krows_total; base += rows_per_pass * U) {
+            float x[U][NCH][VEC];
 #pragma unroll
-                for (int g = 0; g < GT; g++) ssc[row * GT + g] = part[g] * ks;
+            for (int u = 0; u < U; u++) {
+                const int row = base + u * rows_per_pass + warp * rpw + lr;
+                if (row < krows_total) {
+                    load_direct(kbase, a.kanc, a.k_sn, a.k_sj, row, x[u]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < NCH; c++)
+#pragma unroll
+                        for (int e = 0; e < VEC; e++) x[u][c][e] = 0.0f;
+                }
             }
+            float v[M];
+            dots(x, v);
+            const int off = butterfly(v);
+            store_scores(v, off, base, krows_total, 0);
         }
     }
     // raw tail rows
@@ -359,24 +466,6 @@ attn_kernel(AttnArgs a) {
         }
     };
 
-    // one row of run-time dtype (png anchors)
-    auto accum_any = [&](const void *base, int64_t off, int dt, int wrow) {
-        float w[GT];
-#pragma unroll
-        for (int g = 0; g < GT; g++) w[g] = ssc[wrow * GT + g];
-#pragma unroll
-        for (int c = 0; c < NCH; c++)
-#pragma unroll
-            for (int v = 0; v < VEC; v++) {
-                const int64_t d = ((int64_t)c * lpr + li) * VEC + v;
-                if (d < a.D) {
-                    const float x = load_as_f32(base, off + d, dt);
-#pragma unroll
-                    for (int g = 0; g < GT; g++) acc[g][c][v] = fmaf(w[g], x, acc[g][c][v]);
-                }
-            }
-    };
-
     if (BULK) {
         for (int t = ntiles; t < ttot; t++) {
             const bool ok = mbar_wait_bounded(bars + (t % kStages), (t / kStages) & 1, a.status,
@@ -393,16 +482,34 @@ attn_kernel(AttnArgs a) {
             if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
     } else {
-        for (int base = 0; base < krows_total; base += rows_per_pass) {
-            const int row = base + warp * rpw + lr;
-            if (row < krows_total) {
-                const int blk = row / s, j = row % s;
-                if (a.vanc && j == 0)
-                    accum_any(a.vanc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn, a.anc_dtype, row);
-                else
-                    accum_typed(vbase + (int64_t)blk * a.v_sn + (int64_t)(j - (a.vanc ? 1 : 0)) * a.v_sj,
-                                row);
+        // U rows per lane group at a time, loads first (as in pass 1)
+        for (int base = 0; base < krows_total; base += rows_per_pass * U) {
+            float x[U][NCH][VEC];
+            float w[U][GT];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int row = base + u * rows_per_pass + warp * rpw + lr;
+                if (row < krows_total) {
+                    load_direct(vbase, a.vanc, a.v_sn, a.v_sj, row, x[u]);
+#pragma unroll
+                    for (int g = 0; g < GT; g++) w[u][g] = ssc[row * GT + g];
+                } else {
+#pragma unroll
+                    for (int c = 0; c < NCH; c++)
+#pragma unroll
+                        for (int e = 0; e < VEC; e++) x[u][c][e] = 0.0f;
+#pragma unroll
+                    for (int g = 0; g < GT; g++) w[u][g] = 0.0f;
+                }
             }
+#pragma unroll
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int g = 0; g < GT; g++)
+#pragma unroll
+                    for (int c = 0; c < NCH; c++)
+#pragma unroll
+                        for (int e = 0; e < VEC; e++) acc[g][c][e] = fmaf(w[u][g], x[u][c][e], acc[g][c][e]);
         }
     }
     for (int base = 0; base < nraw; base += rows_per_pass) {
@@ -765,7 +872,14 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     int vm = n_blocks > 0 ? pick_vec_mode(D, es, k_rows, v_rows, k_sb, k_sh, k_sn, k_sj,
                                           v_sb, v_sh, v_sn, v_sj, s)
                           : 0;
-    if (png) vm = std::min(vm, 1);  // rows of a block are not one contiguous run
+    if (png) {
+        vm = std::min(vm, 1);  // rows of a block are not one contiguous run
+        // anchors are read with the deltas' vector width (16 / es elements)
+        const int vec = 16 / es, aes = dtype_size(png->dtype);
+        if (vm == 1 && !(aligned(png->k, vec * aes) && aligned(png->v, vec * aes) &&
+                         png->sb % vec == 0 && png->sh % vec == 0 && png->sn % vec == 0))
+            vm = 0;
+    }
     Plan p = make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm);
     if (p.smem > 200 * 1024) { set_error("decode_attn: shared memory plan too large"); return FC_ENOTSUP; }
     if (!workspace || workspace_bytes < p.ws) {

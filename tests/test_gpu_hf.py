@@ -69,7 +69,8 @@ def test_a_explicit_cache():
     assert cache.get_seq_length() == PROMPT_LEN + NEW - 1
     assert cache._seen_tokens == PROMPT_LEN + NEW - 1
     assert len(cache.layers) == model.config.num_hidden_layers
-    raw = (PROMPT_LEN + NEW) * 1 * 2 * 16 * 4 * 2
+    # raw fp32 K+V of every layer: tokens x batch 1 x (2 layers x 2 heads x 16 dims) x 4 B x 2
+    raw = (PROMPT_LEN + NEW) * 1 * 2 * 32 * 4 * 2
     assert cache.storage_bytes() < 0.5 * raw
 
 
@@ -107,7 +108,7 @@ def test_d_long_generation(mode, kw, bound):
     assert cache.get_seq_length() == kv_len
     ks = cache.layers[0]._key_stream
     assert ks.n_archived > 0 and kv_len - ks.n_archived < 8
-    raw = kv_len * 1 * 2 * 16 * 4 * 2
+    raw = kv_len * 1 * 2 * 32 * 4 * 2          # both layers, as in test_a
     assert cache.storage_bytes() < bound * raw
 
 
