@@ -252,17 +252,29 @@ attn_kernel(AttnArgs a) {
     constexpr int UL = (32 / (NCH * VEC)) < 1 ? 1 : (32 / (NCH * VEC));
     constexpr int U = (UL > 8 ? 8 : UL) * GT > 32 ? 32 / GT : (UL > 8 ? 8 : UL);
     constexpr int M = U * GT;
+    // even and odd channels accumulate in the two halves of a paired fp32 FMA
     auto dots = [&](float x[U][NCH][VEC], float v[M]) {
 #pragma unroll
         for (int u = 0; u < U; u++)
 #pragma unroll
             for (int g = 0; g < GT; g++) {
-                float acc_d = 0.0f;
+                if constexpr (VEC % 2 == 0) {
+                    float2 acc2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int c = 0; c < NCH; c++)
+                    for (int c = 0; c < NCH; c++)
 #pragma unroll
-                    for (int e = 0; e < VEC; e++) acc_d = fmaf(qr[g][c][e], x[u][c][e], acc_d);
-                v[u * GT + g] = acc_d;
+                        for (int e = 0; e < VEC; e += 2)
+                            acc2 = __ffma2_rn(make_float2(qr[g][c][e], qr[g][c][e + 1]),
+                                              make_float2(x[u][c][e], x[u][c][e + 1]), acc2);
+                    v[u * GT + g] = acc2.x + acc2.y;
+                } else {
+                    float acc_d = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < NCH; c++)
+#pragma unroll
+                        for (int e = 0; e < VEC; e++) acc_d = fmaf(qr[g][c][e], x[u][c][e], acc_d);
+                    v[u * GT + g] = acc_d;
+                }
             }
     };
     auto butterfly = [&](float v[M]) {
@@ -361,6 +373,44 @@ attn_kernel(AttnArgs a) {
             __syncthreads();
             if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
+    } else if (s % U == 0) {
+        // block-major: each lane group takes whole blocks, U of its rows at a
+        // time (a png block's anchor is row 0 of its first batch)
+        for (int blk0 = 0; blk0 < nb; blk0 += rows_per_pass) {
+            const int blk = blk0 + warp * rpw + lr;
+            const bool bvalid = blk < nb;
+            const RT *rb = kbase + (int64_t)blk * a.k_sn - (a.kanc ? a.k_sj : 0);
+            for (int j0 = 0; j0 < s; j0 += U) {
+                float x[U][NCH][VEC];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    if (!bvalid) {
+#pragma unroll
+                        for (int c = 0; c < NCH; c++)
+#pragma unroll
+                            for (int e = 0; e < VEC; e++) x[u][c][e] = 0.0f;
+                    } else if (u == 0 && j0 == 0 && a.kanc) {
+                        load_any(a.kanc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn,
+                                 a.anc_dtype, x[u]);
+                    } else {
+                        load_typed(rb + (int64_t)(j0 + u) * a.k_sj, x[u]);
+                    }
+                }
+                float v[M];
+                dots(x, v);
+                const int off = butterfly(v);
+                if (writer && bvalid) {
+#pragma unroll
+                    for (int i = 0; i < M; i++) {
+                        if (i < held) {
+                            const int e = off + i;
+                            const int row = blk * s + j0 + e / GT;
+                            ssc[row * GT + e % GT] = v[i] * sks[row];
+                        }
+                    }
+                }
+            }
+        }
     } else {
         for (int base = 0; base < krows_total; base += rows_per_pass * U) {
             float x[U][NCH][VEC];
@@ -448,6 +498,21 @@ attn_kernel(AttnArgs a) {
 #pragma unroll
             for (int v = 0; v < VEC; v++) acc[g][c][v] = 0.0f;
 
+    // acc[g][c][:] += w * x[:], channel pairs in one paired fp32 FMA
+    auto axpy = [&](float w, const float x[VEC], float y[VEC]) {
+        if constexpr (VEC % 2 == 0) {
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+                const float2 r2 = __ffma2_rn(make_float2(w, w), make_float2(x[e], x[e + 1]),
+                                             make_float2(y[e], y[e + 1]));
+                y[e] = r2.x;
+                y[e + 1] = r2.y;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < VEC; e++) y[e] = fmaf(w, x[e], y[e]);
+        }
+    };
     auto accum_typed = [&](const RT *p, int wrow) {
         float w[GT];
 #pragma unroll
@@ -459,9 +524,7 @@ attn_kernel(AttnArgs a) {
                 float x[VEC];
                 load_vec_f32<RT, VEC>(p + d0, x);
 #pragma unroll
-                for (int g = 0; g < GT; g++)
-#pragma unroll
-                    for (int v = 0; v < VEC; v++) acc[g][c][v] = fmaf(w[g], x[v], acc[g][c][v]);
+                for (int g = 0; g < GT; g++) axpy(w[g], x, acc[g][c]);
             }
         }
     };
@@ -480,6 +543,43 @@ attn_kernel(AttnArgs a) {
             }
             __syncthreads();
             if (tid == 0 && t + kStages < ttot) issue(issued++);
+        }
+    } else if (s % U == 0) {
+        // block-major, as in pass 1
+        for (int blk0 = 0; blk0 < nb; blk0 += rows_per_pass) {
+            const int blk = blk0 + warp * rpw + lr;
+            const bool bvalid = blk < nb;
+            const RT *rb = vbase + (int64_t)blk * a.v_sn - (a.vanc ? a.v_sj : 0);
+            for (int j0 = 0; j0 < s; j0 += U) {
+                float x[U][NCH][VEC];
+                float w[U][GT];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    if (!bvalid) {
+#pragma unroll
+                        for (int c = 0; c < NCH; c++)
+#pragma unroll
+                            for (int e = 0; e < VEC; e++) x[u][c][e] = 0.0f;
+#pragma unroll
+                        for (int g = 0; g < GT; g++) w[u][g] = 0.0f;
+                    } else {
+                        if (u == 0 && j0 == 0 && a.vanc)
+                            load_any(a.vanc, b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn,
+                                     a.anc_dtype, x[u]);
+                        else
+                            load_typed(rb + (int64_t)(j0 + u) * a.v_sj, x[u]);
+                        const int row = blk * s + j0 + u;
+#pragma unroll
+                        for (int g = 0; g < GT; g++) w[u][g] = ssc[row * GT + g];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++)
+#pragma unroll
+                    for (int g = 0; g < GT; g++)
+#pragma unroll
+                        for (int c = 0; c < NCH; c++) axpy(w[u][g], x[u][c], acc[g][c]);
+            }
         }
     } else {
         // U rows per lane group at a time, loads first (as in pass 1)
@@ -507,9 +607,7 @@ attn_kernel(AttnArgs a) {
 #pragma unroll
                 for (int g = 0; g < GT; g++)
 #pragma unroll
-                    for (int c = 0; c < NCH; c++)
-#pragma unroll
-                        for (int e = 0; e < VEC; e++) acc[g][c][e] = fmaf(w[u][g], x[u][c][e], acc[g][c][e]);
+                    for (int c = 0; c < NCH; c++) axpy(w[u][g], x[u][c], acc[g][c]);
         }
     }
     for (int base = 0; base < nraw; base += rows_per_pass) {
