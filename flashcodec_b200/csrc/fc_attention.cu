@@ -758,7 +758,9 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
         int64_t ns = (want_ctas + units - 1) / units;
         ns = std::max<int64_t>(1, std::min<int64_t>(ns, (n + kMinChunk - 1) / kMinChunk));
         int64_t chunk = (n + ns - 1) / ns;
-        chunk = std::min<int64_t>(chunk, kTargetChunk);
+        // the bulk-ring variant holds a 32 KB ring besides the per-block
+        // arrays: half-size chunks keep it at 4 CTAs per SM
+        chunk = std::min<int64_t>(chunk, vec_mode == 2 ? kTargetChunk / 2 : kTargetChunk);
         ns = (n + chunk - 1) / chunk;
         chunk = (n + ns - 1) / ns;
         p.n_split = (int)ns;
