@@ -383,8 +383,13 @@ jpeg_decode_d128_kernel(DecArgs a) {
             if (a.scales) {
                 // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
                 const float sc = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
-#pragma unroll
-                for (int v = 0; v < 4; v++) c[j][v] = __fmul_rn(c[j][v], sc);
+                const float2 s2 = make_float2(sc, sc);
+                const float2 p01 = __fmul2_rn(make_float2(c[j][0], c[j][1]), s2);
+                const float2 p23 = __fmul2_rn(make_float2(c[j][2], c[j][3]), s2);
+                c[j][0] = p01.x;
+                c[j][1] = p01.y;
+                c[j][2] = p23.x;
+                c[j][3] = p23.y;
             }
         }
     }
@@ -393,17 +398,19 @@ jpeg_decode_d128_kernel(DecArgs a) {
 #pragma unroll
     for (int i = 0; i < R; i++) {
         if (i >= nrow) break;
-        float o[4];
-#pragma unroll
-        for (int v = 0; v < 4; v++) o[v] = 0.0f;
+        // sequential chains over the coefficients, channel pairs in one
+        // paired fp32 FMA (each half an ordinary fma.rn)
+        float2 o01 = make_float2(0.0f, 0.0f), o23 = make_float2(0.0f, 0.0f);
 #pragma unroll
         for (int j = 0; j < KM; j++) {
             if (j < a.k) {
                 const float m = __ldg(a.basis + j * R + i);
-#pragma unroll
-                for (int v = 0; v < 4; v++) o[v] = __fmaf_rn(c[j][v], m, o[v]);
+                const float2 m2 = make_float2(m, m);
+                o01 = __ffma2_rn(make_float2(c[j][0], c[j][1]), m2, o01);
+                o23 = __ffma2_rn(make_float2(c[j][2], c[j][3]), m2, o23);
             }
         }
+        const float o[4] = {o01.x, o01.y, o23.x, o23.y};
         store_vec_from_f32<OT, 4>(ob + i * a.o_ss, o);
     }
 }
