@@ -181,9 +181,20 @@ def set_attn_kernel(which: str) -> str:
     return {v: k for k, v in codes.items()}[prev]
 
 
-def decode_attn_png(q, kanc, vanc, kdel, vdel, kraw, vraw, A, scale, out) -> None:
+def _visible(vis, B, L):
+    """(B, >= L) key-visibility bytes -> (tensor, batch stride)."""
+    require_cuda(vis)
+    if vis.dtype not in (torch.bool, torch.uint8) or vis.dim() != 2 or vis.shape[0] != B \
+            or vis.shape[1] < L or (L > 1 and vis.stride(1) != 1):
+        raise ValueError(f"visible must be a (B={B}, >= {L}) bool/uint8 tensor with unit "
+                         "stride along the keys")
+    return vis, vis.stride(0)
+
+
+def decode_attn_png(q, kanc, vanc, kdel, vdel, kraw, vraw, A, scale, out, vis=None) -> None:
     """png archive read in place: anchors (B,Hk,n,D) as row 0 of every block,
-    fp32 deltas (B,Hk,n,r-1,D) as rows 1..r-1; A (r,r) tril(ones)."""
+    fp32 deltas (B,Hk,n,r-1,D) as rows 1..r-1; A (r,r) tril(ones).  vis:
+    optional (B, n*r + t) key visibility (fc_decode_attn_masked)."""
     require_cuda(q, kanc, vanc, kdel, vdel, kraw, vraw, A, out)
     _unit_last(kanc, vanc, kdel, vdel)
     if kanc.stride() != vanc.stride() or kdel.stride() != vdel.stride():
@@ -195,6 +206,23 @@ def decode_attn_png(q, kanc, vanc, kdel, vdel, kraw, vraw, A, scale, out) -> Non
     ws = workspace(q.device, attn_workspace_bytes(B, Hq, Hk, D, n, r, r, t))
     z3 = (0, 0, 0)
     st = _stream(q.device)
+    if vis is not None:
+        vis, vis_sb = _visible(vis, B, n * r + t)
+        with torch.cuda.device(q.device):
+            rc = _lib.load().fc_decode_attn_masked(
+                _p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1), Hk, n, r, r,
+                _lib.FC_F32, _p(kdel), *_s(kdel, 0, 1, 2, 3), _p(vdel), *_s(vdel, 0, 1, 2, 3),
+                None, 0, 0, 0, None, 0, 0, 0, _lib.FC_F32,
+                _p(kraw), *(_s(kraw, 0, 1, 2) if kraw is not None else z3),
+                _p(vraw), *(_s(vraw, 0, 1, 2) if vraw is not None else z3),
+                dtype_code(kraw) if kraw is not None else 0, t,
+                _p(A), float(scale), _p(out), dtype_code(out), out.stride(0), out.stride(1),
+                _p(ws), ws.numel(), _p(kanc), _p(vanc), dtype_code(kanc), *_s(kanc, 0, 1, 2),
+                _p(vis), vis_sb, st)
+        if rc != _lib.FC_OK:
+            reset_workspace(q.device)
+        _lib.check(rc, "decode_attn_masked")
+        return
     with torch.cuda.device(q.device):
         rc = _lib.load().fc_decode_attn_png(
             _p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1), Hk, n, r,
@@ -295,9 +323,10 @@ def selftest_bounded_wait(status: torch.Tensor, epoch: int) -> None:
 
 
 def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
-                ws: torch.Tensor | None = None) -> None:
+                ws: torch.Tensor | None = None, vis=None) -> None:
     """q (B,Hq,1,D); krows/vrows (B,Hk,n,s,D) or None; k/vscales (B,Hk,n,s,1)
-    or None; kraw/vraw (B,Hk,t,D) or None; A (r,s) fp32; out (B,Hq,1,D)."""
+    or None; kraw/vraw (B,Hk,t,D) or None; A (r,s) fp32; out (B,Hq,1,D);
+    vis: optional (B, n*r + t) key visibility (fc_decode_attn_masked)."""
     require_cuda(q, krows, vrows, kscales, vscales, kraw, vraw, A, out)
     B, Hq, _, D = q.shape
     n = krows.shape[2] if krows is not None else 0
@@ -310,9 +339,7 @@ def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
         ws = workspace(q.device, need)
     z = (0, 0, 0, 0)
     st = _stream(q.device)
-    with torch.cuda.device(q.device):
-        rc = _lib.load().fc_decode_attn(
-            _p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1),
+    args = (_p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1),
             Hk, n, s, r, dtype_code(krows) if krows is not None else 0,
             _p(krows), *(_s(krows, 0, 1, 2, 3) if krows is not None else z),
             _p(vrows), *(_s(vrows, 0, 1, 2, 3) if vrows is not None else z),
@@ -324,7 +351,14 @@ def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
             dtype_code(kraw) if kraw is not None else 0, t,
             _p(A), float(scale),
             _p(out), dtype_code(out), out.stride(0), out.stride(1),
-            _p(ws), ws.numel(), st)
+            _p(ws), ws.numel())
+    with torch.cuda.device(q.device):
+        if vis is None:
+            rc = _lib.load().fc_decode_attn(*args, st)
+        else:
+            vis, vis_sb = _visible(vis, B, n * r + t)
+            rc = _lib.load().fc_decode_attn_masked(*args, None, None, 0, 0, 0, 0,
+                                                   _p(vis), vis_sb, st)
     if rc != _lib.FC_OK:
         reset_workspace(q.device)
     _lib.check(rc, "decode_attn")

@@ -21,7 +21,8 @@ FC_F32, FC_BF16, FC_F16, FC_I8 = 0, 1, 2, 3
 SYMBOLS = ("fc_version", "fc_last_error_string", "fc_jpeg_encode", "fc_jpeg_decode",
            "fc_png_encode", "fc_png_decode", "fc_decode_attn_workspace_size",
            "fc_decode_attn", "fc_decode_attn_png", "fc_decode_attn_noalloc",
-           "fc_gather_batch", "fc_rope_kv_append", "fc_set_attn_kernel",
+           "fc_gather_batch", "fc_rope_kv_append", "fc_decode_attn_masked",
+           "fc_set_attn_kernel",
            "fc_selftest_bounded_wait")
 FC_ATTN_AUTO, FC_ATTN_CUDA_CORE, FC_ATTN_TENSOR_CORE = 0, 1, 2
 
@@ -76,6 +77,20 @@ _SIGS = {
                            _P, _I64, _I64, _P, _I64, _I64, _I64,
                            _P, _P, _I64,
                            _I32, _I64, _I64, _P], _I32),
+    "fc_decode_attn_masked": ([_P, _I32, _I64, _I64, _I64, _I64, _I64,
+                               _I64, _I64, _I32, _I32, _I32,
+                               _P, _I64, _I64, _I64, _I64,
+                               _P, _I64, _I64, _I64, _I64,
+                               _P, _I64, _I64, _I64,
+                               _P, _I64, _I64, _I64,
+                               _I32,
+                               _P, _I64, _I64, _I64,
+                               _P, _I64, _I64, _I64,
+                               _I32, _I64,
+                               _P, _F32,
+                               _P, _I32, _I64, _I64, _P, ctypes.c_size_t,
+                               _P, _P, _I32, _I64, _I64, _I64,
+                               _P, _I64, _P], _I32),
     "fc_set_attn_kernel": ([_I32], _I32),
     "fc_selftest_bounded_wait": ([_P, _I32, _P], _I32),
 }

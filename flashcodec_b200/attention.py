@@ -50,7 +50,8 @@ def _rows(stream):
     raise AssertionError("png archives are read in place by fc_decode_attn_png")
 
 
-def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="auto"):
+def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="auto",
+                           visible=None):
     """Attention of one new query token against a codec archive without
     materialising the reconstructed KV (flashcodec/attention.py:64-140).
 
@@ -61,6 +62,11 @@ def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="au
         impl: accepted for API compatibility ("auto", "cuda", "triton",
             "torch"); every value runs the sm_100a kernel -- this package has
             exactly one implementation.
+        visible: optional (B, S) bool/uint8 CUDA tensor, nonzero where the
+            query attends (S = the streams' length: archived tokens, then the
+            raw tail); e.g. the padding mask of a left-padded batch.  An
+            extension of the reference API, which has no mask
+            (fc_decode_attn_masked, CUDA-core kernel).
     Returns:
         (B, Hq, 1, D) in the query dtype.  Scores, softmax and accumulation
         are fp32.
@@ -87,10 +93,11 @@ def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="au
         A = _device_A(ks.codec, ks.block_size, query.device)
         K.decode_attn_png(query, ks._anchors[:, :, :n], vs._anchors[:, :, :n],
                           ks._deltas[:, :, :n], vs._deltas[:, :, :n], ks.raw, vs.raw, A,
-                          scale, out)
+                          scale, out, vis=visible)
         return out
     krows, kscales = _rows(ks)
     vrows, vscales = _rows(vs)
     A = _device_A(ks.codec, ks.block_size, query.device) if krows is not None else None
-    K.decode_attn(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale, out)
+    K.decode_attn(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale, out,
+                  vis=visible)
     return out

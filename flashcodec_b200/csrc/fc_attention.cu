@@ -73,6 +73,11 @@ struct AttnArgs {
     const void *kanc, *vanc;
     int anc_dtype;
     int64_t a_sb, a_sh, a_sn;
+    // key visibility (fc_decode_attn_masked): vis[b * vis_sb + position] != 0
+    // where the query attends, over the archived positions then the raw tail;
+    // null = every position
+    const unsigned char *vis;
+    int64_t vis_sb;
     int64_t kr_sb, kr_sh, kr_st, vr_sb, vr_sh, vr_st;
     int n_raw;
     const float *A;
@@ -460,6 +465,10 @@ attn_kernel(AttnArgs a) {
             lg = ssc[(krows_total + pos - nb * r) * GT + my_g];
         }
         lg *= a.scale_log2;
+        if (a.vis) {
+            const int64_t gp = pos < nb * r ? n0 * r + pos : a.n * (int64_t)r + (pos - nb * r);
+            if (!a.vis[b * a.vis_sb + gp]) lg = -INFINITY;
+        }
         slg[idx] = lg;
         tmax = fmaxf(tmax, lg);
     }
@@ -471,7 +480,8 @@ attn_kernel(AttnArgs a) {
     for (int w = 0; w < kWarps; w++) m_g = fmaxf(m_g, sstat[w * GT + my_g]);
     float tsum = 0.0f;
     for (int idx = tid; idx < npos * GT; idx += kThreads) {
-        const float p = exp2f(slg[idx] - m_g);
+        // a chunk whose positions are all masked has m_g = -inf: its weights are 0
+        const float p = exp2f(slg[idx] - (m_g == -INFINITY ? 0.0f : m_g));
         slg[idx] = p;
         tsum += p;
     }
@@ -675,7 +685,8 @@ attn_kernel(AttnArgs a) {
             float o = 0.0f;
 #pragma unroll
             for (int w = 0; w < kWarps; w++) o += sred[(w * GT + g) * a.D + d];
-            store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, o / s_l[g]);
+            store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype,
+                           s_l[g] > 0.0f ? o / s_l[g] : 0.0f);
         }
         return;
     }
@@ -898,7 +909,8 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
                               float softmax_scale, void *out, int out_dtype, int64_t o_sb,
                               int64_t o_sh, void *workspace, size_t workspace_bytes,
                               void *stream,
-                            const PngAnchors *png) {
+                            const PngAnchors *png, const unsigned char *vis = nullptr,
+                            int64_t vis_sb = 0) {
     clear_error();
     if (B < 0 || Hq <= 0 || Hk <= 0 || D <= 0) { set_error("decode_attn: bad shape"); return FC_EINVAL; }
     if (Hq % Hk != 0) { set_error("decode_attn: Hq (%lld) must be a multiple of Hk (%lld)", (long long)Hq, (long long)Hk); return FC_EINVAL; }
@@ -916,8 +928,9 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     if (!q || !out || (n_blocks > 0 && (!k_rows || !v_rows || !A))) { set_error("decode_attn: null pointer"); return FC_EINVAL; }
     if (n_blocks == 0) { s = 1; r = std::max<int>(r, 1); rows_dtype = FC_F32; }
 
-    // png rows come from two tensors: the CUDA-core kernel's direct-load path
-    const int sel = png ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
+    // png rows come from two tensors (the CUDA-core kernel's direct-load path);
+    // a visibility mask is applied by the CUDA-core kernel
+    const int sel = (png || vis) ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
     if (n_blocks > 0 && sel != FC_ATTN_CUDA_CORE) {
         const int64_t G = Hq / Hk, row = (int64_t)s * D;
         const bool contig = tc_supported(D, s, r, G, rows_dtype) && k_sj == D && k_sn == row &&
@@ -1006,6 +1019,8 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     a.kr_sb = kr_sb; a.kr_sh = kr_sh; a.kr_st = kr_st;
     a.vr_sb = vr_sb; a.vr_sh = vr_sh; a.vr_st = vr_st;
     a.n_raw = (int)n_raw;
+    a.vis = vis;
+    a.vis_sb = vis_sb;
     a.A = A;
     a.scale_log2 = softmax_scale * 1.4426950408889634f;
     a.out = out; a.out_dtype = out_dtype; a.o_sb = o_sb; a.o_sh = o_sh;
@@ -1081,6 +1096,44 @@ extern "C" int fc_decode_attn_png(const void *q, int q_dtype, int64_t B, int64_t
                             v_raw, vr_sb, vr_sh, vr_st, raw_dtype, n_raw, A, softmax_scale, out,
                             out_dtype, o_sb, o_sh, workspace, workspace_bytes, stream,
                             n_blocks > 0 ? &png : nullptr);
+}
+
+extern "C" int fc_decode_attn_masked(const void *q, int q_dtype, int64_t B, int64_t Hq,
+                                     int64_t D, int64_t q_sb, int64_t q_sh, int64_t Hk,
+                                     int64_t n_blocks, int s, int r, int rows_dtype,
+                                     const void *k_rows, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                                     int64_t k_sj, const void *v_rows, int64_t v_sb, int64_t v_sh,
+                                     int64_t v_sn, int64_t v_sj, const void *k_scales,
+                                     int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                                     const void *v_scales, int64_t vs_sb, int64_t vs_sh,
+                                     int64_t vs_sn, int scale_dtype, const void *k_raw,
+                                     int64_t kr_sb, int64_t kr_sh, int64_t kr_st, const void *v_raw,
+                                     int64_t vr_sb, int64_t vr_sh, int64_t vr_st, int raw_dtype,
+                                     int64_t n_raw, const float *A, float softmax_scale, void *out,
+                                     int out_dtype, int64_t o_sb, int64_t o_sh, void *workspace,
+                                     size_t workspace_bytes, const void *k_anchors,
+                                     const void *v_anchors, int anchor_dtype, int64_t a_sb,
+                                     int64_t a_sh, int64_t a_sn, const unsigned char *visible,
+                                     int64_t vis_sb, void *stream) {
+    clear_error();
+    if (!visible) { set_error("decode_attn_masked: null visibility mask"); return FC_EINVAL; }
+    if ((k_anchors == nullptr) != (v_anchors == nullptr)) {
+        set_error("decode_attn_masked: K and V anchors go together");
+        return FC_EINVAL;
+    }
+    if (k_anchors && n_blocks > 0 &&
+        (s != r || r < 2 || rows_dtype != FC_F32 || !is_float_dtype(anchor_dtype))) {
+        set_error("decode_attn_masked: png rows need s == r >= 2, fp32 deltas and f32/bf16/f16 anchors");
+        return FC_EINVAL;
+    }
+    const PngAnchors png{k_anchors, v_anchors, anchor_dtype, a_sb, a_sh, a_sn};
+    return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype,
+                            k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj,
+                            k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn,
+                            scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st,
+                            raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh,
+                            workspace, workspace_bytes, stream,
+                            (k_anchors && n_blocks > 0) ? &png : nullptr, visible, vis_sb);
 }
 
 namespace fc {

@@ -165,7 +165,7 @@ __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t gr
         float L = 0.0f;
         for (int i = 0; i < P.n_split; i++) {
             const int64_t si = (grp * P.n_split + i) * P.GT + tid;
-            const float f = exp2f(__ldcg(P.pm + si) - M);
+            const float f = M == -INFINITY ? 0.0f : exp2f(__ldcg(P.pm + si) - M);
             fac[i * P.GT + tid] = f;
             L += __ldcg(P.pl + si) * f;
         }
@@ -179,7 +179,8 @@ __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t gr
         float o = 0.0f;
         for (int i = 0; i < P.n_split; i++)
             o = fmaf(__ldcg(P.pacc + ((grp * P.n_split + i) * P.GT + g) * P.D + d), fac[i * P.GT + g], o);
-        store_from_f32(out, o_base + (hq0 + g) * o_sh + d, out_dtype, o / Ls[g]);
+        // Ls == 0 only when every position of the group was masked out
+        store_from_f32(out, o_base + (hq0 + g) * o_sh + d, out_dtype, Ls[g] > 0.0f ? o / Ls[g] : 0.0f);
     }
     if (tid == 0) P.cnt[grp] = 0;  // ready for the next launch
 }

@@ -20,10 +20,12 @@ flashcodec/patch_attention.py:51-63):
 * the cache layer is a ``FlashCodecLayer``, the module is in eval mode, the
   step has one query token, ``position_embeddings`` is given, the module has
   no sliding window and its model file defines ``apply_rotary_pos_emb``;
-* batch 1, or any batch when transformers passes no attention mask (no row is
-  padded: beam search, sampled returns, equal-length prompts).  The reference
-  stops at batch 1 (flashcodec/patch_attention.py:54); a padded batch keeps the
-  original forward, which masks the reconstructed view.
+* any batch size.  The reference stops at batch 1
+  (flashcodec/patch_attention.py:54).  Without padding transformers passes no
+  mask.  A padded batch's mask, a (B, 1, 1, S+1) boolean or additive tensor at
+  a decode step, becomes the kernel's per-key visibility
+  (fc_decode_attn_masked).  A mask of any other shape keeps the original
+  forward.
 """
 
 from __future__ import annotations
@@ -79,6 +81,21 @@ def _fused_rope(rope, q, k, v, cos, sin, key_stream):
     return ok
 
 
+def _key_visibility(attention_mask, batch, keys):
+    """(B, keys) visibility from a decode step's attention mask, or None when
+    the mask has another form."""
+    m = attention_mask
+    if m is None or m.dim() != 4 or m.shape[0] != batch or m.shape[-2] != 1 \
+            or m.shape[-1] < keys or m.shape[1] != 1:
+        return None
+    row = m[:, 0, -1, :keys]
+    if row.dtype == torch.bool:
+        return row
+    if row.is_floating_point():          # additive mask: 0 where visible
+        return row > torch.finfo(row.dtype).min / 2
+    return None
+
+
 def _codec_layer(module, past_key_values):
     from .hf_cache import FlashCodecLayer
     layers = getattr(past_key_values, "layers", None)
@@ -96,9 +113,12 @@ def _decode_forward(module, orig, hidden_states, position_embeddings=None,
     layer = _codec_layer(module, past_key_values)
     batch, q_len = hidden_states.shape[0], hidden_states.shape[-2]
     rope = _rope_fn(module)
+    visible = None
+    if layer is not None and batch != 1 and attention_mask is not None:
+        visible = _key_visibility(attention_mask, batch, layer._key_stream.seq_len + 1)
     if (layer is None or module.training or q_len != 1 or position_embeddings is None
             or getattr(module, "sliding_window", None) is not None or rope is None
-            or (batch != 1 and attention_mask is not None)):
+            or (batch != 1 and attention_mask is not None and visible is None)):
         return orig(hidden_states, position_embeddings=position_embeddings,
                     attention_mask=attention_mask, past_key_values=past_key_values,
                     **kwargs)
@@ -135,7 +155,7 @@ def _decode_forward(module, orig, hidden_states, position_embeddings=None,
         ks.append(k)
         vs.append(v)
     from .attention import codec_decode_attention
-    out = codec_decode_attention(q, ks, vs, scale=module.scaling)
+    out = codec_decode_attention(q, ks, vs, scale=module.scaling, visible=visible)
     out = out.transpose(1, 2).reshape(*lead, -1)
     if gate is not None:
         out = out * torch.sigmoid(gate)

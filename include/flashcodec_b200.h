@@ -286,6 +286,32 @@ FC_API int fc_rope_kv_append(const void *q, int64_t q_sb, int64_t q_sh, void *q_
                              const void *cos, const void *sin, int64_t cs_sb,
                              int dtype, int64_t B, int64_t D, void *stream);
 
+/* Decode attention with a key-visibility mask: the arguments of fc_decode_attn,
+ * optional png anchors, and visible[b * vis_sb + p] (one byte per key
+ * position, nonzero = the query attends): positions 0 .. n_blocks*r - 1 are
+ * the archived tokens, then the n_raw tail tokens.  Serves left-padded
+ * batches, whose padding the reference cannot skip on its coefficient-domain
+ * path (flashcodec/patch_attention.py:52-54 falls back to the reconstructed
+ * view for any batch > 1).  Masked logits are -inf; a query with no visible
+ * key gets a zero output.  With k_anchors/v_anchors non-null the rows are a
+ * png archive as in fc_decode_attn_png (rows = fp32 deltas, s == r).  Always
+ * runs the CUDA-core kernel. */
+FC_API int fc_decode_attn_masked(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                 int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int s,
+                                 int r, int rows_dtype, const void *k_rows, int64_t k_sb,
+                                 int64_t k_sh, int64_t k_sn, int64_t k_sj, const void *v_rows,
+                                 int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t v_sj,
+                                 const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                                 const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                                 int scale_dtype, const void *k_raw, int64_t kr_sb, int64_t kr_sh,
+                                 int64_t kr_st, const void *v_raw, int64_t vr_sb, int64_t vr_sh,
+                                 int64_t vr_st, int raw_dtype, int64_t n_raw, const float *A,
+                                 float softmax_scale, void *out, int out_dtype, int64_t o_sb,
+                                 int64_t o_sh, void *workspace, size_t workspace_bytes,
+                                 const void *k_anchors, const void *v_anchors, int anchor_dtype,
+                                 int64_t a_sb, int64_t a_sh, int64_t a_sn,
+                                 const unsigned char *visible, int64_t vis_sb, void *stream);
+
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
  * AUTO uses the tcgen05 int8 tensor-core kernel whenever the archive allows
  * it (contiguous (B, Hk, cap, s, 128) int8 codes, block size 8 with

@@ -145,3 +145,23 @@ def test_rope_kv_append_validates_on_the_host(lib):
     assert call(q_out=q) == _lib.FC_EINVAL
     assert call(B=-1) == _lib.FC_EINVAL
     assert call(B=0) == _lib.FC_OK
+
+
+def test_masked_attention_validates_on_the_host(lib):
+    """fc_decode_attn_masked refuses a null mask and half-given png anchors."""
+    from flashcodec_b200 import _lib
+    P = ctypes.c_void_p
+    d = P(0x1000)
+
+    def call(vis=d, kanc=None, vanc=None):
+        return lib.fc_decode_attn_masked(
+            d, _lib.FC_F32, 1, 4, 64, 256, 64, 2, 4, 2, 8, _lib.FC_I8,
+            d, 0, 0, 0, 0, d, 0, 0, 0, 0, d, 0, 0, 0, d, 0, 0, 0, _lib.FC_F32,
+            None, 0, 0, 0, None, 0, 0, 0, _lib.FC_F32, 0,
+            d, 0.125, d, _lib.FC_F32, 256, 64, None, 0,
+            kanc, vanc, _lib.FC_F32, 0, 0, 0, vis, 64, None)
+
+    assert call(vis=None) == _lib.FC_EINVAL
+    assert b"visibility" in lib.fc_last_error_string()
+    assert call(kanc=d) == _lib.FC_EINVAL
+    assert call() == _lib.FC_ERANGE          # valid so far; no workspace given
