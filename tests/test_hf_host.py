@@ -127,3 +127,24 @@ def test_layer_structural_ops_before_any_data():
     layer.batch_select_indices(torch.tensor([0]))
     layer.reset()
     assert layer.storage_bytes() == 0 and layer.get_mask_sizes(1) == (1, 0)
+
+
+def test_decode_mask_to_key_visibility():
+    """The patched attention turns a decode step's (B, 1, 1, S+1) mask into
+    per-key visibility: boolean masks as they are, additive masks where the
+    bias is 0; other shapes keep the original forward (None)."""
+    from flashcodec_b200.patch_attention import _key_visibility
+    B, L = 3, 10
+    vis = torch.ones(B, L, dtype=torch.bool)
+    vis[1, :4] = False
+    m_bool = vis[:, None, None, :]
+    assert torch.equal(_key_visibility(m_bool, B, L), vis)
+    m_add = torch.zeros(B, 1, 1, L).masked_fill(~vis[:, None, None, :],
+                                                torch.finfo(torch.float32).min)
+    assert torch.equal(_key_visibility(m_add, B, L), vis)
+    assert torch.equal(_key_visibility(m_bool, B, L - 2), vis[:, :L - 2])
+    assert _key_visibility(None, B, L) is None
+    assert _key_visibility(m_bool, B, L + 1) is None             # shorter than the keys
+    assert _key_visibility(m_bool[:2], B, L) is None             # batch mismatch
+    assert _key_visibility(vis[:, None, :].expand(B, 2, L)[:, None], B, L) is None  # 2 queries
+    assert _key_visibility(m_bool.int(), B, L) is None           # integer masks: unknown form
