@@ -560,8 +560,12 @@ def run_decode_step(args):
     sampler.start()
     time.sleep(0.5)
     t0 = time.time()
+    torch.cuda.nvtx.range_push("fused")
     ms_f = timed(fused)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.nvtx.range_push("unfused")
     ms_u = timed(unfused)
+    torch.cuda.nvtx.range_pop()
     clocks = sampler.stop(t0, time.time())
     assert K.attn_status(dev) == 0, "a bounded wait in the attention kernel gave up"
     L = len(layers)
