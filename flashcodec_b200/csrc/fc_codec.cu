@@ -31,6 +31,7 @@ struct EncArgs {
     int scale_dtype;
     int64_t s_sb, s_sh, s_sn;
     int *err;
+    int bpw;  // blocks per warp of the d128 fast path (kEncBlocks, or 1 for small launches)
 };
 
 __device__ __forceinline__ float nan_max(float m, float a) {
@@ -164,7 +165,7 @@ jpeg_encode_kernel(EncArgs a) {
 
 // Fast path of the archive for head dim 128 (four channels per lane), block
 // length R in {8, 16} and k <= KM frequencies.  Each warp takes kEncBlocks
-// consecutive blocks and loads the rows of the next one (as raw words) while
+// consecutive blocks (one in launches smaller than a wave) and loads the rows of the next one (as raw words) while
 // it computes the current one, so HBM latency overlaps the FMA chains,
 // amax reduction and quantizer; coefficients stay in registers and the tiny
 // basis is read with uniform loads.  Same operations in the same order as
@@ -184,9 +185,9 @@ jpeg_encode_d128_kernel(EncArgs a) {
     using W = typename Rows::W;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t total = a.B * a.H * a.nblk;
-    const int64_t g0 = ((int64_t)blockIdx.x * kWarpsPerCta + warp) * kEncBlocks;
+    const int64_t g0 = ((int64_t)blockIdx.x * kWarpsPerCta + warp) * a.bpw;
     if (g0 >= total) return;
-    const int nb = (int)min((int64_t)kEncBlocks, total - g0);
+    const int nb = (int)min((int64_t)a.bpw, total - g0);
     constexpr int dt = Elem<T>::code;
     const bool quant = a.scales != nullptr;
     const int d0 = lane * 4;
@@ -631,7 +632,11 @@ extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, 
             return FC_EINVAL;
         } else {
             if (v4 && D == 128 && (r == 8 || r == 16) && k <= 8) {
-                const unsigned g = grid_for((B * H * nblk + kEncBlocks - 1) / kEncBlocks);
+                // a launch smaller than one wave at kEncBlocks per warp (a decode
+                // step archives one block per stream) spreads its blocks, one per warp
+                const int64_t total = B * H * nblk;
+                a.bpw = total >= (int64_t)kEncBlocks * kWarpsPerCta * num_sms() ? kEncBlocks : 1;
+                const unsigned g = grid_for((total + a.bpw - 1) / a.bpw);
                 if (r == 8 && k <= 4) jpeg_encode_d128_kernel<T, 8, 4><<<g, kWarpsPerCta * 32, 0, st>>>(a);
                 else if (r == 8) jpeg_encode_d128_kernel<T, 8, 8><<<g, kWarpsPerCta * 32, 0, st>>>(a);
                 else if (k <= 4) jpeg_encode_d128_kernel<T, 16, 4><<<g, kWarpsPerCta * 32, 0, st>>>(a);
