@@ -135,16 +135,20 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic():
-    """Per-launch DRAM bytes of the attention kernel from the committed ncu
-    summary (profiles/attn_decode_cfg2.json), or None."""
+def ncu_traffic(per_launch):
+    """Per-launch DRAM bytes (read + write) of the attention kernel at this
+    workload, from the committed one-kernel ncu capture of a small case
+    (profiles/attn_decode_cfg2.json): its measured bytes per algorithmic byte
+    times this launch's algorithmic bytes (the kernel streams each archive
+    byte once, so traffic grows in proportion), or None."""
     p = ROOT / "profiles" / "attn_decode_cfg2.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text()).get("dram_bytes_per_launch")
-        except Exception:
-            return None
-    return None
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d["dram_bytes_per_launch"] / d["algorithmic_bytes_per_launch"] * per_launch
+    except Exception:
+        return None
 
 
 class ClockSampler:
@@ -229,31 +233,119 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
-def build_layers(cfg, rank, device):
-    """Archive every layer's synthetic K/V through the product's append path
-    (the jpeg int8 archive kernel); returns [(k_stream, v_stream, q)]."""
+def make_bench_codec(cfg):
     import flashcodec_b200 as fc
+    codec = cfg.get("codec", "jpeg-int8")
+    if codec == "png":
+        return fc.make_codec("png", block_size=cfg["r"], keep_ratio=1.0)
+    return fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"],
+                         quant_bits=8 if codec == "jpeg-int8" else 0,
+                         scale_dtype=torch.float16 if cfg["scale_dtype"] == "fp16"
+                         else torch.float32)
+
+
+def _fill_rows(st, b0, x):
+    """Archive x (b, H, S, D) into rows b0:b0+b of a preallocated stream (the
+    same kernels and slots as ``_CodecStream.append``)."""
+    from flashcodec_b200 import _kernels as K
+    from flashcodec_b200.codecs.jpeg import device_basis
+    r, b = st.block_size, x.shape[0]
+    n = st.n_blocks
+    rows = slice(b0, b0 + b)
+    if st.codec.name == "jpeg":
+        k = st.codec.keep_freqs
+        basis = device_basis(r, k, x.device)
+        K.jpeg_encode(x[:, :, :n * r], basis, r, k, st._coeffs[rows, :, :n],
+                      st._scales[rows, :, :n] if st.codec.quantized else None)
+    else:
+        K.png_encode(x[:, :, :n * r], r, st.codec.keep_m, st._deltas[rows, :, :n],
+                     st._anchors[rows, :, :n])
+    if st._raw_len:
+        st._raw_buf[rows, :, :st._raw_len].copy_(x[:, :, n * r:])
+
+
+CHUNK = 16   # sequences generated (and seeded) together
+
+
+def build_layers(cfg, device, rows, heads=None, Bg=None):
+    """Archive every layer's synthetic K/V for global batch rows
+    [rows[0], rows[1]) and KV heads [heads[0], heads[1]) (default all) through
+    the product's archive kernels; returns [(k_stream, v_stream, q)].
+
+    The global batch is generated in chunks of CHUNK sequences, chunk c of
+    layer L from seed 1000 * c + L, so a row holds the same data whichever
+    rank owns it (weak, strong and head-split runs agree row by row)."""
+    import flashcodec_b200 as fc
+    Hq, Hk, D, r = cfg["Hq"], cfg["Hk"], cfg["D"], cfg["r"]
+    G = Hq // Hk
+    Bg = Bg or rows[1]
+    h0, h1 = heads or (0, Hk)
+    b0, b1 = rows
+    S = cfg["S"] + cfg["tail"]
+    n, t = S // r, S % r
     layers = []
     for L in range(cfg["layers"]):
-        seed = 1000 * rank + L
-        k, v, q = synth_case(cfg["B"], cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"],
-                             cfg["rho"], seed, device=device, dtype=torch.bfloat16)
-        codec = cfg.get("codec", "jpeg-int8")
-        if codec == "png":
-            c = fc.make_codec("png", block_size=cfg["r"], keep_ratio=1.0)
-        else:
-            c = fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"],
-                              quant_bits=8 if codec == "jpeg-int8" else 0,
-                              scale_dtype=torch.float16 if cfg["scale_dtype"] == "fp16"
-                              else torch.float32)
-        ks, vs = fc._CodecStream(c), fc._CodecStream(c)
-        ks.append(k)
-        del k
-        vs.append(v)
-        del v
-        layers.append((ks, vs, q))
+        codec = make_bench_codec(cfg)
+        pair = []
+        like = torch.empty(b1 - b0, h1 - h0, 0, D, dtype=torch.bfloat16, device=device)
+        for _ in range(2):
+            st = fc._CodecStream(codec)
+            st.meta, st.dtype = (b1 - b0, h1 - h0, D, 2), torch.bfloat16
+            st._grow(n, like)
+            st.n_blocks, st.n_archived = n, n * r
+            if t:
+                st._ensure_raw(like)
+                st._raw_len = t
+            pair.append(st)
+        qs = []
+        for c in range(b0 // CHUNK, (b1 - 1) // CHUNK + 1):
+            c0, c1 = c * CHUNK, min((c + 1) * CHUNK, Bg)
+            k, v, q = synth_case(c1 - c0, Hq, Hk, S, D, cfg["rho"], 1000 * c + L, device=device,
+                                 dtype=torch.bfloat16)
+            lo, hi = max(b0, c0), min(b1, c1)
+            sel = slice(lo - c0, hi - c0)
+            for st, x in zip(pair, (k, v)):
+                _fill_rows(st, lo - b0, x[sel, h0:h1])
+            qs.append(q[sel, h0 * G:h1 * G])
+            del k, v
+        layers.append((pair[0], pair[1], torch.cat(qs).contiguous()))
     torch.cuda.synchronize()
     return layers
+
+
+def check_outputs(layers, outs, which, b=0):
+    """The checker, outside every timed region: sequence b of the given layers
+    against the fp64 CPU oracle on the archive rows read back from the device.
+    Bound: 2e-3 + one bf16 rounding of the output (2^-8 relative), the
+    attention parity bar for bf16 outputs."""
+    import numpy as np
+    from oracle import oracle as orc
+    import flashcodec_b200 as fc
+    f = lambda x: x.float().cpu().numpy()  # noqa: E731
+    worst, ok = 0.0, True
+    for i in which:
+        ks, vs, q = layers[i]
+        n, sel = ks.n_blocks, slice(b, b + 1)
+        rows = {}
+        for nm, st in (("k", ks), ("v", vs)):
+            if st.codec.name == "png":
+                rows[nm] = orc.stored_rows("png", anchors=f(st._anchors[sel, :, :n]),
+                                           deltas=f(st._deltas[sel, :, :n]))
+            elif st.codec.quantized:
+                rows[nm] = orc.stored_rows("jpeg", codes=f(st._coeffs[sel, :, :n]),
+                                           scales=f(st._scales[sel, :, :n]))
+            else:
+                rows[nm] = orc.stored_rows("jpeg", codes=f(st._coeffs[sel, :, :n]))
+            rows[nm + "raw"] = f(st.raw[sel]) if st.raw is not None else None
+        A = f(fc.block_basis(ks.codec, ks.block_size))
+        ref = orc.decode_attention(f(q[sel]), rows["k"], rows["v"], rows["kraw"], rows["vraw"], A)
+        err = np.abs(f(outs[i][sel]) - ref)
+        ok = ok and bool(np.all(err <= 2e-3 + 2.0 ** -8 * np.abs(ref)))
+        worst = max(worst, float(err.max()))
+    return {"checked": f"sequence {b} of layers {list(which)} vs the fp64 CPU oracle "
+                       "(oracle.decode_attention) on the archive read back",
+            "bound": "|out - ref| <= 2e-3 + 2^-8 |ref| (bf16 output)",
+            "max_abs_err": worst, "pass": ok}
 
 
 def cpu_sample_from(layers, cfg, b_sample=1):
@@ -263,88 +355,100 @@ def cpu_sample_from(layers, cfg, b_sample=1):
     out = {}
     for nm, st in (("k", ks), ("v", vs)):
         out[nm] = st._coeffs[:b_sample, :, :n].cpu().numpy()
-        out[nm + "s"] = st._scales[:b_sample, :, :n].cpu().numpy()
-        out[nm + "raw"] = st.raw[:b_sample].float().cpu().numpy()
+        out[nm + "s"] = st._scales[:b_sample, :, :n].float().cpu().numpy()
+        out[nm + "raw"] = st.raw[:b_sample].float().cpu().numpy() if st.raw is not None else None
     out["q"] = q[:b_sample].float().cpu().numpy()
     return out
 
 
-def time_cpu_baseline(sample, cfg, reps, threads):
-    """Time the oracle's fp32 restatement of the reference's torch attention
-    path on host cores; tokens/s scaled from the sample (b_sample sequences,
-    one layer) to the 36-layer step."""
-    import numpy as np
+def cpu_attention_call(sample, cfg):
+    """(fn, args) of the timed CPU arm: the oracle's port of the reference's
+    torch attention path, spread over every host thread."""
     from oracle import oracle as orc
     import flashcodec_b200 as fc
     A = fc.block_basis(fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"]),
                        cfg["r"]).numpy()
+    threads = os.cpu_count() or 1
     args = (sample["q"], sample["k"], sample["ks"], sample["v"], sample["vs"], sample["kraw"],
             sample["vraw"], A)
-    orc.reference_attention_int8(*args)
+    return (lambda: orc.reference_attention_int8_mt(*args, threads=threads)), threads
+
+
+CPU_SAMPLE_DESC = ("one layer of the step, sequence 0 of {B}, all {Hk} KV heads, full context "
+                   "({n} blocks + {t} raw): oracle.reference_attention_int8_mt, the port of the "
+                   "reference's torch path (fp32 dequantize, q.rows, expansion through A, fp32 "
+                   "softmax, fold back, weighted V sum) on {threads} host threads; "
+                   "tokens/s = 1 / ({layers} layers x sample time)")
+
+
+def time_cpu_baseline(sample, cfg, reps):
+    """Time the CPU arm on a bounded sample (one layer, one sequence) on the
+    host cores; tokens/s = 1 / (layers x time)."""
+    fn, threads = cpu_attention_call(sample, cfg)
+    fn()
     ts = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        orc.reference_attention_int8(*args)
+        fn()
         ts.append(time.perf_counter() - t0)
     t = statistics.median(ts)
-    b = sample["q"].shape[0]
-    nbytes = attn_bytes(b, cfg["Hq"], cfg["Hk"], cfg["D"], sample["k"].shape[2], cfg["K"],
-                        cfg["tail"])
-    return {"value": b / (cfg["layers"] * t), "unit": "tokens/s", "cores": threads,
+    n = sample["k"].shape[2]
+    tail = 0 if sample["kraw"] is None else sample["kraw"].shape[2]
+    nbytes = attn_bytes(1, cfg["Hq"], cfg["Hk"], cfg["D"], n, cfg["K"], tail)
+    return {"value": 1.0 / (cfg["layers"] * t), "unit": "tokens/s", "cores": threads,
             "kind": "port",
-            "sample": (f"one layer, batch {b} of {cfg['B']}, all {cfg['Hk']} KV heads, full "
-                       f"context; median of {reps} calls of "
-                       f"oracle.reference_attention_int8 (numpy: fp32 dequantize + fp32 BLAS) "
-                       f"= {t * 1e3:.1f} ms ({nbytes / t / 1e9:.2f} GB/s of compressed "
-                       f"bytes); tokens/s = batch / (36 layers x time)")}
+            "sample": CPU_SAMPLE_DESC.format(B=cfg["B"], Hk=cfg["Hk"], n=n, t=tail,
+                                             threads=threads, layers=cfg["layers"])
+            + f"; median of {reps} = {t * 1e3:.1f} ms ({nbytes / t / 1e9:.2f} GB/s of "
+              "compressed bytes)"}
 
 
 def run_reference(args, cfg):
     """--impl reference: the reference algorithm's CPU implementation (the
-    oracle port) on the host cores, same metric/config/unit."""
+    oracle's port of its torch path) on the host cores, same metric, unit and
+    workload.  The reference is Python: it does not travel to the GPU box, so
+    its arithmetic runs as the port.  Each step is one bounded sample of the
+    workload (one layer, one sequence, full context) and ms_per_step is that
+    sample's measured time; tokens/s = 1 / (layers x step time).  Under
+    torchrun only rank 0 runs (one host's cores; the value does not grow
+    with --gpus)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1 and rank != 0:
         return
-    import numpy as np
     from oracle import oracle as orc
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    b = 1
-    k, v, q = synth_case(b, cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"], cfg["rho"],
-                         0, dtype=torch.bfloat16)
     import flashcodec_b200 as fc
+    k, v, q = synth_case(1, cfg["Hq"], cfg["Hk"], cfg["S"] + cfg["tail"], cfg["D"], cfg["rho"],
+                         0, dtype=torch.bfloat16)
     basis = fc.dct_basis(cfg["r"], cfg["K"]).numpy()
     n = cfg["S"] // cfg["r"]
-    rows = {}
+    sample = {"q": q.float().numpy()}
     for nm, x in (("k", k), ("v", v)):
         xn = x.float().numpy()
         coef = orc.jpeg_encode(xn[:, :, :n * cfg["r"]], cfg["r"], cfg["K"], basis, "bf16")
-        rows[nm], rows[nm + "s"] = orc.jpeg_quantize(coef, "bf16")
-        rows[nm + "raw"] = xn[:, :, n * cfg["r"]:]
-    A = basis[:cfg["K"], :cfg["r"]].T.copy()
-    call = (q.float().numpy(), rows["k"], rows["ks"], rows["v"], rows["vs"], rows["kraw"],
-            rows["vraw"], A)
+        sample[nm], sample[nm + "s"] = orc.jpeg_quantize(coef, "bf16")
+        sample[nm + "raw"] = xn[:, :, n * cfg["r"]:] if cfg["tail"] else None
+    fn, threads = cpu_attention_call(sample, cfg)
     for _ in range(args.warmup):
-        orc.reference_attention_int8(*call)
+        fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        orc.reference_attention_int8(*call)
+        fn()
     dt = (time.perf_counter() - t0) / max(args.steps, 1)
-    value = b / (cfg["layers"] * dt)
+    value = 1.0 / (cfg["layers"] * dt)
+    desc = CPU_SAMPLE_DESC.format(B=cfg["B"], Hk=cfg["Hk"], n=n, t=cfg["tail"], threads=threads,
+                                  layers=cfg["layers"])
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dt * cfg["layers"] * cfg["B"] / b * 1e3,
+            "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
             "config": workload_config(cfg, world),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
                              "kind": "port",
-                             "sample": (f"each step: one layer, batch {b} of {cfg['B']}, all "
-                                        f"{cfg['Hk']} KV heads, full context, "
-                                        "oracle.reference_attention_int8 (numpy: fp32 dequantize + fp32 BLAS); "
-                                        "tokens/s = batch / (36 layers x step time); "
-                                        "ms_per_step scaled to the full 36-layer batch-16 step")},
+                             "sample": "each step: " + desc + "; ms_per_step is the measured "
+                                       "time of that sample (one host's cores, the same for "
+                                       "every --gpus)"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -590,11 +694,17 @@ def run_decode_step(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(cfg, world):
-    name = ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K decode-attention "
-            "launch per layer over the int8 DCT archive") if cfg["config"] == 2 else (
-            "config 5: long-context decode, batch-sharded (16 sequences per GPU = global 128 "
-            "at 8 GPUs), S=131072, 8 layer archives, one split-K decode-attention launch per layer")
+def workload_config(cfg, world, plan=None, Bg=None):
+    if cfg["config"] == 2:
+        name = ("config 2: Qwen3-8B-shaped decode, 36 layers, one split-K decode-attention "
+                "launch per layer over the int8 DCT archive")
+    elif plan is None:
+        name = ("config 5: long-context decode, batch-sharded (16 sequences per GPU = global "
+                "128 at 8 GPUs), S=131072, 8 layer archives, one split-K decode-attention "
+                "launch per layer")
+    else:
+        name = (f"config 5: long-context decode, global batch {Bg} sharded over {world} GPU(s), "
+                "S=131072, 8 layer archives, one split-K decode-attention launch per layer")
     codec = cfg.get("codec", "jpeg-int8")
     if codec == "jpeg-fp":
         name = name.replace("int8 DCT archive", "unquantized DCT archive (bf16 coefficients)")
@@ -605,13 +715,25 @@ def workload_config(cfg, world):
         desc = f"png r={cfg['r']} keep_ratio=1.0"
     else:
         desc = f"jpeg r={cfg['r']} K={cfg['K']} int8, {cfg['scale_dtype']} scales"
+    if plan is None:
+        par = f"batch-sharded x{world} (no collective), {cfg['B']} sequences per GPU"
+        gb, per = cfg["B"] * world, cfg["B"]
+    elif plan.mode == "batch":
+        par = f"batch-sharded x{world} (no collective), global batch {Bg}"
+        gb, per = Bg, f"{Bg // world}-{-(-Bg // world)}"
+    else:
+        par = (f"KV-head-sharded x{world}: {world // Bg} ranks per sequence, "
+               f"{cfg['Hk'] // (world // Bg)} KV heads each; one NCCL all_gather of the "
+               "(B, Hq_local, 1, D) outputs per layer inside the step")
+        gb, per = Bg, f"1 sequence, {cfg['Hk'] // (world // Bg)} of {cfg['Hk']} KV heads"
     return {"workload": name,
-            "layers": cfg["layers"], "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
+            "layers": cfg["layers"], "batch_per_gpu": per, "global_batch": gb,
             "Hq": cfg["Hq"], "Hkv": cfg["Hk"], "head_dim": cfg["D"], "context": cfg["S"],
             "raw_tail": cfg["tail"],
             "codec": desc,
-            "kv_dtype": "bf16", "parallelism": f"batch-sharded x{world} (no collective)",
-            "l2": "no flush: the archive read each step (>8 GB per GPU) is >60x L2"}
+            "kv_dtype": "bf16", "parallelism": par,
+            "l2": "no flush: the archives read each step are larger than L2 "
+                  "(> 8 GB per GPU at the default sizes)"}
 
 
 def main():
@@ -623,14 +745,21 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=(2, 5),
                     help="attention workload: config 2 (default, the headline) or config 5")
     ap.add_argument("--layers", type=int, default=None,
-                    help="layers (default 36; fewer only for profiling a small case)")
+                    help="layers (default 36 / 8; fewer only for profiling a small case)")
     ap.add_argument("--batch", type=int, default=None,
-                    help="sequences per GPU (default 16; smaller only for profiling)")
+                    help="sequences per GPU in weak scaling (default 16; smaller only for "
+                         "profiling)")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="strong scaling: this many sequences in total, sharded over the GPUs "
+                         "by batch (>= GPUs) or by KV head (< GPUs; one NCCL all_gather of "
+                         "outputs per layer)")
     ap.add_argument("--codec", default="jpeg-int8", choices=("jpeg-int8", "jpeg-fp", "png"),
                     help="archive format of the attention workload: jpeg-int8 (default, the "
                          "headline), jpeg-fp (quant_bits=0, bf16 coefficients) or png "
                          "(r=8, lossless; 4 layers by default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the post-timing oracle check (profiling runs only)")
     ap.add_argument("--workload", default="attention", choices=("attention",) + CODEC_WORKLOADS,
                     help="attention (default, config 2) or one codec kernel's HBM throughput")
     args = ap.parse_args()
@@ -659,17 +788,44 @@ def main():
 
     import flashcodec_b200 as fc
     from flashcodec_b200 import _kernels as K
+    from flashcodec_b200 import sharding
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    layers = build_layers(cfg, rank, dev)
+    Hk, G = cfg["Hk"], cfg["Hq"] // cfg["Hk"]
+    plan, Bg = None, None
+    if args.global_batch:
+        Bg = args.global_batch
+        plan = sharding.plan_shards(Bg, Hk, cfg["Hq"], world)
+        rows, heads = plan.batch_range(rank), plan.kv_head_range(rank)
+    else:
+        rows, heads = (rank * cfg["B"], (rank + 1) * cfg["B"]), (0, Hk)
+    gather = plan is not None and plan.needs_gather()
+    layers = build_layers(cfg, dev, rows, heads, Bg=Bg or world * cfg["B"])
     n = layers[0][0].n_blocks
-    per_launch = codec_attn_bytes(cfg, n)
-    outs = [torch.empty_like(q) for _, _, q in layers]
+    local_cfg = dict(cfg, B=rows[1] - rows[0], Hk=heads[1] - heads[0],
+                     Hq=(heads[1] - heads[0]) * G)
+    per_launch = codec_attn_bytes(local_cfg, n)
+    outs = [None] * len(layers)
+    full = [None] * len(layers)
 
-    def step():
+    def step(with_gather=gather):
         for i, (ks, vs, q) in enumerate(layers):
             outs[i] = fc.codec_decode_attention(q, ks, vs)
+            if with_gather:
+                full[i] = sharding.gather_outputs(plan, outs[i])
+
+    def timed(steps, with_gather=gather):
+        stream = torch.cuda.current_stream(dev)
+        barrier(world)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            step(with_gather)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return start.elapsed_time(end) / steps
 
     for _ in range(args.warmup):
         step()
@@ -677,90 +833,120 @@ def main():
     if sampler:
         sampler.start()
         time.sleep(0.5)
-    stream = torch.cuda.current_stream(dev)
     # The attention launches run back to back as a model issues them (no
     # event between them, so each launch may be scheduled while the previous
     # one drains); the kernel's average launch duration is the timed region
-    # divided by the launches in it (nothing else runs in the region).
-    barrier(world)
+    # divided by the launches in it (nothing else runs in the region unless
+    # the heads are split, where each layer adds one all_gather).
     t_wall0 = time.time()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
     torch.cuda.nvtx.range_push("timed")
-    for _ in range(args.steps):
-        for i, (ks, vs, q) in enumerate(layers):
-            outs[i] = fc.codec_decode_attention(q, ks, vs)
+    ms = timed(args.steps)
     torch.cuda.nvtx.range_pop()
-    end.record(stream)
-    torch.cuda.synchronize()
     t_wall1 = time.time()
-    barrier(world)
-    ms = start.elapsed_time(end) / args.steps
-    kern_ms = ms / len(layers)
-    ms_max = max_over_ranks(ms, world)
-    kern_max = max_over_ranks(kern_ms, world)
     clocks = sampler.stop(t_wall0, t_wall1) if sampler else None
-    assert K.attn_status(dev) == 0, "a bounded wait in the attention kernel gave up"
+    ms_max = max_over_ranks(ms, world)
+    ms_compute = max_over_ranks(timed(max(1, args.steps // 2), False), world) if gather else ms_max
+    kern_max = ms_compute / len(layers)
+    status = K.attn_status(dev)
 
     # end to end through the public API with host buffers: H2D of every
-    # layer's query from pinned memory, the attention calls, D2H of outputs
+    # layer's query from pinned memory, the attention calls (and the output
+    # gather when heads are split), D2H of the step's outputs
     qh = torch.stack([q for _, _, q in layers]).cpu().pin_memory()
-    oh = torch.empty_like(qh).pin_memory()
+    res = full if gather else outs
+    oh = torch.empty((len(layers),) + tuple(res[0].shape), dtype=res[0].dtype).pin_memory()
     qd = torch.empty_like(qh, device=dev)
-    for _ in range(2):
+
+    def e2e_step():
         qd.copy_(qh, non_blocking=True)
         for i, (ks, vs, _) in enumerate(layers):
             outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
-        oh.copy_(torch.stack(outs), non_blocking=True)
+            if gather:
+                full[i] = sharding.gather_outputs(plan, outs[i])
+        oh.copy_(torch.stack(full if gather else outs), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
     barrier(world)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_steps = max(1, args.steps // 3)
+    stream = torch.cuda.current_stream(dev)
     e_start.record(stream)
     for _ in range(e_steps):
-        qd.copy_(qh, non_blocking=True)
-        for i, (ks, vs, _) in enumerate(layers):
-            outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
-        oh.copy_(torch.stack(outs), non_blocking=True)
+        e2e_step()
     e_end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
     e_ms = max_over_ranks(e_start.elapsed_time(e_end) / e_steps, world)
 
+    # the checker (outside the timed regions): sequence 0 of this rank's first
+    # and last layer against the fp64 oracle; with split heads also that the
+    # gathered output holds this rank's piece where the plan puts it
+    check = None
+    if not args.no_check:
+        step()
+        torch.cuda.synchronize()
+        check = check_outputs(layers, outs, sorted({0, len(layers) - 1}))
+        if gather:
+            b0, b1 = rows
+            q0, q1 = heads[0] * G, heads[1] * G
+            placed = all(torch.equal(full[i][b0:b1, q0:q1], outs[i]) for i in range(len(layers)))
+            check["gather_placement"] = placed
+            check["pass"] = check["pass"] and placed
+        bad = max_over_ranks(0.0 if check["pass"] else 1.0, world)
+        check["pass"] = bad == 0.0
+        check["ranks"] = world
+        check["status_word"] = status
+
     cpu = None
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and cfg["config"] == 2
             and cfg["codec"] == "jpeg-int8"):
-        threads = os.cpu_count() or 1
-        torch.set_num_threads(threads)
-        cpu = time_cpu_baseline(cpu_sample_from(layers, cfg), cfg, reps=5, threads=threads)
+        cpu = time_cpu_baseline(cpu_sample_from(layers, cfg), cfg, reps=5)
 
     if rank == 0:
         peak, kind = measured_peaks()
         achieved = per_launch / (kern_max * 1e-3) / 1e9
-        traffic = (ncu_traffic() if cfg["config"] == 2 and cfg["B"] == CFG2["B"]
-                   and cfg["codec"] == "jpeg-int8" else None)
+        traffic = (ncu_traffic(per_launch) if cfg["config"] == 2 and plan is None
+                   and cfg["B"] == CFG2["B"] and cfg["codec"] == "jpeg-int8" else None)
+        tokens = Bg if plan is not None else world * cfg["B"]
         line = {
             "metric": METRIC if cfg["codec"] == "jpeg-int8" else
             f"decode-attn tokens/s & achieved HBM GB/s (% of peak) on {cfg['codec']} KV, 1 B200",
-            "value": world * cfg["B"] / (ms_max * 1e-3), "unit": "tokens/s",
+            "value": tokens / (ms_max * 1e-3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": workload_config(cfg, world),
+            "higher_is_better": True, "scaling": "strong" if plan is not None else "weak",
+            "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": workload_config(cfg, world, plan, Bg),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": per_launch,
-                         "kernel_ms": kern_max},
+                         "kernel_ms": kern_max,
+                         "kernel": "attn_tc_kernel" if cfg["codec"] == "jpeg-int8"
+                         else "attn_kernel"},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * cfg["B"] / (e_ms * 1e-3), "unit": "tokens/s",
+            "e2e": {"value": tokens / (e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": qh.numel() * qh.element_size(),
                     "d2h_bytes_per_step": oh.numel() * oh.element_size(),
                     "ms_per_step": e_ms},
+            "check": check,
             "gpu_launches": args.steps * len(layers),
             "clocks": clocks,
         }
+        if gather:
+            g_ms = (ms_max - ms_compute) / len(layers)
+            line["head_split"] = {
+                "allgather_ms_per_layer": g_ms, "allgather_share": (ms_max - ms_compute) / ms_max,
+                "attention_ms_per_layer": kern_max,
+                "allgather_bytes_per_rank_per_layer": outs[0].numel() * outs[0].element_size(),
+                "note": "all_gather time = step time with the gather minus the step without it"}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    if check is not None and not check["pass"]:
+        raise SystemExit("decode attention output differs from the oracle (see the check field)")
+    if status != 0:
+        raise SystemExit(f"a bounded wait in the attention kernel gave up (launch {status})")
 
 
 if __name__ == "__main__":

@@ -12,7 +12,7 @@ C ABI in include/flashcodec_b200.h).  CUDA tensors only: there is no CPU
 implementation in this package.
 """
 
-from .attention import block_basis, codec_decode_attention
+from .attention import attention_status, block_basis, codec_decode_attention
 from .cache import CodecKVCache, _CodecStream, make_codec
 from .codecs import (JPEGCodec, PNGCodec, dct_basis, dct_compress, dct_decompress,
                      dequantize_coeffs, png_filter, png_reconstruct, quantize_coeffs)
@@ -41,7 +41,7 @@ __all__ = [
     "apply_codec_attention", "remove_codec_attention", "codec_attention_stats",
     "CodecKVCache", "FlashCodecCache", "FlashCodecLayer", "make_codec",
     "HAS_HF_CACHE", "JPEGCodec", "PNGCodec",
-    "codec_decode_attention", "block_basis",
+    "codec_decode_attention", "block_basis", "attention_status",
     "dct_basis", "dct_compress", "dct_decompress",
     "quantize_coeffs", "dequantize_coeffs",
     "png_filter", "png_reconstruct",

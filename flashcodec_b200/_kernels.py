@@ -169,6 +169,53 @@ def attn_status(device: torch.device) -> int:
     return 0 if ws is None else int(ws[:4].view(torch.int32).item())
 
 
+class StatusProbe:
+    """A copy of an attention status word in flight to pinned host memory.
+
+    0 means every decode-attention call on that stream's workspace since the
+    last reset produced valid output; a positive value is the launch number of
+    a call whose bounded wait gave up (its output is invalid)."""
+
+    def __init__(self, host: torch.Tensor, event: torch.cuda.Event | None):
+        self._host, self._event = host, event
+
+    def ready(self) -> bool:
+        """True once the copy has landed (never blocks)."""
+        return self._event is None or self._event.query()
+
+    def value(self) -> int:
+        """The status word (waits for the copy only, not for later work)."""
+        if self._event is not None:
+            self._event.synchronize()
+        return int(self._host[0])
+
+    def check(self) -> None:
+        """Raise FlashCodecError if a call gave up."""
+        v = self.value()
+        if v:
+            raise _lib.FlashCodecError(
+                _lib.FC_ECUDA, f"decode attention launch {v} gave up waiting for a staged "
+                "tile (bounded wait); its output is invalid")
+
+
+def attn_status_async(device: torch.device, reset: bool = False) -> StatusProbe:
+    """Queue a copy of the current stream's workspace status word to pinned
+    host memory, in stream order, without synchronising; reset=True clears the
+    word after the copy.  Poll the probe after a model step."""
+    stream = torch.cuda.current_stream(device)
+    ws = _workspaces.get((device.index, stream.cuda_stream))
+    host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    if ws is None:
+        return StatusProbe(host, None)
+    word = ws[:4].view(torch.int32)
+    host.copy_(word, non_blocking=True)
+    if reset:
+        word.zero_()
+    ev = torch.cuda.Event()
+    ev.record(stream)
+    return StatusProbe(host, ev)
+
+
 def set_attn_kernel(which: str) -> str:
     """Select the decode-attention kernel process-wide: "auto" (tensor cores
     whenever the archive allows, the default), "cuda-core" or "tensor-core".

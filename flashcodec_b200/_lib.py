@@ -21,9 +21,9 @@ FC_F32, FC_BF16, FC_F16, FC_I8 = 0, 1, 2, 3
 SYMBOLS = ("fc_version", "fc_last_error_string", "fc_jpeg_encode", "fc_jpeg_decode",
            "fc_png_encode", "fc_png_decode", "fc_decode_attn_workspace_size",
            "fc_decode_attn", "fc_decode_attn_png", "fc_decode_attn_noalloc",
-           "fc_gather_batch", "fc_rope_kv_append", "fc_decode_attn_masked",
+           "fc_decode_attn_noalloc_status", "fc_gather_batch", "fc_rope_kv_append", "fc_decode_attn_masked",
            "fc_set_attn_kernel",
-           "fc_selftest_bounded_wait")
+           "fc_selftest_bounded_wait", "fc_selftest_noalloc_wait")
 FC_ATTN_AUTO, FC_ATTN_CUDA_CORE, FC_ATTN_TENSOR_CORE = 0, 1, 2
 
 _I64, _I32, _P, _F32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float
@@ -71,6 +71,7 @@ _SIGS = {
                                 _I32, _I64,
                                 _P, _F32,
                                 _P, _I32, _I64, _I64, _P], _I32),
+    "fc_decode_attn_noalloc_status": ([_P, _I32, _P], _I32),
     "fc_gather_batch": ([_P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _I32),
     "fc_rope_kv_append": ([_P, _I64, _I64, _P, _I64, _I64, _I64,
                            _P, _I64, _I64, _P, _I64, _I64,
@@ -93,6 +94,7 @@ _SIGS = {
                                _P, _I64, _P], _I32),
     "fc_set_attn_kernel": ([_I32], _I32),
     "fc_selftest_bounded_wait": ([_P, _I32, _P], _I32),
+    "fc_selftest_noalloc_wait": ([_I32, _P], _I32),
 }
 
 _lock = threading.Lock()

@@ -101,3 +101,22 @@ def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="au
     K.decode_attn(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale, out,
                   vis=visible)
     return out
+
+
+def attention_status(device=None, reset=False):
+    """Failure status of the decode-attention calls issued on the current
+    stream of ``device``, without synchronising (an extension: the reference
+    kernels have no failure status).
+
+    Every wait inside the attention kernels is bounded; a call whose wait
+    gave up leaves invalid output and records its launch number in the
+    stream's workspace.  This queues a copy of that word to pinned host
+    memory and returns a probe: ``probe.ready()`` polls, ``probe.value()``
+    returns the word (0 = every call since the last reset was valid),
+    ``probe.check()`` raises if some call gave up.  ``reset=True`` clears the
+    word after the copy.  Typical use: take a probe after each decode step
+    and check the previous step's probe before using its tokens."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    return K.attn_status_async(dev, reset=reset)
+

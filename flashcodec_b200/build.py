@@ -51,12 +51,16 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     out = PKG / "_build"
     out.mkdir(exist_ok=True)
     objs = []
+    newest_header = max(p.stat().st_mtime for p in HEADERS)
     for src in SOURCES:
         obj = out / (src.stem + ".o")
-        cmd = [nvcc(), *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        subprocess.check_call(cmd)
+        fresh = (not force and obj.exists() and
+                 obj.stat().st_mtime >= max(src.stat().st_mtime, newest_header))
+        if not fresh:
+            cmd = [nvcc(), *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            subprocess.check_call(cmd)
         objs.append(str(obj))
     tmp = LIB.with_suffix(f".{os.getpid()}.tmp")
     subprocess.check_call([nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared",

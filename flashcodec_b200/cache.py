@@ -41,10 +41,10 @@ def make_codec(mode="jpeg", block_size=8, keep_freqs=2, keep_ratio=1.0,
                          quant_bits=quant_bits, scale_dtype=scale_dtype)
     if mode == "png":
         if quant_bits:
-            raise ValueError("quant_bits is only supported for mode='jpeg' "
-                             "(the png lossless tier must keep fp32 deltas)")
+            raise ValueError(f"quant_bits={quant_bits} applies to the jpeg codec only: png "
+                             "stores fp32 deltas, which is what makes it lossless")
         return PNGCodec(block_size=block_size, keep_ratio=keep_ratio)
-    raise ValueError(f"unknown mode: {mode!r} (expected 'jpeg' | 'png')")
+    raise ValueError(f"mode must be 'jpeg' or 'png', not {mode!r}")
 
 
 class _CodecStream:
@@ -366,12 +366,18 @@ def append_rotary(key_stream, value_stream, q, k, v, cos, sin):
 
 
 class CodecKVCache:
-    """Codec KV cache, multi-layer, duck-typed as a HuggingFace Cache
-    (flashcodec/cache.py:328-440).
+    """Compressed K and V streams for every layer of a model, with the
+    method names of a HuggingFace Cache (flashcodec/cache.py:328-440).
 
-        cache = CodecKVCache(mode="jpeg", block_size=8, keep_freqs=2)
-        k, v = cache.update(k_states, v_states, layer_idx=0)   # incremental
-        k, v = cache.forward(k_seq, v_seq, layer_idx=0)        # full sequence
+    ``update(k, v, layer_idx)`` appends new tokens of one layer and returns
+    that layer's reconstructed (K, V) views; ``append`` only appends (the
+    decode-attention path reads the archive directly); ``forward`` replaces a
+    layer's contents with a whole sequence.  All tensors are (B, H, S, D) on
+    one CUDA device, for example::
+
+        kv = CodecKVCache("jpeg", block_size=8, keep_freqs=4, quant_bits=8)
+        kv.append(k_prompt, v_prompt, layer_idx=3)
+        out = codec_decode_attention(q, kv._keys[3], kv._values[3])
     """
 
     def __init__(self, mode="jpeg", block_size=8, keep_freqs=2,
@@ -455,18 +461,21 @@ class CodecKVCache:
             sum(self._values[i].storage_bytes() for i in layers if i in self._values)
 
     def stats(self, layer_idx=0):
-        ks = self._keys.get(layer_idx)
-        if ks is None or ks.meta is None:
-            return {"tokens": 0, "archived": 0, "raw": 0, "storage_bytes": 0, "raw_bytes": 0}
-        B, H, D, elem = ks.meta
-        tokens = ks.seq_len
-        return {"tokens": tokens, "archived": ks.n_archived, "raw": tokens - ks.n_archived,
+        """Token counts and byte sizes of one layer: compressed storage
+        (archive plus raw tail, K and V) next to what the same tokens take
+        uncompressed in the stream dtype."""
+        st = self._keys.get(layer_idx)
+        if st is None or st.meta is None:
+            return dict.fromkeys(("tokens", "archived", "raw", "storage_bytes", "raw_bytes"), 0)
+        B, H, D, elem = st.meta
+        seq = st.seq_len
+        return {"tokens": seq, "archived": st.n_archived, "raw": seq - st.n_archived,
                 "storage_bytes": self.storage_bytes(layer_idx),
-                "raw_bytes": tokens * B * H * D * elem * 2}
+                "raw_bytes": 2 * seq * B * H * D * elem}
 
     def __repr__(self):
-        return (f"CodecKVCache(mode={self.mode!r}, codec={self.codec}, "
-                f"layers={sorted(set(self._keys) | set(self._values))})")
+        layers = sorted(set(self._keys) | set(self._values))
+        return f"CodecKVCache({self.codec!r} over {len(layers)} layer(s) {layers})"
 
 
 def __getattr__(name):

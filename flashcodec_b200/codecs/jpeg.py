@@ -158,10 +158,11 @@ class JPEGCodec:
 
     def __init__(self, block_size=8, keep_freqs=2, quant_bits=0, scale_dtype=torch.float32):
         assert 1 <= keep_freqs <= block_size, \
-            f"keep_freqs must be within [1, {block_size}]"
+            f"keep_freqs={keep_freqs} is outside 1..{block_size} (the block length)"
         assert quant_bits in (0, 8), \
-            f"quant_bits must be 0 (store in input dtype) or 8, got {quant_bits}"
-        assert scale_dtype in (torch.float32, torch.float16), "scale_dtype: float32 or float16"
+            f"quant_bits={quant_bits}: use 0 (coefficients kept in the input dtype) or 8 (int8)"
+        assert scale_dtype in (torch.float32, torch.float16), \
+            "scale_dtype must be torch.float32 or torch.float16"
         self.block_size = block_size
         self.keep_freqs = keep_freqs
         self.quant_bits = quant_bits
@@ -169,31 +170,36 @@ class JPEGCodec:
 
     @property
     def quantized(self):
+        """True when the archive holds int8 codes plus scales."""
         return self.quant_bits > 0
 
     def compress(self, x):
+        """(B, H, S, D) -> kept DCT coefficients (B, H, n, keep_freqs, D)."""
         return dct_compress(x, self.block_size, self.keep_freqs)
 
     def quantize(self, coeffs):
-        """Coefficients -> (int8, scale) when quantized, else (None, None)."""
-        if not self.quantized:
-            return None, None
-        return quantize_coeffs(coeffs, self.quant_bits)
+        """int8 codes and scales of ``coeffs`` for an int8 codec; (None, None)
+        for an unquantized one."""
+        if self.quantized:
+            return quantize_coeffs(coeffs, self.quant_bits)
+        return None, None
 
     def decompress(self, coeffs, out_len=None, scales=None):
+        """Coefficients (or int8 codes with their scales) -> (B, H, out_len, D)."""
         if self.quantized:
-            assert scales is not None, "quantized codec needs the scales"
+            assert scales is not None, "an int8 archive is decoded with its scales"
             coeffs = dequantize_coeffs(coeffs, scales)
         return dct_decompress(coeffs, self.block_size, out_len)
 
     def storage_ratio(self):
-        """Archive bytes / original bytes assuming fp32 input, excluding the
-        raw tail (jpeg.py:144-153): k/r, or k/r/4 when int8."""
-        if not self.quantized:
-            return self.keep_freqs / self.block_size
-        return (self.keep_freqs / self.block_size) / 4.0
+        """Archive size over an fp32 input of the same length, raw tail and
+        scale bytes left out (flashcodec/codecs/jpeg.py:144-153): the kept
+        fraction keep_freqs / block_size, a quarter of that for int8 codes."""
+        kept = self.keep_freqs / self.block_size
+        return kept / 4.0 if self.quantized else kept
 
     def __repr__(self):
-        q = f", quant_bits={self.quant_bits}" if self.quantized else ""
-        return (f"JPEGCodec(block_size={self.block_size}, "
-                f"keep_freqs={self.keep_freqs}{q})")
+        extra = "" if not self.quantized else f", quant_bits={self.quant_bits}"
+        if self.scale_dtype != torch.float32:
+            extra += ", scale_dtype=torch.float16"
+        return f"JPEGCodec(block_size={self.block_size}, keep_freqs={self.keep_freqs}{extra})"

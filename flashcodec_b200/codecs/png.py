@@ -119,29 +119,34 @@ def png_reconstruct(deltas, anchor):
 
 
 class PNGCodec:
-    """PNG-style prediction-filter codec (flashcodec/codecs/png.py:77-107)."""
+    """Lossless-tier delta codec (flashcodec/codecs/png.py:77-107): each block
+    keeps its first token as the anchor and the fp32 steps between neighbours,
+    of which the keep_ratio largest per channel survive."""
 
     name = "png"
 
     def __init__(self, block_size=8, keep_ratio=1.0):
-        assert 0 < keep_ratio <= 1.0, "keep_ratio must be within (0, 1]"
+        assert 0 < keep_ratio <= 1.0, f"keep_ratio={keep_ratio} must lie in (0, 1]"
         self.block_size = block_size
         self.keep_ratio = keep_ratio
 
     @property
     def keep_m(self):
+        """Deltas kept per (block, channel)."""
         return _keep_m(self.block_size, self.keep_ratio)
 
     def filter(self, x):
+        """(B, H, S, D) -> (fp32 deltas (B, H, n, r-1, D), anchors (B, H, n, D))."""
         return png_filter(x, self.block_size, self.keep_ratio)
 
     def reconstruct(self, deltas, anchor):
+        """Anchors plus running sums of the deltas -> (B, H, n*r, D)."""
         return png_reconstruct(deltas, anchor)
 
     def storage_ratio(self):
-        """Dense storage ratio: 1.0 for fp32 input (png.py:93-103)."""
+        """1.0: an anchor and r-1 fp32 steps take as many elements as the r
+        fp32 tokens they replace (png.py:93-103)."""
         return 1.0
 
     def __repr__(self):
-        return (f"PNGCodec(block_size={self.block_size}, "
-                f"keep_ratio={self.keep_ratio})")
+        return f"PNGCodec(block_size={self.block_size}, keep_ratio={self.keep_ratio})"

@@ -17,24 +17,28 @@ constexpr int kGatherThreads = 256;
 template <bool VEC16>
 __global__ void __launch_bounds__(kGatherThreads)
 gather_batch_kernel(const unsigned char *src, unsigned char *dst, const int64_t *idx,
-                    int64_t B_src, int64_t H, int64_t slab, int64_t s_sb, int64_t s_sh,
-                    int64_t d_sb, int64_t d_sh) {
-    // blockIdx.y = destination (b, h); blockIdx.x walks the slab
-    const int64_t bh = blockIdx.y;
-    const int64_t b = bh / H, h = bh % H;
-    const int64_t sb = idx[b];
-    if (sb < 0 || sb >= B_src) return;  // the host refuses such indices before launch
-    const unsigned char *s = src + sb * s_sb + h * s_sh;
-    unsigned char *d = dst + b * d_sb + h * d_sh;
-    if (VEC16) {
-        const int64_t n16 = slab / 16;
-        for (int64_t i = (int64_t)blockIdx.x * kGatherThreads + threadIdx.x; i < n16;
-             i += (int64_t)gridDim.x * kGatherThreads)
-            reinterpret_cast<uint4 *>(d)[i] = __ldcs(reinterpret_cast<const uint4 *>(s) + i);
-    } else {
-        for (int64_t i = (int64_t)blockIdx.x * kGatherThreads + threadIdx.x; i < slab;
-             i += (int64_t)gridDim.x * kGatherThreads)
-            d[i] = s[i];
+                    int64_t B_src, int64_t H, int64_t n_slabs, int per_slab, int64_t slab,
+                    int64_t s_sb, int64_t s_sh, int64_t d_sb, int64_t d_sh) {
+    // work item w = (destination slab (b, h), part of the slab); the grid
+    // strides over the items, so any number of (batch, head) slabs works
+    const int64_t items = n_slabs * per_slab;
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+        const int64_t bh = w / per_slab;
+        const int part = (int)(w - bh * per_slab);
+        const int64_t b = bh / H, h = bh - b * H;
+        const int64_t sb = idx[b];
+        if (sb < 0 || sb >= B_src) continue;  // the host refuses such indices before launch
+        const unsigned char *s = src + sb * s_sb + h * s_sh;
+        unsigned char *d = dst + b * d_sb + h * d_sh;
+        const int64_t stride = (int64_t)per_slab * kGatherThreads;
+        if (VEC16) {
+            const int64_t n16 = slab / 16;
+            for (int64_t i = (int64_t)part * kGatherThreads + threadIdx.x; i < n16; i += stride)
+                reinterpret_cast<uint4 *>(d)[i] = __ldcs(reinterpret_cast<const uint4 *>(s) + i);
+        } else {
+            for (int64_t i = (int64_t)part * kGatherThreads + threadIdx.x; i < slab; i += stride)
+                d[i] = s[i];
+        }
     }
 }
 
@@ -52,21 +56,25 @@ extern "C" int fc_gather_batch(const void *src, int64_t B_src, void *dst, int64_
     if (B == 0 || H == 0 || slab_bytes == 0) return FC_OK;
     if (!src || !dst || !idx) { set_error("gather_batch: null pointer"); return FC_EINVAL; }
     if (src == dst) { set_error("gather_batch: destination must not be the source"); return FC_EINVAL; }
-    if (B * H > 65535) { set_error("gather_batch: more than 65535 (batch, head) slabs"); return FC_ENOTSUP; }
     const bool v16 = slab_bytes % 16 == 0 && aligned(src, 16) && aligned(dst, 16) &&
                      src_sb % 16 == 0 && src_sh % 16 == 0 && dst_sb % 16 == 0 && dst_sh % 16 == 0;
     const int64_t units = v16 ? slab_bytes / 16 : slab_bytes;
-    // enough CTAs per slab to stream it at full width, at most 64
-    const int64_t per_slab = std::min<int64_t>(64, (units + kGatherThreads * 4 - 1) / (kGatherThreads * 4));
-    dim3 grid((unsigned)std::max<int64_t>(1, per_slab), (unsigned)(B * H));
+    // enough CTAs per slab to stream it at full width, at most 64; the grid
+    // covers every (slab, part) item once, capped at a few waves (the kernel
+    // strides over the rest)
+    const int per_slab = (int)std::min<int64_t>(
+        64, std::max<int64_t>(1, (units + kGatherThreads * 4 - 1) / (kGatherThreads * 4)));
+    const int64_t items = B * H * per_slab;
+    const int64_t cap = (int64_t)num_sms() * 32;
+    dim3 grid((unsigned)std::min<int64_t>(items, cap));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     auto s = static_cast<const unsigned char *>(src);
     auto d = static_cast<unsigned char *>(dst);
     if (v16)
-        gather_batch_kernel<true><<<grid, kGatherThreads, 0, st>>>(s, d, idx, B_src, H, slab_bytes,
-                                                                  src_sb, src_sh, dst_sb, dst_sh);
+        gather_batch_kernel<true><<<grid, kGatherThreads, 0, st>>>(
+            s, d, idx, B_src, H, B * H, per_slab, slab_bytes, src_sb, src_sh, dst_sb, dst_sh);
     else
-        gather_batch_kernel<false><<<grid, kGatherThreads, 0, st>>>(s, d, idx, B_src, H, slab_bytes,
-                                                                   src_sb, src_sh, dst_sb, dst_sh);
+        gather_batch_kernel<false><<<grid, kGatherThreads, 0, st>>>(
+            s, d, idx, B_src, H, B * H, per_slab, slab_bytes, src_sb, src_sh, dst_sb, dst_sh);
     return check_launch("gather_batch");
 }

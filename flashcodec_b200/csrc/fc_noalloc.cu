@@ -13,6 +13,14 @@
 // process exits.  In host code `g_attn_scratch` is only a stand-in symbol,
 // never a device address: the address is looked up with cudaGetSymbolAddress
 // once per device (the first call on that device, with it current) and cached.
+//
+// Layout of the scratch is the workspace layout of fc_decode_attn: a 256-byte
+// header whose first int32 is the status word, then the arrival counters,
+// then the split partials.  The status word is sticky: each call clears the
+// counters only, so a bounded wait that gave up in any call since the last
+// fc_decode_attn_noalloc_status(..., reset = 1) stays visible.
+#include <stdio.h>
+
 #include <mutex>
 
 #include "fc_common.cuh"
@@ -20,6 +28,7 @@
 namespace {
 
 constexpr size_t kScratchBytes = FC_NOALLOC_SCRATCH_BYTES;
+constexpr size_t kHeaderBytes = 256;  // the workspace header (status word first)
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_attn_scratch[kScratchBytes];
@@ -28,11 +37,11 @@ std::mutex g_mu;
 void *g_scratch_ptr[kMaxDevices] = {nullptr};
 
 // Device address of g_attn_scratch on the current device (looked up once).
-int scratch_address(void **out) {
+int scratch_address(void **out, const char *who) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-        fc::set_error("decode_attn_noalloc: no current CUDA device (%s)", cudaGetErrorString(e));
+        fc::set_error("%s: no current CUDA device (%s)", who, cudaGetErrorString(e));
         return FC_ECUDA;
     }
     std::lock_guard<std::mutex> lock(g_mu);
@@ -40,8 +49,8 @@ int scratch_address(void **out) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_attn_scratch);
         if (e != cudaSuccess || p == nullptr) {
-            fc::set_error("decode_attn_noalloc: cudaGetSymbolAddress failed on device %d (%s)",
-                          dev, cudaGetErrorString(e));
+            fc::set_error("%s: cudaGetSymbolAddress failed on device %d (%s)", who, dev,
+                          cudaGetErrorString(e));
             return FC_ECUDA;
         }
         g_scratch_ptr[dev] = p;
@@ -70,35 +79,77 @@ extern "C" int fc_decode_attn_noalloc(
                               scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh,
                               vr_st, raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb,
                               o_sh, nullptr, 0, stream);  // argument errors, reported as usual
-    const size_t need = fc_decode_attn_workspace_size(B, Hq, Hk, D, n_blocks, s, r, n_raw);
-    if (need > kScratchBytes) {
+    // The arrival counters (one int32 per (batch, KV head, head group) unit of
+    // either kernel) follow the header and must start at zero; the partials
+    // are written before they are read.  If the counters alone do not fit,
+    // nothing is cleared and the call is refused here.
+    const int64_t groups = (Hq / Hk + 7) / 8;
+    const size_t counters = (((size_t)(B * Hk * groups) * 4 + 255) / 256) * 256;
+    if (counters > kScratchBytes - kHeaderBytes) {
         fc::set_error(
-            "decode_attn_noalloc: this call needs %zu bytes of scratch but the fixed scratch "
-            "holds %zu (FC_NOALLOC_SCRATCH_BYTES); use fc_decode_attn with a workspace",
-            need, kScratchBytes);
+            "decode_attn_noalloc: %lld (batch, KV head) units need more than the fixed scratch "
+            "of %zu bytes (FC_NOALLOC_SCRATCH_BYTES); use fc_decode_attn with a workspace",
+            (long long)(B * Hk), kScratchBytes);
         return FC_ERANGE;
     }
     void *ws = nullptr;
-    int rc = scratch_address(&ws);
+    int rc = scratch_address(&ws, "decode_attn_noalloc");
     if (rc != FC_OK) return rc;
-    // The status word and the per-(batch, KV head, head group) arrival
-    // counters must start at zero; the partials are written before they are
-    // read.  Clearing them here also forgets whatever an earlier call (or an
-    // aborted one) left behind.
-    const int64_t groups = (Hq / Hk + 7) / 8;
-    size_t clear = 256 + (((size_t)(B * Hk * groups) * 4 + 255) / 256) * 256;
-    if (clear > need) clear = need;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(ws, 0, clear, st);
+    // Clearing the counters also forgets whatever an aborted call left there;
+    // the status word in the header is left as it is (sticky until read).
+    cudaError_t e = cudaMemsetAsync(static_cast<unsigned char *>(ws) + kHeaderBytes, 0,
+                                    counters, st);
     if (e != cudaSuccess) {
         fc::set_error("decode_attn_noalloc: clearing the scratch counters failed (%s)",
                       cudaGetErrorString(e));
         return FC_ECUDA;
     }
-    return fc_decode_attn(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype,
-                          k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj,
-                          k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn,
-                          scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st,
-                          raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh, ws,
-                          kScratchBytes, stream);
+    // fc_decode_attn sizes the plan it will actually run against the scratch
+    // and refuses it (FC_ERANGE) if it needs more.
+    rc = fc_decode_attn(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype,
+                        k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj,
+                        k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn,
+                        scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st,
+                        raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh, ws,
+                        kScratchBytes, stream);
+    if (rc == FC_ERANGE) {
+        char msg[384];
+        snprintf(msg, sizeof(msg), "%s", fc_last_error_string());
+        fc::set_error("decode_attn_noalloc: the plan does not fit the fixed scratch of %zu bytes "
+                      "(FC_NOALLOC_SCRATCH_BYTES); use fc_decode_attn with a workspace [%s]",
+                      kScratchBytes, msg);
+    }
+    return rc;
+}
+
+extern "C" int fc_decode_attn_noalloc_status(int *status, int reset, void *stream) {
+    fc::clear_error();
+    if (!status) {
+        fc::set_error("decode_attn_noalloc_status: null destination");
+        return FC_EINVAL;
+    }
+    void *ws = nullptr;
+    int rc = scratch_address(&ws, "decode_attn_noalloc_status");
+    if (rc != FC_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(status, ws, sizeof(int), cudaMemcpyDefault, st);
+    if (e == cudaSuccess && reset) e = cudaMemsetAsync(ws, 0, sizeof(int), st);
+    if (e != cudaSuccess) {
+        fc::set_error("decode_attn_noalloc_status: %s", cudaGetErrorString(e));
+        return FC_ECUDA;
+    }
+    return FC_OK;
+}
+
+extern "C" int fc_selftest_noalloc_wait(int epoch, void *stream) {
+    fc::clear_error();
+    if (epoch <= 0) {
+        fc::set_error("selftest_noalloc_wait: epoch <= 0");
+        return FC_EINVAL;
+    }
+    void *ws = nullptr;
+    int rc = scratch_address(&ws, "selftest_noalloc_wait");
+    if (rc != FC_OK) return rc;
+    return fc_selftest_bounded_wait(static_cast<int *>(ws), epoch, stream);
 }

@@ -16,6 +16,8 @@
 //
 // Work: one warp per row (a q, k or v head of one sequence); lane l handles
 // the pairs (d, d + D/2) for d = l, l + 32, ...
+#include <algorithm>
+
 #include "fc_common.cuh"
 
 namespace fc {
@@ -115,9 +117,44 @@ extern "C" int fc_rope_kv_append(const void *q, int64_t q_sb, int64_t q_sh, void
         set_error("rope_kv_append: null pointer");
         return FC_EINVAL;
     }
-    if (q_out == q || k_out == k || (v && v_out == v)) {
-        set_error("rope_kv_append: outputs must not alias their inputs");
-        return FC_EINVAL;
+    // Byte ranges [lo, hi) covered by each (B, H, D) operand; an output that
+    // shares a byte with any input or with another output would race (other
+    // warps may still read x[d + D/2] or a neighbouring row), so it is refused.
+    {
+        const int64_t es = dtype_size(dtype);
+        struct Span { uintptr_t lo, hi; };
+        auto span = [&](const void *p, int64_t H, int64_t sb, int64_t sh) {
+            const int64_t a = (B - 1) * sb, b = (H - 1) * sh;
+            const int64_t lo = std::min<int64_t>(0, a) + std::min<int64_t>(0, b);
+            const int64_t hi = std::max<int64_t>(0, a) + std::max<int64_t>(0, b) + D;
+            const uintptr_t base = reinterpret_cast<uintptr_t>(p);
+            return Span{base + (uintptr_t)(lo * es), base + (uintptr_t)(hi * es)};
+        };
+        const int64_t cs_rows = cs_sb ? B : 1;
+        auto cspan = [&](const void *p) {
+            const uintptr_t base = reinterpret_cast<uintptr_t>(p);
+            return Span{base, base + (uintptr_t)(((cs_rows - 1) * cs_sb + D) * es)};
+        };
+        Span ins[5], outs[3];
+        int ni = 0, no = 0;
+        if (Hq) { ins[ni++] = span(q, Hq, q_sb, q_sh); outs[no++] = span(q_out, Hq, qo_sb, qo_sh); }
+        if (Hk) { ins[ni++] = span(k, Hk, k_sb, k_sh); outs[no++] = span(k_out, Hk, ko_sb, ko_sh); }
+        if (Hk && v) { ins[ni++] = span(v, Hk, v_sb, v_sh); outs[no++] = span(v_out, Hk, vo_sb, vo_sh); }
+        ins[ni++] = cspan(cos);
+        ins[ni++] = cspan(sin);
+        auto meet = [](Span x, Span y) { return x.lo < y.hi && y.lo < x.hi; };
+        for (int o = 0; o < no; ++o) {
+            for (int i = 0; i < ni; ++i)
+                if (meet(outs[o], ins[i])) {
+                    set_error("rope_kv_append: an output overlaps an input");
+                    return FC_EINVAL;
+                }
+            for (int o2 = o + 1; o2 < no; ++o2)
+                if (meet(outs[o], outs[o2])) {
+                    set_error("rope_kv_append: two outputs overlap");
+                    return FC_EINVAL;
+                }
+        }
     }
     const int64_t blocks = (rows + kRopeRows - 1) / kRopeRows;
     if (blocks > 0x7fffffff) { set_error("rope_kv_append: too many rows"); return FC_ENOTSUP; }

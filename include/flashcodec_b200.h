@@ -226,14 +226,20 @@ FC_API int fc_decode_attn_png(const void *q, int q_dtype, int64_t B, int64_t Hq,
  * library's kernels until the process exits.
  *
  * - Calls whose plan needs more scratch than that return FC_ERANGE (use
- *   fc_decode_attn with a workspace); fc_decode_attn_workspace_size tells the
- *   size in advance.
+ *   fc_decode_attn with a workspace).  The check is made against the plan
+ *   this call runs; fc_decode_attn_workspace_size gives an upper bound of it
+ *   in advance (the largest plan over row types and kernels).
  * - The first call on a device looks up the scratch address on that device
  *   (cudaGetSymbolAddress, with the device current); make that first call
  *   before any stream capture.
- * - Each call clears the scratch counters (cudaMemsetAsync on `stream`) and
- *   then launches the attention kernel; no cudaMalloc, cudaFree or other
- *   allocating call is made.
+ * - Each call clears the scratch's arrival counters (cudaMemsetAsync on
+ *   `stream`) and then launches the attention kernel; no cudaMalloc, cudaFree
+ *   or other allocating call is made.
+ * - The scratch's status word (as in the workspace of fc_decode_attn) is NOT
+ *   cleared by the calls: once a bounded wait of some call gave up, it holds
+ *   that call's positive launch number until fc_decode_attn_noalloc_status
+ *   reads it with reset = 1.  Read it after a step to learn whether every
+ *   output of the step is valid.
  * - All calls on a device share one scratch array: calls that can overlap on
  *   the GPU (different streams, or host threads without ordering) race and
  *   must not be issued that way.
@@ -253,6 +259,44 @@ FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t
                    const float *A, float softmax_scale,
                    void *out, int out_dtype, int64_t o_sb, int64_t o_sh, void *stream);
 
+/* Status word of fc_decode_attn_noalloc's scratch on the current device,
+ * copied to *status (device memory, or host memory the copy engine can reach;
+ * pinned host memory keeps the call asynchronous) in order on `stream`:
+ * 0 = every no-alloc call since the last reset produced valid output,
+ * > 0 = the launch number of a call whose bounded wait gave up.  reset != 0
+ * clears the word after the copy (also in stream order).  Allocates nothing.
+ * No counterpart in the reference (it has no failure status). */
+FC_API int fc_decode_attn_noalloc_status(int *status, int reset, void *stream);
+
+/* One entry of fc_append_tokens' stream table: one K or V stream of one layer. */
+typedef struct fc_append_stream {
+    const void *token;       /* (B, H, D) new token, element strides token_sb, token_sh */
+    int64_t token_sb, token_sh;
+    void *raw;               /* (B, H, r, D) raw-tail buffer, contiguous */
+    void *codes;             /* (B, H, capacity, k, D) archive, contiguous: int8 codes when
+                                `scales` is non-NULL, else coefficients of the token dtype */
+    void *scales;            /* (B, H, capacity, k) scales of scale_dtype, or NULL */
+    int64_t capacity;        /* archive capacity in blocks */
+} fc_append_stream;
+
+/* Append one token to many jpeg streams in one launch: replaces the
+ * per-layer, per-stream _CodecStream.append (flashcodec/cache.py:143-159) of
+ * a decode step, and the _archive (cache.py:123-141) of every block that
+ * token completes (dct_compress + quantize_coeffs, codecs/jpeg.py:55-100).
+ * Every stream shares dtype (f32/bf16/f16), B, H, D (a multiple of 4, at
+ * most 512), block length r <= 64, k <= 8 kept frequencies, and the raw slot
+ * `slot` (0 .. r-1) the token goes to.  When slot == r - 1 the completed
+ * block -- raw rows 0 .. r-2 and the new token -- is written to archive
+ * block `block` (< capacity) of every stream, bit-identical to
+ * fc_jpeg_encode; `err` (optional device int) is set when an F16 scale
+ * cannot hold its value.  The table is read on the host and passed to the
+ * kernel by value (no device table); streams must not share buffers.
+ * No counterpart in the reference beyond the per-stream calls it fuses. */
+FC_API int fc_append_tokens(const fc_append_stream *streams, int n_streams, int dtype,
+                            int64_t B, int64_t H, int64_t D, int r, int k, int64_t slot,
+                            int64_t block, const float *basis, int scale_dtype, int *err,
+                            void *stream);
+
 /* Batch gather for beam-search reordering: replaces the index_select +
  * copy-back of every stream tensor in _CodecStream.select_batch
  * (flashcodec/cache.py:259-301).  For each destination (b, h) in B x H, copies
@@ -260,7 +304,8 @@ FC_API int fc_decode_attn_noalloc(const void *q, int q_dtype, int64_t B, int64_t
  * dst + b*dst_sb + h*dst_sh (strides in bytes; a slab is the live prefix of
  * one (batch, head) row of an archive, reconstruction or raw-tail tensor).
  * idx: B device int64 values in [0, B_src) (the caller checks them; the kernel
- * skips any outside); dst must not overlap src; B * H <= 65535. */
+ * skips any outside); dst must not overlap src.  Any number of (batch, head)
+ * slabs: the grid strides over them. */
 FC_API int fc_gather_batch(const void *src, int64_t B_src, void *dst, int64_t B, int64_t H,
                            int64_t slab_bytes, int64_t src_sb, int64_t src_sh,
                            int64_t dst_sb, int64_t dst_sh, const int64_t *idx, void *stream);
@@ -275,8 +320,9 @@ FC_API int fc_gather_batch(const void *src, int64_t B_src, void *dst, int64_t B,
  * tensors have element type `dtype` (fp32, bf16 or fp16) and unit stride
  * along D; strides are in elements.  Each product and the sum are rounded to
  * `dtype` as torch's elementwise ops round them, so the result is
- * bit-identical to the unfused expression.  Outputs must not alias inputs;
- * D must be even. */
+ * bit-identical to the unfused expression.  No output may overlap an input
+ * or another output (byte ranges spanned by the shapes and strides are
+ * checked; FC_EINVAL otherwise); D must be even. */
 FC_API int fc_rope_kv_append(const void *q, int64_t q_sb, int64_t q_sh, void *q_out,
                              int64_t qo_sb, int64_t qo_sh, int64_t Hq,
                              const void *k, int64_t k_sb, int64_t k_sh, void *k_out,
@@ -333,6 +379,12 @@ FC_API int fc_set_attn_kernel(int which);
  * usable.  Returns FC_OK when the launch was issued.  No counterpart in the
  * reference. */
 FC_API int fc_selftest_bounded_wait(int *status, int epoch, void *stream);
+
+/* The same self-test aimed at the status word of fc_decode_attn_noalloc's
+ * scratch on the current device (whose address callers never see), so that
+ * fc_decode_attn_noalloc_status can be shown to report a wait that gave up.
+ * No counterpart in the reference. */
+FC_API int fc_selftest_noalloc_wait(int epoch, void *stream);
 
 #ifdef __cplusplus
 }

@@ -274,3 +274,54 @@ def reference_attention_int8(q, kcodes, kscales, vcodes, vscales, kraw, vraw, A,
     krows = kcodes.astype(np.float32) * kscales
     vrows = vcodes.astype(np.float32) * vscales
     return reference_attention_fp32(q, krows, vrows, kraw, vraw, A, scale)
+
+
+def reference_attention_int8_mt(q, kcodes, kscales, vcodes, vscales, kraw, vraw, A,
+                                scale=None, threads=None, chunk_blocks=512):
+    """reference_attention_int8 spread over host threads: the same operation
+    sequence (fp32 dequantize of the codes, q . rows, expansion through A,
+    fp32 softmax over all keys, weights folded back through A, weighted sum of
+    the V rows) on (sequence, KV head, block chunk) tiles, so that the timed
+    CPU baseline uses every core as the reference's torch path does
+    (flashcodec/attention.py:101-140 runs on torch's intra-op thread pool).
+    numpy releases the GIL inside these array operations."""
+    from concurrent.futures import ThreadPoolExecutor
+    B, Hq, _, D = q.shape
+    scale = D ** -0.5 if scale is None else scale
+    Hk, n, s = kcodes.shape[1], kcodes.shape[2], kcodes.shape[3]
+    r = A.shape[0]
+    G = Hq // Hk
+    t = 0 if kraw is None else kraw.shape[2]
+    qg = np.ascontiguousarray(q.reshape(B, Hk, G, D), dtype=np.float32)
+    A32 = np.ascontiguousarray(A, dtype=np.float32)
+    tiles = [(b, h, c0, min(n, c0 + chunk_blocks)) for b in range(B) for h in range(Hk)
+             for c0 in range(0, n, chunk_blocks)]
+    logits = np.empty((B, Hk, G, n * r + t), np.float32)
+    out = np.zeros((B, Hk, G, D), np.float32)
+    partial = {}
+
+    def k_tile(tile):
+        b, h, c0, c1 = tile
+        rows = kcodes[b, h, c0:c1].astype(np.float32) * kscales[b, h, c0:c1]
+        sc = (qg[b, h] @ rows.reshape(-1, D).T).reshape(G, c1 - c0, s)
+        logits[b, h, :, c0 * r:c1 * r] = (sc @ A32.T).reshape(G, -1) * np.float32(scale)
+
+    def v_tile(tile):
+        b, h, c0, c1 = tile
+        rows = vcodes[b, h, c0:c1].astype(np.float32) * vscales[b, h, c0:c1]
+        w = logits[b, h, :, c0 * r:c1 * r].reshape(G, c1 - c0, r) @ A32
+        partial[tile] = w.reshape(G, -1) @ rows.reshape(-1, D)
+
+    with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as ex:
+        list(ex.map(k_tile, tiles))
+        if t:
+            logits[..., n * r:] = np.einsum("bhgd,bhtd->bhgt", qg, kraw) * np.float32(scale)
+        logits -= logits.max(axis=-1, keepdims=True)
+        np.exp(logits, out=logits)
+        logits /= logits.sum(axis=-1, keepdims=True)
+        list(ex.map(v_tile, tiles))
+    for (b, h, _, _), part in partial.items():
+        out[b, h] += part
+    if t:
+        out += np.einsum("bhgt,bhtd->bhgd", logits[..., n * r:], vraw)
+    return out.reshape(B, Hq, 1, D)

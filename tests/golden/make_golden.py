@@ -31,7 +31,10 @@ import numpy as np
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "tests" / "golden"))
-sys.path.insert(0, os.environ.get("FLASHCODEC_REF", "/root/reference"))
+if "FLASHCODEC_REF" not in os.environ:
+    raise SystemExit("set FLASHCODEC_REF to the flashcodec source tree (the directory that "
+                     "holds the flashcodec package) to regenerate the fixtures")
+sys.path.insert(0, os.environ["FLASHCODEC_REF"])
 
 import cases  # noqa: E402
 from cases import f32, sha  # noqa: E402

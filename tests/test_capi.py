@@ -125,11 +125,14 @@ def test_new_entry_points_validate_on_the_host(lib):
     # self-test: null status, epoch <= 0
     assert lib.fc_selftest_bounded_wait(None, 1, None) == _lib.FC_EINVAL
     assert lib.fc_selftest_bounded_wait(d, 0, None) == _lib.FC_EINVAL
+    # no-alloc status and its self-test: null destination, epoch <= 0
+    assert lib.fc_decode_attn_noalloc_status(None, 1, None) == _lib.FC_EINVAL
+    assert lib.fc_selftest_noalloc_wait(0, None) == _lib.FC_EINVAL
 
 
 def test_rope_kv_append_validates_on_the_host(lib):
     """fc_rope_kv_append refuses odd head dims, integer dtypes, a v without
-    v_out and aliased outputs before any CUDA call; empty work is a no-op."""
+    v_out and outputs overlapping an input or each other before any CUDA call; empty work is a no-op."""
     from flashcodec_b200 import _lib
     P = ctypes.c_void_p
     q, qo, k, ko, v, vo, c, s = (P(0x1000 * (i + 1)) for i in range(8))
@@ -143,6 +146,9 @@ def test_rope_kv_append_validates_on_the_host(lib):
     assert call(dt=_lib.FC_I8) == _lib.FC_EINVAL
     assert call(v_out=None) == _lib.FC_EINVAL
     assert call(q_out=q) == _lib.FC_EINVAL
+    assert call(q_out=P(0x1000 + 128)) == _lib.FC_EINVAL     # partial overlap with q
+    assert b"overlap" in lib.fc_last_error_string()
+    assert call(v_out=P(0x4000 + 64)) == _lib.FC_EINVAL      # v_out inside k_out's rows
     assert call(B=-1) == _lib.FC_EINVAL
     assert call(B=0) == _lib.FC_OK
 

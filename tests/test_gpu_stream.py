@@ -236,3 +236,20 @@ def test_reorder_gathers_archive_bitwise_and_checks_indices():
         with pytest.raises(IndexError):
             c.reorder_cache(torch.tensor([0, 7]))
         assert ks.raw.shape[0] == 4
+
+
+def test_gather_batch_more_than_65535_slabs():
+    """fc_gather_batch strides its grid over the (batch, head) slabs, so a
+    beam batch with more than 65,535 of them (e.g. 256 sequences x 8 beams x
+    32 KV heads) is reordered like any other."""
+    from flashcodec_b200 import _kernels as K
+    g = torch.Generator(device=DEV).manual_seed(9)
+    src = torch.randint(-128, 127, (6, 20000, 3, 16), dtype=torch.int8, device=DEV, generator=g)
+    idx = torch.tensor([5, 0, 0, 3], dtype=torch.int64, device=DEV)
+    for live in (2, 3):            # 32-byte (vector) and 48-byte slabs
+        dst = K.gather_batch(src, idx, live)
+        assert dst.shape == (4, 20000, 3, 16)
+        assert torch.equal(dst[:, :, :live], src.index_select(0, idx)[:, :, :live])
+    odd = src[..., :5].contiguous()  # 5-byte rows: the byte-copy kernel
+    dst = K.gather_batch(odd, idx, 3)
+    assert torch.equal(dst, odd.index_select(0, idx))
