@@ -536,7 +536,11 @@ def run_stream(args):
     layer per step; each step also reads layer 0's view incrementally.
     Timed over 256-step windows at the start (from an empty cache) and at the
     end of the 65536-token range (after a bulk prefill to 65280 tokens), with
-    CUDA events around every step (host launch overhead included)."""
+    CUDA events around every step (host launch overhead included).  Three
+    ways to append the step's 56 tokens: one fc_append_tokens launch for all
+    layers (CodecKVCache.append_layers, the headline of this line), one launch
+    per layer (CodecKVCache.append), and one append per stream (the stream's
+    own append: a copy per token plus an archive launch per completed block)."""
     import flashcodec_b200 as fc
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -544,8 +548,21 @@ def run_stream(args):
     g = torch.Generator(device=dev).manual_seed(4)
     toks = [(torch.randn(B, H, 1, D, generator=g, device=dev).to(torch.bfloat16),
              torch.randn(B, H, 1, D, generator=g, device=dev).to(torch.bfloat16)) for _ in range(L)]
+    kt, vt = [k for k, _ in toks], [v for _, v in toks]
 
-    def window(cache, steps):
+    def step_all(cache):
+        cache.append_layers(kt, vt)
+
+    def step_layer(cache):
+        for i in range(L):
+            cache.append(kt[i], vt[i], i)
+
+    def step_stream(cache):
+        for i in range(L):
+            cache._keys[i].append(kt[i])
+            cache._values[i].append(vt[i])
+
+    def window(cache, steps, fn):
         stream = torch.cuda.current_stream(dev)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(steps)]
@@ -553,8 +570,7 @@ def run_stream(args):
         t0 = time.perf_counter()
         for a, b in ev:
             a.record(stream)
-            for i in range(L):
-                cache.append(toks[i][0], toks[i][1], i)
+            fn(cache)
             cache._keys[0].read()
             b.record(stream)
         torch.cuda.synchronize()
@@ -562,37 +578,47 @@ def run_stream(args):
         return statistics.mean(a.elapsed_time(b) for a, b in ev), wall
 
     def new_cache():
-        return fc.CodecKVCache("jpeg", block_size=8, keep_freqs=2, quant_bits=8)
+        c = fc.CodecKVCache("jpeg", block_size=8, keep_freqs=2, quant_bits=8)
+        for i in range(L):  # first token: allocate the streams
+            c.append(kt[i], vt[i], i)
+        return c
 
-    c0 = new_cache()
-    for i in range(L):  # first token: allocate the streams
-        c0.append(toks[i][0], toks[i][1], i)
-    window(c0, 8)       # warm-up (kernels loaded, first archive)
-    del c0
-    c1 = new_cache()
-    start_ms, start_wall = window(c1, W)
-    del c1
+    modes = (("one launch per step", step_all), ("one launch per layer", step_layer),
+             ("one append per stream", step_stream))
+    res = {}
+    for name, fn in modes:
+        c0 = new_cache()
+        window(c0, 16, fn)           # warm-up (kernels loaded, first archives)
+        del c0
+        c1 = new_cache()
+        res[name] = {"start": window(c1, W, fn)}
+        del c1
     torch.cuda.empty_cache()
-    c2 = new_cache()
-    S_pre = S_end - W
+    c2 = fc.CodecKVCache("jpeg", block_size=8, keep_freqs=2, quant_bits=8)
+    S_pre = S_end - W * len(modes)
     for i in range(L):
         k = synth_stream(B, H, S_pre, D, 0.95, 2 * i, device=dev, dtype=torch.bfloat16)
         c2.append(k, k, i)  # value content does not change the work
         del k
     c2._keys[0].read()
-    end_ms, end_wall = window(c2, W)
+    for name, fn in modes:
+        res[name]["end"] = window(c2, W, fn)
+    head = res["one launch per step"]
+    end_ms = head["end"][0]
+    detail = {name: {"window_start_ms_per_step": v["start"][0],
+                     "window_start_wall_ms_per_step": v["start"][1],
+                     "window_end_ms_per_step": v["end"][0],
+                     "window_end_wall_ms_per_step": v["end"][1]} for name, v in res.items()}
     line = {"metric": "config 4 streaming step (append 28 layers + incremental read of one layer)",
-            "value": end_ms, "unit": "ms/step", "n_gpus": 1, "steps": W, "warmup": 8,
+            "value": end_ms, "unit": "ms/step", "n_gpus": 1, "steps": W, "warmup": 16,
             "ms_per_step": end_ms, "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "config 4: Qwen3-0.6B-shaped streaming append/archive",
                        "layers": L, "batch": B, "Hkv": H, "head_dim": D,
                        "codec": "jpeg r=8 K=2 int8, fp32 scales",
-                       "window_start": {"context": [0, W], "ms_per_step": start_ms,
-                                        "wall_ms_per_step": start_wall},
-                       "window_end": {"context": [S_pre, S_end], "ms_per_step": end_ms,
-                                      "wall_ms_per_step": end_wall},
+                       "windows": {"start": [0, W], "end": [S_end - W, S_end]},
                        "timing": "CUDA events around each step on the current stream"},
+            "append_modes": detail,
             "gpu_launches": None}
     print(json.dumps(line), flush=True)
 

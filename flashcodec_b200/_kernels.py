@@ -409,3 +409,75 @@ def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
     if rc != _lib.FC_OK:
         reset_workspace(q.device)
     _lib.check(rc, "decode_attn")
+
+
+# ------------------------------------------------------------ one-launch append
+def append_tokens(table, n: int, dtype: torch.dtype, B: int, H: int, D: int, r: int, k: int,
+                  slot: int, block: int, basis: torch.Tensor | None, scale_dtype,
+                  device: torch.device) -> None:
+    """fc_append_tokens over the first n entries of a ctypes AppendStream
+    array (one entry per K or V stream; the caller fills it)."""
+    sd = DTYPE_CODE.get(scale_dtype, 0) if scale_dtype is not None else 0
+    with torch.cuda.device(device):
+        rc = _lib.load().fc_append_tokens(
+            ctypes.cast(table, ctypes.c_void_p), n, DTYPE_CODE[dtype], B, H, D, r, k, slot,
+            block, _p(basis), sd, _stream(device))
+    _lib.check(rc, "append_tokens")
+
+
+# ------------------------------------------------------- per-group scale format
+def jpeg_encode_grouped(x: torch.Tensor, basis: torch.Tensor, r: int, k: int, out: torch.Tensor,
+                        scales: torch.Tensor, group: int, err: torch.Tensor | None = None) -> None:
+    """x (B,H,S,D) -> int8 codes out (B,H,n,k,D) with one scale per `group`
+    channels, scales (B,H,n,k,D//group) (fc_jpeg_encode_grouped)."""
+    require_cuda(x, basis, out, scales)
+    _unit_last(x, out, scales)
+    B, H, S, D = x.shape
+    with torch.cuda.device(x.device):
+        rc = _lib.load().fc_jpeg_encode_grouped(
+            _p(x), dtype_code(x), B, H, S, D, *_s(x, 0, 1, 2), _p(basis), r, k,
+            _p(out), *_s(out, 0, 1, 2, 3), _p(scales), dtype_code(scales), int(group),
+            *_s(scales, 0, 1, 2, 3), _p(err), _stream(x.device))
+    _lib.check(rc, "jpeg_encode_grouped")
+
+
+def jpeg_decode_grouped(codes: torch.Tensor, scales: torch.Tensor, group: int,
+                        basis: torch.Tensor, r: int, out: torch.Tensor, out_len: int) -> None:
+    """int8 codes (B,H,n,k,D) + scales (B,H,n,k,D//group) -> out (B,H,>=out_len,D)."""
+    require_cuda(codes, scales, basis, out)
+    _unit_last(codes, scales, out)
+    B, H, n, k, D = codes.shape
+    with torch.cuda.device(codes.device):
+        rc = _lib.load().fc_jpeg_decode_grouped(
+            _p(codes), B, H, n, D, k, *_s(codes, 0, 1, 2, 3), _p(scales), dtype_code(scales),
+            int(group), *_s(scales, 0, 1, 2, 3), _p(basis), r, _p(out), dtype_code(out),
+            out_len, *_s(out, 0, 1, 2), _stream(codes.device))
+    _lib.check(rc, "jpeg_decode_grouped")
+
+
+def decode_attn_grouped(q, krows, vrows, kscales, vscales, group, kraw, vraw, A, scale,
+                        out) -> None:
+    """decode_attn over int8 codes (B,Hk,n,s,D) whose scales are
+    (B,Hk,n,s,D//group) (fc_decode_attn_grouped)."""
+    require_cuda(q, krows, vrows, kscales, vscales, kraw, vraw, A, out)
+    _unit_last(krows, vrows, kscales, vscales)
+    B, Hq, _, D = q.shape
+    Hk, n, s = krows.shape[1], krows.shape[2], krows.shape[3]
+    r = A.shape[0]
+    t = kraw.shape[2] if kraw is not None else 0
+    ws = workspace(q.device, attn_workspace_bytes(B, Hq, Hk, D, n, s, r, t))
+    z3 = (0, 0, 0)
+    with torch.cuda.device(q.device):
+        rc = _lib.load().fc_decode_attn_grouped(
+            _p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1), Hk, n, s, r,
+            _p(krows), *_s(krows, 0, 1, 2, 3), _p(vrows), *_s(vrows, 0, 1, 2, 3),
+            _p(kscales), *_s(kscales, 0, 1, 2, 3), _p(vscales), *_s(vscales, 0, 1, 2, 3),
+            dtype_code(kscales), int(group),
+            _p(kraw), *(_s(kraw, 0, 1, 2) if kraw is not None else z3),
+            _p(vraw), *(_s(vraw, 0, 1, 2) if vraw is not None else z3),
+            dtype_code(kraw) if kraw is not None else 0, t,
+            _p(A), float(scale), _p(out), dtype_code(out), out.stride(0), out.stride(1),
+            _p(ws), ws.numel(), _stream(q.device))
+    if rc != _lib.FC_OK:
+        reset_workspace(q.device)
+    _lib.check(rc, "decode_attn_grouped")

@@ -19,14 +19,23 @@ FC_F32, FC_BF16, FC_F16, FC_I8 = 0, 1, 2, 3
 
 # exported symbols, in header order (tests check the library exports them all)
 SYMBOLS = ("fc_version", "fc_last_error_string", "fc_jpeg_encode", "fc_jpeg_decode",
-           "fc_png_encode", "fc_png_decode", "fc_decode_attn_workspace_size",
-           "fc_decode_attn", "fc_decode_attn_png", "fc_decode_attn_noalloc",
-           "fc_decode_attn_noalloc_status", "fc_gather_batch", "fc_rope_kv_append", "fc_decode_attn_masked",
+           "fc_jpeg_encode_grouped", "fc_jpeg_decode_grouped", "fc_png_encode", "fc_png_decode", "fc_decode_attn_workspace_size",
+           "fc_decode_attn", "fc_decode_attn_grouped", "fc_decode_attn_png",
+           "fc_decode_attn_noalloc",
+           "fc_decode_attn_noalloc_status", "fc_append_tokens", "fc_gather_batch", "fc_rope_kv_append", "fc_decode_attn_masked",
            "fc_set_attn_kernel",
            "fc_selftest_bounded_wait", "fc_selftest_noalloc_wait")
 FC_ATTN_AUTO, FC_ATTN_CUDA_CORE, FC_ATTN_TENSOR_CORE = 0, 1, 2
 
 _I64, _I32, _P, _F32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float
+
+
+class AppendStream(ctypes.Structure):
+    """fc_append_stream: one K or V stream of one layer in fc_append_tokens."""
+    _fields_ = [("token", _P), ("token_sb", _I64), ("token_sh", _I64), ("raw", _P),
+                ("codes", _P), ("scales", _P), ("capacity", _I64), ("err", _P)]
+
+
 _SIGS = {
     "fc_version": ([], ctypes.c_char_p),
     "fc_last_error_string": ([], ctypes.c_char_p),
@@ -35,6 +44,12 @@ _SIGS = {
     "fc_jpeg_decode": ([_P, _I32, _I64, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _I64,
                         _P, _I32, _I64, _I64, _I64, _P, _I32, _P, _I32, _I64, _I64, _I64,
                         _I64, _P], _I32),
+    "fc_jpeg_encode_grouped": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I32,
+                                _I32, _P, _I64, _I64, _I64, _I64, _P, _I32, _I32, _I64, _I64,
+                                _I64, _I64, _P, _P], _I32),
+    "fc_jpeg_decode_grouped": ([_P, _I64, _I64, _I64, _I64, _I32, _I64, _I64, _I64, _I64, _P,
+                                _I32, _I32, _I64, _I64, _I64, _I64, _P, _I32, _P, _I32, _I64,
+                                _I64, _I64, _I64, _P], _I32),
     "fc_png_encode": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32,
                        _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P], _I32),
     "fc_png_decode": ([_P, _I64, _I64, _I64, _I64, _P, _I32, _I64, _I64, _I64,
@@ -54,6 +69,19 @@ _SIGS = {
                         _P, _F32,
                         _P, _I32, _I64, _I64,
                         _P, ctypes.c_size_t, _P], _I32),
+    "fc_decode_attn_grouped": ([_P, _I32, _I64, _I64, _I64, _I64, _I64,
+                                _I64, _I64, _I32, _I32,
+                                _P, _I64, _I64, _I64, _I64,
+                                _P, _I64, _I64, _I64, _I64,
+                                _P, _I64, _I64, _I64, _I64,
+                                _P, _I64, _I64, _I64, _I64,
+                                _I32, _I32,
+                                _P, _I64, _I64, _I64,
+                                _P, _I64, _I64, _I64,
+                                _I32, _I64,
+                                _P, _F32,
+                                _P, _I32, _I64, _I64,
+                                _P, ctypes.c_size_t, _P], _I32),
     "fc_decode_attn_png": ([_P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32,
                             _P, _P, _I32, _I64, _I64, _I64,
                             _P, _P, _I64, _I64, _I64, _I64,
@@ -72,6 +100,8 @@ _SIGS = {
                                 _P, _F32,
                                 _P, _I32, _I64, _I64, _P], _I32),
     "fc_decode_attn_noalloc_status": ([_P, _I32, _P], _I32),
+    "fc_append_tokens": ([_P, _I32, _I32, _I64, _I64, _I64, _I32, _I32, _I64, _I64, _P, _I32,
+                          _P], _I32),
     "fc_gather_batch": ([_P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _I32),
     "fc_rope_kv_append": ([_P, _I64, _I64, _P, _I64, _I64, _I64,
                            _P, _I64, _I64, _P, _I64, _I64,

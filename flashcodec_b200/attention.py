@@ -98,6 +98,14 @@ def codec_decode_attention(query, key_stream, value_stream, scale=None, impl="au
     krows, kscales = _rows(ks)
     vrows, vscales = _rows(vs)
     A = _device_A(ks.codec, ks.block_size, query.device) if krows is not None else None
+    group = getattr(ks.codec, "group_size", None)
+    if group is not None and krows is not None:
+        # per-group scales (the per-32 coefficient format)
+        if visible is not None:
+            raise NotImplementedError("a visibility mask is not supported on per-group archives")
+        K.decode_attn_grouped(query, krows, vrows, kscales, vscales, group, ks.raw, vs.raw, A,
+                              scale, out)
+        return out
     K.decode_attn(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale, out,
                   vis=visible)
     return out

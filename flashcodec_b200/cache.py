@@ -26,20 +26,29 @@ Differences a caller can observe, none of them in values:
 
 from __future__ import annotations
 
+import threading
+
+import numpy as np
 import torch
 
 from . import _kernels as K
+from . import _lib
 from .codecs import JPEGCodec, PNGCodec
 from .codecs.jpeg import device_basis
 
 
 def make_codec(mode="jpeg", block_size=8, keep_freqs=2, keep_ratio=1.0,
-               quant_bits=0, scale_dtype=torch.float32):
-    """Build a codec from a mode name (flashcodec/cache.py:39-54)."""
+               quant_bits=0, scale_dtype=torch.float32, group_size=None):
+    """Build a codec from a mode name (flashcodec/cache.py:39-54).
+    ``scale_dtype`` and ``group_size`` (jpeg int8 only) are extensions; see
+    JPEGCodec."""
     if mode == "jpeg":
         return JPEGCodec(block_size=block_size, keep_freqs=keep_freqs,
-                         quant_bits=quant_bits, scale_dtype=scale_dtype)
+                         quant_bits=quant_bits, scale_dtype=scale_dtype,
+                         group_size=group_size)
     if mode == "png":
+        if group_size is not None:
+            raise ValueError("group_size applies to the jpeg int8 codec only")
         if quant_bits:
             raise ValueError(f"quant_bits={quant_bits} applies to the jpeg codec only: png "
                              "stores fp32 deltas, which is what makes it lossless")
@@ -111,8 +120,10 @@ class _CodecStream:
         if self.codec.name == "jpeg":
             k = self.codec.keep_freqs
             if self.codec.quantized:
+                g = self.codec.group_size
                 return [("_coeffs", (B, H, cap, k, D), torch.int8),
-                        ("_scales", (B, H, cap, k, 1), self.codec.scale_dtype)]
+                        ("_scales", (B, H, cap, k, 1 if g is None else D // g),
+                         self.codec.scale_dtype)]
             return [("_coeffs", (B, H, cap, k, D), self.dtype)]
         r = self.block_size
         return [("_deltas", (B, H, cap, r - 1, D), torch.float32),
@@ -157,8 +168,13 @@ class _CodecStream:
             if self.codec.quantized:
                 if self.codec.scale_dtype == torch.float16 and self._scale_err is None:
                     self._scale_err = torch.zeros(1, dtype=torch.int32, device=x.device)
-                K.jpeg_encode(x, basis, r, k, self._coeffs[:, :, sl], self._scales[:, :, sl],
-                              self._scale_err)
+                if self.codec.group_size is not None:
+                    K.jpeg_encode_grouped(x, basis, r, k, self._coeffs[:, :, sl],
+                                          self._scales[:, :, sl], self.codec.group_size,
+                                          self._scale_err)
+                else:
+                    K.jpeg_encode(x, basis, r, k, self._coeffs[:, :, sl],
+                                  self._scales[:, :, sl], self._scale_err)
             else:
                 K.jpeg_encode(x, basis, r, k, self._coeffs[:, :, sl])
         else:
@@ -225,7 +241,12 @@ class _CodecStream:
         like = self._coeffs if self.codec.name == "jpeg" else self._deltas
         self._ensure_rec((b + 1) * r, like)
         dst = self._rec[:, :, a * r:]
-        if self.codec.name == "jpeg":
+        if self.codec.name == "jpeg" and getattr(self.codec, "group_size", None) is not None:
+            K.jpeg_decode_grouped(self._coeffs[:, :, a:b], self._scales[:, :, a:b],
+                                  self.codec.group_size,
+                                  device_basis(r, self.codec.keep_freqs, dst.device), r, dst,
+                                  (b - a) * r)
+        elif self.codec.name == "jpeg":
             k = self.codec.keep_freqs
             K.jpeg_decode(self._coeffs[:, :, a:b],
                           self._scales[:, :, a:b] if self.codec.quantized else None,
@@ -330,6 +351,91 @@ class _CodecStream:
         return bool(self._scale_err is not None and int(self._scale_err.item()) != 0)
 
 
+_APPEND_LOCAL = threading.local()
+
+
+def _append_table(n):
+    """Thread-local (ctypes AppendStream array, int64 numpy view) of >= n rows."""
+    tbl = getattr(_APPEND_LOCAL, "tbl", None)
+    if tbl is None or len(tbl[0]) < n:
+        arr = (_lib.AppendStream * max(n, 64))()
+        tbl = (arr, np.frombuffer(arr, dtype=np.int64).reshape(len(arr), 8))
+        _APPEND_LOCAL.tbl = tbl
+    return tbl
+
+
+def append_one_token(streams, tokens) -> bool:
+    """Append one token to every jpeg stream in ``streams`` with a single
+    fc_append_tokens launch, archiving in the same launch the blocks it
+    completes.  ``tokens[i]`` is the (B, H, 1, D) token of ``streams[i]``.
+    Returns False, having changed nothing, when the streams do not share one
+    layout (codec settings, dtype, shape, raw position, archived blocks,
+    device) or a layout the launch does not take; the caller then appends
+    stream by stream.  Results are bit-identical to ``append``."""
+    st0, t0 = streams[0], tokens[0]
+    c0 = st0.codec
+    if c0.name != "jpeg" or c0.keep_freqs > 8 or c0.block_size > 64 or t0.dim() != 4 \
+            or c0.group_size is not None:
+        return False
+    B, H, m, D = t0.shape
+    r, pos, nb = c0.block_size, st0._raw_len, st0.n_blocks
+    if m != 1 or D % 4 or D > 512 or t0.dtype not in (torch.float32, torch.bfloat16,
+                                                      torch.float16):
+        return False
+    es = t0.element_size()
+    dev = t0.device
+    for st, tk in zip(streams, tokens):
+        c = st.codec
+        if (c.name != "jpeg" or c.block_size != r or c.keep_freqs != c0.keep_freqs
+                or c.quant_bits != c0.quant_bits or c.scale_dtype != c0.scale_dtype
+                or c.group_size is not None):
+            return False
+        rb = st._raw_buf
+        if (st.meta is None or rb is None or st.dtype != tk.dtype or tk.shape != t0.shape
+                or tk.device != dev or tk.stride(-1) != 1 or st._raw_len != pos
+                or st.n_blocks != nb or rb.shape != (B, H, r, D) or not rb.is_contiguous()
+                or rb.device != dev or tk.data_ptr() % (4 * es) or tk.stride(0) % 4
+                or tk.stride(1) % 4):
+            return False
+    archive = pos == r - 1
+    if archive:
+        for st in streams:
+            st._grow(nb + 1, st._raw_buf)
+            if not st._coeffs.is_contiguous() or (st._scales is not None
+                                                  and not st._scales.is_contiguous()):
+                return False
+    quant = c0.quantized
+    fp16 = quant and c0.scale_dtype == torch.float16
+    if fp16:
+        for st in streams:
+            if st._scale_err is None:
+                st._scale_err = torch.zeros(1, dtype=torch.int32, device=dev)
+    n = len(streams)
+    arr, tab = _append_table(n)
+    tab[:n, 0] = [tk.data_ptr() for tk in tokens]
+    tab[:n, 1] = [tk.stride(0) for tk in tokens]
+    tab[:n, 2] = [tk.stride(1) for tk in tokens]
+    tab[:n, 3] = [st._raw_buf.data_ptr() for st in streams]
+    if archive:
+        tab[:n, 4] = [st._coeffs.data_ptr() for st in streams]
+        tab[:n, 5] = [st._scales.data_ptr() for st in streams] if quant else 0
+        tab[:n, 6] = [st._capacity for st in streams]
+        tab[:n, 7] = [st._scale_err.data_ptr() for st in streams] if fp16 else 0
+    else:
+        tab[:n, 4:] = 0
+    K.append_tokens(arr, n, t0.dtype, B, H, D, r, c0.keep_freqs, pos, nb,
+                    device_basis(r, c0.keep_freqs, dev) if archive else None,
+                    c0.scale_dtype if quant else None, dev)
+    for st in streams:
+        if archive:
+            st.n_blocks = nb + 1
+            st.n_archived += r
+            st._raw_len = 0
+        else:
+            st._raw_len = pos + 1
+    return True
+
+
 def append_rotary(key_stream, value_stream, q, k, v, cos, sin):
     """One decode token of one layer: rotary embedding of q and k and the
     append of (rotated k, v) to the layer's streams in one launch
@@ -381,10 +487,11 @@ class CodecKVCache:
     """
 
     def __init__(self, mode="jpeg", block_size=8, keep_freqs=2,
-                 keep_ratio=1.0, quant_bits=0, scale_dtype=torch.float32):
+                 keep_ratio=1.0, quant_bits=0, scale_dtype=torch.float32, group_size=None):
         self.mode = mode
         self.codec = make_codec(mode, block_size, keep_freqs, keep_ratio,
-                                quant_bits=quant_bits, scale_dtype=scale_dtype)
+                                quant_bits=quant_bits, scale_dtype=scale_dtype,
+                                group_size=group_size)
         self._keys = {}
         self._values = {}
 
@@ -405,9 +512,38 @@ class CodecKVCache:
     decode_step = update
 
     def append(self, key_states, value_states, layer_idx=0):
-        """Append without materialising the view (the decode-attention path)."""
-        self._stream(self._keys, layer_idx).append(key_states)
-        self._stream(self._values, layer_idx).append(value_states)
+        """Append without materialising the view (the decode-attention path).
+        A single token goes to both streams in one launch when they allow it
+        (fc_append_tokens), else stream by stream."""
+        ks = self._stream(self._keys, layer_idx)
+        vs = self._stream(self._values, layer_idx)
+        if key_states.dim() == 4 and key_states.shape[-2] == 1 and \
+                append_one_token((ks, vs), (key_states, value_states)):
+            return
+        ks.append(key_states)
+        vs.append(value_states)
+
+    def append_layers(self, key_states, value_states, layer_ids=None):
+        """Append one decode token to several layers at once: ``key_states[i]``
+        and ``value_states[i]`` ((B, H, 1, D) each) go to layer
+        ``layer_ids[i]`` (default: layers 0, 1, ...).  When every stream
+        shares one layout, all of them -- K and V of every layer, including
+        the archive of the blocks this token completes -- take a single
+        fc_append_tokens launch; otherwise each layer is appended in turn.
+        An extension of the reference API for engines that produce a step's
+        K/V for many layers together (e.g. replaying a cached step)."""
+        ids = list(range(len(key_states))) if layer_ids is None else list(layer_ids)
+        if not (len(ids) == len(key_states) == len(value_states)):
+            raise ValueError("one key and one value tensor per layer id")
+        streams, tokens = [], []
+        for i, k, v in zip(ids, key_states, value_states):
+            streams += [self._stream(self._keys, i), self._stream(self._values, i)]
+            tokens += [k, v]
+        if streams and all(t.dim() == 4 and t.shape[-2] == 1 for t in tokens) and \
+                append_one_token(streams, tokens):
+            return
+        for i, k, v in zip(ids, key_states, value_states):
+            self.append(k, v, i)
 
     def forward(self, key_seq, value_seq, layer_idx=0):
         """Reset the layer, fill it with the whole sequence, return the view."""

@@ -107,23 +107,33 @@ def dct_decompress(coeffs, r, out_len=None):
     return _DctDecompress.apply(coeffs, r, out_len)
 
 
-def quantize_coeffs(coeffs, bits=8):
-    """Symmetric per-(block, frequency) int8 quantization
+def quantize_coeffs(coeffs, bits=8, group_size=None):
+    """Symmetric int8 quantization of coefficients
     (flashcodec/codecs/jpeg.py:85-100): coeffs (..., n, k, D) ->
-    (int8 codes, fp32 scales (..., n, k, 1)).  Run by the archive kernel with a
-    one-sample block, so codes and scales are the ones the cache stores."""
+    (int8 codes, fp32 scales (..., n, k, 1)), one scale per (block,
+    frequency) row.  Run by the archive kernel with a one-sample block, so
+    codes and scales are the ones the cache stores.
+
+    ``group_size`` (an extension: the per-32 coefficient quantizer of
+    docs/llama-cpp-kv-quantization.md:179-234) gives one scale per
+    ``group_size`` channels of a row instead: scales (..., n, k, D //
+    group_size), each group quantized exactly as a row is."""
     if bits != 8:
         raise ValueError(f"only 8-bit coefficient quantization is supported, "
                          f"got bits={bits}")
     K.require_cuda(coeffs)
     c = coeffs.detach()
     D = c.shape[-1]
-    rows = c.reshape(-1, D) if c.stride(-1) == 1 else c.contiguous().reshape(-1, D)
+    g = D if group_size is None else int(group_size)
+    if g < 1 or D % g:
+        raise ValueError(f"group_size={group_size} must divide the last dimension ({D})")
+    rows = c.reshape(-1, g) if c.stride(-1) == 1 and c.is_contiguous() else \
+        c.contiguous().reshape(-1, g)
     R = rows.shape[0]
-    codes = torch.empty(1, 1, R, 1, D, dtype=torch.int8, device=c.device)
+    codes = torch.empty(1, 1, R, 1, g, dtype=torch.int8, device=c.device)
     scales = torch.empty(1, 1, R, 1, 1, dtype=torch.float32, device=c.device)
     K.jpeg_encode(rows[None, None], _identity(c.device), 1, 1, codes, scales)
-    return codes.reshape(c.shape), scales.reshape(*c.shape[:-1], 1)
+    return codes.reshape(c.shape), scales.reshape(*c.shape[:-1], D // g)
 
 
 def dequantize_coeffs(q, scale, dtype=torch.float32):
@@ -134,6 +144,15 @@ def dequantize_coeffs(q, scale, dtype=torch.float32):
     rounding, so the result matches the reference's ``dtype`` product."""
     K.require_cuda(q, scale)
     D = q.shape[-1]
+    G = scale.shape[-1] if scale.dim() else 1
+    if G > 1:
+        # one scale per D // G channels (quantize_coeffs(..., group_size)):
+        # each group dequantizes like a row
+        if D % G:
+            raise ValueError(f"{G} scales per row do not divide the last dimension ({D})")
+        out = dequantize_coeffs(q.reshape(*q.shape[:-1], G, D // G),
+                                scale.reshape(*scale.shape[:-1], G, 1), dtype)
+        return out.reshape(q.shape)
     qr = q.reshape(-1, D)
     R = qr.shape[0]
     s = scale.to(dtype).float() if dtype != torch.float32 else scale.float()
@@ -150,23 +169,31 @@ class JPEGCodec:
     """JPEG-style lossy frequency-domain codec (flashcodec/codecs/jpeg.py:108-159).
 
     ``quant_bits=8`` stores int8 coefficients with a per-(block, frequency)
-    scale.  ``scale_dtype`` (an addition, default fp32 as the reference) may be
-    torch.float16 to halve the scale bytes; the archive kernel reports any
-    scale that fp16 cannot hold exactly."""
+    scale.  Additions to the reference: ``scale_dtype`` (default fp32 as the
+    reference) may be torch.float16 to halve the scale bytes, the archive
+    kernel reporting any scale that fp16 cannot hold exactly; ``group_size``
+    (default None: one scale per row, as the reference) stores one scale per
+    that many channels of a row -- 32 gives the per-32 coefficient format of
+    docs/llama-cpp-kv-quantization.md:179-234."""
 
     name = "jpeg"
 
-    def __init__(self, block_size=8, keep_freqs=2, quant_bits=0, scale_dtype=torch.float32):
+    def __init__(self, block_size=8, keep_freqs=2, quant_bits=0, scale_dtype=torch.float32,
+                 group_size=None):
         assert 1 <= keep_freqs <= block_size, \
             f"keep_freqs={keep_freqs} is outside 1..{block_size} (the block length)"
         assert quant_bits in (0, 8), \
             f"quant_bits={quant_bits}: use 0 (coefficients kept in the input dtype) or 8 (int8)"
         assert scale_dtype in (torch.float32, torch.float16), \
             "scale_dtype must be torch.float32 or torch.float16"
+        assert group_size is None or (quant_bits == 8 and int(group_size) >= 4
+                                      and int(group_size) % 4 == 0), \
+            "group_size needs quant_bits=8 and a multiple of 4 channels (32 for per-32)"
         self.block_size = block_size
         self.keep_freqs = keep_freqs
         self.quant_bits = quant_bits
         self.scale_dtype = scale_dtype
+        self.group_size = None if group_size is None else int(group_size)
 
     @property
     def quantized(self):
@@ -181,7 +208,7 @@ class JPEGCodec:
         """int8 codes and scales of ``coeffs`` for an int8 codec; (None, None)
         for an unquantized one."""
         if self.quantized:
-            return quantize_coeffs(coeffs, self.quant_bits)
+            return quantize_coeffs(coeffs, self.quant_bits, self.group_size)
         return None, None
 
     def decompress(self, coeffs, out_len=None, scales=None):
@@ -202,4 +229,6 @@ class JPEGCodec:
         extra = "" if not self.quantized else f", quant_bits={self.quant_bits}"
         if self.scale_dtype != torch.float32:
             extra += ", scale_dtype=torch.float16"
+        if self.group_size is not None:
+            extra += f", group_size={self.group_size}"
         return f"JPEGCodec(block_size={self.block_size}, keep_freqs={self.keep_freqs}{extra})"

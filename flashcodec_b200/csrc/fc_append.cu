@@ -27,7 +27,6 @@ struct AppendArgs {
     int n_streams, r, k, scale_dtype;
     int64_t B, H, D, slot, block;
     const float *basis;
-    int *err;
     fc_append_stream s[kAppendMaxStreams];
 };
 
@@ -130,7 +129,7 @@ append_tokens_kernel(const __grid_constant__ AppendArgs a) {
             if (a.scale_dtype == FC_F16) {
                 const __half hs = __float2half_rn(sc);
                 static_cast<__half *>(st.scales)[blk + j] = hs;
-                if (__half2float(hs) != sc && a.err) atomicOr(a.err, 1);
+                if (__half2float(hs) != sc && st.err) atomicOr(st.err, 1);
             } else {
                 static_cast<float *>(st.scales)[blk + j] = sc;
             }
@@ -145,7 +144,7 @@ using namespace fc;
 
 extern "C" int fc_append_tokens(const fc_append_stream *streams, int n_streams, int dtype,
                                 int64_t B, int64_t H, int64_t D, int r, int k, int64_t slot,
-                                int64_t block, const float *basis, int scale_dtype, int *err,
+                                int64_t block, const float *basis, int scale_dtype,
                                 void *stream) {
     clear_error();
     if (n_streams < 0 || B < 0 || H < 0 || D <= 0) { set_error("append_tokens: bad shape"); return FC_EINVAL; }
@@ -190,7 +189,7 @@ extern "C" int fc_append_tokens(const fc_append_stream *streams, int n_streams, 
     AppendArgs a;
     a.r = r; a.k = k; a.scale_dtype = scale_dtype;
     a.B = B; a.H = H; a.D = D; a.slot = slot; a.block = block;
-    a.basis = basis; a.err = err;
+    a.basis = basis;
     const int ch = (int)((D + 127) / 128);
     for (int first = 0; first < n_streams; first += kAppendMaxStreams) {
         const int n = std::min(kAppendMaxStreams, n_streams - first);

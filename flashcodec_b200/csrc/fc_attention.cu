@@ -66,6 +66,11 @@ struct AttnArgs {
     const void *ksc, *vsc;
     int sc_dtype;
     int64_t ks_sb, ks_sh, ks_sn, vs_sb, vs_sh, vs_sn;
+    // per-group scales (fc_decode_attn_grouped): one scale per `sgrp`
+    // channels, frequency strides ks_sj / vs_sj, group stride 1; sgrp = 0
+    // for the reference's one scale per row
+    int sgrp;
+    int64_t ks_sj, vs_sj;
     const void *kraw, *vraw;
     int raw_dtype;
     // png archives: row 0 of every block from these anchors (own dtype and
@@ -98,7 +103,7 @@ struct AttnArgs {
 };
 
 // ------------------------------------------------------------------ kernel
-template <typename RT, int VEC, int NCH, int GT, bool BULK>
+template <typename RT, int VEC, int NCH, int GT, bool BULK, bool GS = false>
 __global__ void __launch_bounds__(kThreads)
 attn_kernel(AttnArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -171,11 +176,36 @@ attn_kernel(AttnArgs a) {
     for (int i = tid; i < r * s; i += kThreads) sA[i] = a.A ? a.A[i] : 0.0f;
     for (int i = tid; i < nb * s; i += kThreads) {
         const int blk = i / s, j = i % s;
-        sks[i] = a.ksc ? load_as_f32(a.ksc, b * a.ks_sb + hk * a.ks_sh + (n0 + blk) * a.ks_sn + j,
-                                     a.sc_dtype) : 1.0f;
-        svs[i] = a.vsc ? load_as_f32(a.vsc, b * a.vs_sb + hk * a.vs_sh + (n0 + blk) * a.vs_sn + j,
-                                     a.sc_dtype) : 1.0f;
+        sks[i] = a.ksc && !GS ? load_as_f32(a.ksc, b * a.ks_sb + hk * a.ks_sh +
+                                                    (n0 + blk) * a.ks_sn + j, a.sc_dtype) : 1.0f;
+        svs[i] = a.vsc && !GS ? load_as_f32(a.vsc, b * a.vs_sb + hk * a.vs_sh +
+                                                    (n0 + blk) * a.vs_sn + j, a.sc_dtype) : 1.0f;
     }
+    // per-group scales: each chunk of VEC channels a lane holds lies in one
+    // group (sgrp % VEC == 0, checked on the host); a row's chunk is scaled
+    // right after it is loaded (dequantize_coeffs with the group's scale)
+    const int s_shift = (s & (s - 1)) == 0 ? __ffs(s) - 1 : -1;
+    auto group_scale = [&](const void *sc, int64_t sb, int64_t sh, int64_t sn, int64_t sj,
+                           int row, float x[NCH][VEC]) {
+        const int blk = s_shift >= 0 ? row >> s_shift : row / s;
+        const int j = row - blk * s;
+        const int64_t base = b * sb + hk * sh + (n0 + blk) * sn + j * sj;
+#pragma unroll
+        for (int c = 0; c < NCH; c++) {
+            const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
+            if (d0 < a.D) {
+                const float f = load_as_f32(sc, base + d0 / a.sgrp, a.sc_dtype);
+#pragma unroll
+                for (int e = 0; e < VEC; e++) x[c][e] = __fmul_rn(x[c][e], f);
+            }
+        }
+    };
+    auto kgs = [&](int row, float x[NCH][VEC]) {
+        if constexpr (GS) group_scale(a.ksc, a.ks_sb, a.ks_sh, a.ks_sn, a.ks_sj, row, x);
+    };
+    auto vgs = [&](int row, float x[NCH][VEC]) {
+        if constexpr (GS) group_scale(a.vsc, a.vs_sb, a.vs_sh, a.vs_sn, a.vs_sj, row, x);
+    };
 
     // q for this lane's channels, fp32 registers
     float qr[GT][NCH][VEC];
@@ -363,6 +393,7 @@ attn_kernel(AttnArgs a) {
                     const int row = base + u * rows_per_pass + warp * rpw + lr;
                     if (row < trows) {
                         load_typed(tile + (int64_t)row * row_elems, x[u]);
+                        kgs(t * a.tb * s + row, x[u]);
                     } else {
 #pragma unroll
                         for (int c = 0; c < NCH; c++)
@@ -399,6 +430,7 @@ attn_kernel(AttnArgs a) {
                                  a.anc_dtype, x[u]);
                     } else {
                         load_typed(rb + (int64_t)(j0 + u) * a.k_sj, x[u]);
+                        kgs(blk * s + j0 + u, x[u]);
                     }
                 }
                 float v[M];
@@ -424,6 +456,7 @@ attn_kernel(AttnArgs a) {
                 const int row = base + u * rows_per_pass + warp * rpw + lr;
                 if (row < krows_total) {
                     load_direct(kbase, a.kanc, a.k_sn, a.k_sj, row, x[u]);
+                    kgs(row, x[u]);
                 } else {
 #pragma unroll
                     for (int c = 0; c < NCH; c++)
@@ -528,13 +561,15 @@ attn_kernel(AttnArgs a) {
 #pragma unroll
         for (int g = 0; g < GT; g++) w[g] = ssc[wrow * GT + g];
 #pragma unroll
+        float x[NCH][VEC];
+        load_typed(p, x);
+        vgs(wrow, x);
+#pragma unroll
         for (int c = 0; c < NCH; c++) {
             const int64_t d0 = ((int64_t)c * lpr + li) * VEC;
             if (d0 < a.D) {
-                float x[VEC];
-                load_vec_f32<RT, VEC>(p + d0, x);
 #pragma unroll
-                for (int g = 0; g < GT; g++) axpy(w[g], x, acc[g][c]);
+                for (int g = 0; g < GT; g++) axpy(w[g], x[c], acc[g][c]);
             }
         }
     };
@@ -579,6 +614,7 @@ attn_kernel(AttnArgs a) {
                         else
                             load_typed(rb + (int64_t)(j0 + u) * a.v_sj, x[u]);
                         const int row = blk * s + j0 + u;
+                        vgs(row, x[u]);
 #pragma unroll
                         for (int g = 0; g < GT; g++) w[u][g] = ssc[row * GT + g];
                     }
@@ -601,6 +637,7 @@ attn_kernel(AttnArgs a) {
                 const int row = base + u * rows_per_pass + warp * rpw + lr;
                 if (row < krows_total) {
                     load_direct(vbase, a.vanc, a.v_sn, a.v_sj, row, x[u]);
+                    vgs(row, x[u]);
 #pragma unroll
                     for (int g = 0; g < GT; g++) w[u][g] = ssc[row * GT + g];
                 } else {
@@ -839,6 +876,14 @@ int launch_gt(const Plan &p, AttnArgs &args, dim3 grid, cudaStream_t st) {
         kern<<<grid, kThreads, p.smem, st>>>(args);
     };
     constexpr int V16 = 16 / (int)sizeof(RT);
+    if constexpr (std::is_same<RT, int8_t>::value) {
+        if (args.sgrp) {  // per-group scales (int8 codes only)
+            if (p.vec_mode == 2) setup(attn_kernel<RT, V16, 1, GT, true, true>);
+            else if (p.vec_mode == 1) setup(attn_kernel<RT, V16, 1, GT, false, true>);
+            else setup(attn_kernel<RT, 1, kMaxD / 32, GT, false, true>);
+            return check_launch("decode_attn");
+        }
+    }
     if (p.vec_mode == 2) setup(attn_kernel<RT, V16, 1, GT, true>);
     else if (p.vec_mode == 1) setup(attn_kernel<RT, V16, 1, GT, false>);
     else setup(attn_kernel<RT, 1, kMaxD / 32, GT, false>);
@@ -910,7 +955,8 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
                               int64_t o_sh, void *workspace, size_t workspace_bytes,
                               void *stream,
                             const PngAnchors *png, const unsigned char *vis = nullptr,
-                            int64_t vis_sb = 0) {
+                            int64_t vis_sb = 0, int sgrp = 0, int64_t ks_sj = 1,
+                            int64_t vs_sj = 1) {
     clear_error();
     if (B < 0 || Hq <= 0 || Hk <= 0 || D <= 0) { set_error("decode_attn: bad shape"); return FC_EINVAL; }
     if (Hq % Hk != 0) { set_error("decode_attn: Hq (%lld) must be a multiple of Hk (%lld)", (long long)Hq, (long long)Hk); return FC_EINVAL; }
@@ -926,11 +972,25 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     if (B == 0) return FC_OK;
     if (n_blocks == 0 && n_raw == 0) { set_error("decode_attn: empty cache (caller returns zeros)"); return FC_EINVAL; }
     if (!q || !out || (n_blocks > 0 && (!k_rows || !v_rows || !A))) { set_error("decode_attn: null pointer"); return FC_EINVAL; }
-    if (n_blocks == 0) { s = 1; r = std::max<int>(r, 1); rows_dtype = FC_F32; }
+    if (sgrp && (rows_dtype != FC_I8 || !k_scales || !v_scales || sgrp < 1 || D % sgrp != 0 || png)) {
+        set_error("decode_attn_grouped: per-group scales need int8 rows with scales and a group "
+                  "size dividing the head dim (got %d for D %lld)", sgrp, (long long)D);
+        return FC_EINVAL;
+    }
+    if (sgrp == D) sgrp = 0;  // one group per row: the row-scale layout with frequency stride ks_sj
+    if (sgrp == 0 && (ks_sj != 1 || vs_sj != 1) && n_blocks > 0) {
+        set_error("decode_attn: row scales need frequency stride 1");
+        return FC_EINVAL;
+    }
+    if (n_blocks == 0) { s = 1; r = std::max<int>(r, 1); rows_dtype = FC_F32; sgrp = 0; }
 
     // png rows come from two tensors (the CUDA-core kernel's direct-load path);
     // a visibility mask is applied by the CUDA-core kernel
-    const int sel = (png || vis) ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
+    const int sel = (png || vis || sgrp) ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
+    if (sgrp && g_attn_kernel.load() == FC_ATTN_TENSOR_CORE) {
+        set_error("decode_attn: the tensor-core kernel takes one scale per row only");
+        return FC_ENOTSUP;
+    }
     if (n_blocks > 0 && sel != FC_ATTN_CUDA_CORE) {
         const int64_t G = Hq / Hk, row = (int64_t)s * D;
         const bool contig = tc_supported(D, s, r, G, rows_dtype) && k_sj == D && k_sn == row &&
@@ -985,6 +1045,8 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     int vm = n_blocks > 0 ? pick_vec_mode(D, es, k_rows, v_rows, k_sb, k_sh, k_sn, k_sj,
                                           v_sb, v_sh, v_sn, v_sj, s)
                           : 0;
+    // a lane's VEC channels must share one scale group
+    if (sgrp && vm > 0 && sgrp % (16 / es) != 0) vm = 0;
     if (png) {
         vm = std::min(vm, 1);  // rows of a block are not one contiguous run
         // anchors are read with the deltas' vector width (16 / es elements)
@@ -1009,6 +1071,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     a.k_sb = k_sb; a.k_sh = k_sh; a.k_sn = k_sn; a.k_sj = k_sj;
     a.v_sb = v_sb; a.v_sh = v_sh; a.v_sn = v_sn; a.v_sj = v_sj;
     a.ksc = k_scales; a.vsc = v_scales; a.sc_dtype = scale_dtype;
+    a.sgrp = sgrp; a.ks_sj = ks_sj; a.vs_sj = vs_sj;
     a.ks_sb = ks_sb; a.ks_sh = ks_sh; a.ks_sn = ks_sn;
     a.vs_sb = vs_sb; a.vs_sh = vs_sh; a.vs_sn = vs_sn;
     a.kraw = k_raw; a.vraw = v_raw; a.raw_dtype = raw_dtype;
@@ -1068,6 +1131,27 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
                               int64_t o_sh, void *workspace, size_t workspace_bytes,
                               void *stream) {
     return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype, k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj, k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn, scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st, raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int fc_decode_attn_grouped(
+    const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D, int64_t q_sb, int64_t q_sh,
+    int64_t Hk, int64_t n_blocks, int s, int r, const void *k_rows, int64_t k_sb, int64_t k_sh,
+    int64_t k_sn, int64_t k_sj, const void *v_rows, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+    int64_t v_sj, const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+    int64_t ks_sj, const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+    int64_t vs_sj, int scale_dtype, int scale_group, const void *k_raw, int64_t kr_sb,
+    int64_t kr_sh, int64_t kr_st, const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+    int raw_dtype, int64_t n_raw, const float *A, float softmax_scale, void *out, int out_dtype,
+    int64_t o_sb, int64_t o_sh, void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (scale_group < 1) { set_error("decode_attn_grouped: scale_group must be >= 1"); return FC_EINVAL; }
+    return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, FC_I8, k_rows,
+                            k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj, k_scales,
+                            ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn, scale_dtype,
+                            k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st, raw_dtype,
+                            n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh, workspace,
+                            workspace_bytes, stream, nullptr, nullptr, 0, scale_group, ks_sj,
+                            vs_sj);
 }
 
 extern "C" int fc_decode_attn_png(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,

@@ -10,6 +10,8 @@
 // bit-identical to the reference.
 #include <math.h>
 
+#include <algorithm>
+
 #include "fc_common.cuh"
 
 namespace fc {
@@ -29,9 +31,10 @@ struct EncArgs {
     int64_t o_sb, o_sh, o_sn, o_sj;
     void *scales;
     int scale_dtype;
-    int64_t s_sb, s_sh, s_sn;
+    int64_t s_sb, s_sh, s_sn, s_sj;  // scale (b, h, block, frequency) strides; group stride 1
     int *err;
-    int bpw;  // blocks per warp of the d128 fast path (kEncBlocks, or 1 for small launches)
+    int bpw;    // blocks per warp of the d128 fast path (kEncBlocks, or 1 for small launches)
+    int group;  // channels sharing one scale: D (one scale per row, the reference) or a divisor
 };
 
 __device__ __forceinline__ float nan_max(float m, float a) {
@@ -112,6 +115,39 @@ jpeg_encode_kernel(EncArgs a) {
                 }
             }
             if (!quant) continue;
+            if (a.group != a.D) {
+                // one scale per `group` channels: lane-strided over the groups
+                // of each row, same arithmetic as the row-wise quantizer below
+                __syncwarp();
+                const int64_t ng = a.D / a.group;
+                for (int jj = 0; jj < nj; jj++) {
+                    int8_t *orow = static_cast<int8_t *>(a.out) + b * a.o_sb + h * a.o_sh +
+                                   blk * a.o_sn + (j0 + jj) * a.o_sj;
+                    for (int64_t g = lane; g < ng; g += 32) {
+                        const float *cg = tile + jj * a.D + g * a.group;
+                        float m = 0.0f;
+                        for (int e = 0; e < a.group; e++) m = nan_max(m, fabsf(cg[e]));
+                        float sg = round_to_dtype(__fdiv_rn(m, 127.0f), dt);
+                        if (!(sg > 0.0f)) sg = 1.0f;
+                        for (int e = 0; e < a.group; e++) {
+                            float q = rintf(__fdiv_rn(cg[e], sg));
+                            q = fminf(fmaxf(q, -127.0f), 127.0f);
+                            orow[g * a.group + e] = (int8_t)(int)q;
+                        }
+                        const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn +
+                                           (j0 + jj) * a.s_sj + g;
+                        if (a.scale_dtype == FC_F16) {
+                            const __half hs = __float2half_rn(sg);
+                            static_cast<__half *>(a.scales)[si] = hs;
+                            if (__half2float(hs) != sg && a.err) atomicOr(a.err, 1);
+                        } else {
+                            static_cast<float *>(a.scales)[si] = sg;
+                        }
+                    }
+                }
+                __syncwarp();
+                continue;
+            }
     #pragma unroll
             for (int jj = 0; jj < kEncTile; jj++)
     #pragma unroll
@@ -148,7 +184,7 @@ jpeg_encode_kernel(EncArgs a) {
                     }
                 }
                 if (lane == 0) {
-                    const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + (j0 + jj);
+                    const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + (j0 + jj) * a.s_sj;
                     if (a.scale_dtype == FC_F16) {
                         const __half hs = __float2half_rn(s);
                         static_cast<__half *>(a.scales)[si] = hs;
@@ -225,56 +261,112 @@ jpeg_encode_d128_kernel(EncArgs a) {
         for (int i = 0; i < R; i++) load_vec_f32<T, 4>(reinterpret_cast<const T *>(&cur.w[i]), xv[i]);
         int64_t b, h, blk;
         locate(g0 + e, b, h, blk);
+        // coefficients of every kept frequency: sequential fp32 FMA chain
+        // over the R samples, rounded to the input dtype (jpeg.py:66-67)
+        float c[KM][4];
 #pragma unroll
         for (int j = 0; j < KM; j++) {
-            if (j >= a.k) break;
-            float c[4];
 #pragma unroll
-            for (int v = 0; v < 4; v++) c[v] = 0.0f;
+            for (int v = 0; v < 4; v++) c[j][v] = 0.0f;
+            if (j >= a.k) continue;
 #pragma unroll
             for (int i = 0; i < R; i++)
 #pragma unroll
-                for (int v = 0; v < 4; v++) c[v] = __fmaf_rn(xv[i][v], mb[j][i], c[v]);
+                for (int v = 0; v < 4; v++) c[j][v] = __fmaf_rn(xv[i][v], mb[j][i], c[j][v]);
 #pragma unroll
-            for (int v = 0; v < 4; v++) c[v] = round_to_dtype(c[v], dt);  // .to(x.dtype), jpeg.py:67
-            const int64_t orow = b * a.o_sb + h * a.o_sh + blk * a.o_sn + j * a.o_sj + d0;
-            if (!quant) {
-                store_vec_from_f32<T, 4>(static_cast<T *>(a.out) + orow, c);
-                continue;
-            }
-            // amax over the row: |c| bit patterns order like the values (a NaN
-            // pattern is above every number, so NaN propagates like torch.amax)
+            for (int v = 0; v < 4; v++) c[j][v] = round_to_dtype(c[j][v], dt);
+        }
+        const int64_t obase = b * a.o_sb + h * a.o_sh + blk * a.o_sn + d0;
+        if (!quant) {
+#pragma unroll
+            for (int j = 0; j < KM; j++)
+                if (j < a.k) store_vec_from_f32<T, 4>(static_cast<T *>(a.out) + obase + j * a.o_sj, c[j]);
+            continue;
+        }
+        // amax of each frequency row over each scale group of its channels
+        // (the head dim when group == D): |c| bit patterns order like the
+        // values (a NaN pattern is above every number, so NaN propagates like
+        // torch.amax).  A group spans gl = group / 4 aligned lanes.
+        const int gl = a.group >> 2, G = 32 / gl, mygrp = lane / gl;
+        float amax[KM];
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
             unsigned ab = 0u;
 #pragma unroll
-            for (int v = 0; v < 4; v++) ab = max(ab, __float_as_uint(c[v]) & 0x7fffffffu);
-            const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, ab));
-            // scale = amax / 127 in the coefficient dtype; 1 where it is 0
-            float sc = round_to_dtype(__fdiv_rn(amax, 127.0f), dt);
-            if (!(sc > 0.0f)) sc = 1.0f;
-            // q = rint(c / scale) with the IEEE quotient.  c * (1/scale) is within
-            // 2^-23 relative (|q| <= 128: 3e-5 absolute) of it, so it rounds to the
-            // same integer unless it lies within 1e-4 of a half-integer; there (and
-            // for NaN or infinities) the exact quotient is taken.
-            const float rs = __frcp_rn(sc);
-            uint32_t packed = 0u;
+            for (int v = 0; v < 4; v++) ab = max(ab, __float_as_uint(c[j][v]) & 0x7fffffffu);
+            if (gl == 32) {
+                ab = __reduce_max_sync(0xffffffffu, ab);
+            } else {
+                for (int o = 1; o < gl; o <<= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
+            }
+            amax[j] = __uint_as_float(ab);
+        }
+        // scale = amax / 127 in the coefficient dtype, 1 where it is 0
+        // (jpeg.py:96-97): lane p computes the scale of (frequency p / G,
+        // group p % G) and its reciprocal once, every lane takes the ones it
+        // needs by shuffle
+        const int pj = lane / G, pg = lane - pj * G;
+        float mine = 0.0f;
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
+            const float t = __shfl_sync(0xffffffffu, amax[j], pg * gl);
+            mine = pj == j ? t : mine;
+        }
+        float sl = round_to_dtype(__fdiv_rn(mine, 127.0f), dt);
+        if (!(sl > 0.0f)) sl = 1.0f;
+        const float rl = __frcp_rn(sl);
+        // q = clamp(rint(c / scale), -127, 127) with the IEEE quotient: c * (1/scale)
+        // is within 2^-23 relative (|q| <= 128: 3e-5 absolute) of it, so both
+        // round to the same integer unless the product lies within 1e-4 of a
+        // half-integer.  Clamping before rounding is exact (the bounds are
+        // integers); adding 1.5 * 2^23 rounds half to even and leaves the
+        // code's two's-complement byte in the low byte of the sum.  A warp
+        // with any element near a half-integer (or a NaN / infinite product)
+        // redoes its block's rows with the IEEE quotient.
+        constexpr float kRound = 12582912.0f;
+        uint32_t packed[KM];
+        bool near_tie = false;
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
+            const float rs = __shfl_sync(0xffffffffu, rl, j * G + mygrp);
+            uint32_t bytes[4];
 #pragma unroll
             for (int v = 0; v < 4; v++) {
-                const float y = __fmul_rn(c[v], rs);
-                float q = rintf(y);
-                if (!(fabsf(fabsf(y - q) - 0.5f) > 1e-4f)) q = rintf(__fdiv_rn(c[v], sc));
-                q = fminf(fmaxf(q, -127.0f), 127.0f);
-                packed |= ((uint32_t)((int)q & 0xFF)) << (8 * v);
+                const float y = fminf(fmaxf(__fmul_rn(c[j][v], rs), -127.0f), 127.0f);
+                const float u = __fadd_rn(y, kRound);
+                const float t = __fsub_rn(y, __fsub_rn(u, kRound));   // in [-0.5, 0.5]
+                near_tie |= !(fabsf(t) < 0.4999f);
+                bytes[v] = __float_as_uint(u);
             }
-            *reinterpret_cast<uint32_t *>(static_cast<int8_t *>(a.out) + orow) = packed;
-            if (lane == 0) {
-                const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + j;
-                if (a.scale_dtype == FC_F16) {
-                    const __half hs = __float2half_rn(sc);
-                    static_cast<__half *>(a.scales)[si] = hs;
-                    if (__half2float(hs) != sc && a.err) atomicOr(a.err, 1);
-                } else {
-                    static_cast<float *>(a.scales)[si] = sc;
+            packed[j] = __byte_perm(__byte_perm(bytes[0], bytes[1], 0x0040),
+                                    __byte_perm(bytes[2], bytes[3], 0x0040), 0x5410);
+        }
+        if (__any_sync(0xffffffffu, near_tie)) {
+#pragma unroll
+            for (int j = 0; j < KM; j++) {
+                const float sc = __shfl_sync(0xffffffffu, sl, j * G + mygrp);
+                uint32_t p = 0u;
+#pragma unroll
+                for (int v = 0; v < 4; v++) {
+                    float q = rintf(__fdiv_rn(c[j][v], sc));
+                    q = fminf(fmaxf(q, -127.0f), 127.0f);
+                    p |= ((uint32_t)((int)q & 0xFF)) << (8 * v);
                 }
+                packed[j] = p;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < KM; j++)
+            if (j < a.k)
+                *reinterpret_cast<uint32_t *>(static_cast<int8_t *>(a.out) + obase + j * a.o_sj) = packed[j];
+        if (pj < a.k) {
+            const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + pj * a.s_sj + pg;
+            if (a.scale_dtype == FC_F16) {
+                const __half hs = __float2half_rn(sl);
+                static_cast<__half *>(a.scales)[si] = hs;
+                if (__half2float(hs) != sl && a.err) atomicOr(a.err, 1);
+            } else {
+                static_cast<float *>(a.scales)[si] = sl;
             }
         }
     }
@@ -287,12 +379,13 @@ struct DecArgs {
     int64_t c_sb, c_sh, c_sn, c_sj;
     const void *scales;
     int scale_dtype;
-    int64_t s_sb, s_sh, s_sn;
+    int64_t s_sb, s_sh, s_sn, s_sj;  // scale (b, h, block, frequency) strides; group stride 1
     const float *basis;
     int r;
     void *out;
     int out_dtype;
     int64_t out_len, o_sb, o_sh, o_ss;
+    int group;  // channels sharing one scale (D: one per row)
 };
 
 // coefficients (B,H,n,k,D) -> (B,H,out_len,D); KM >= k coefficient registers.
@@ -314,15 +407,17 @@ jpeg_decode_kernel(DecArgs a) {
         const int64_t blk = (int64_t)((unsigned)gw - bh * (unsigned)a.n);
         const int64_t b = bh / (unsigned)a.H, h = bh % (unsigned)a.H;
         const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh + blk * a.c_sn;
-        float sc[KM];
-    #pragma unroll
-        for (int j = 0; j < KM; j++) {
-            sc[j] = 1.0f;
-            if (j < a.k && a.scales)
-                sc[j] = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
-        }
         const int64_t obase = b * a.o_sb + h * a.o_sh;
         for (int64_t d0 = (int64_t)lane * VEC; d0 < a.D; d0 += 32 * VEC) {
+            // the VEC channels of a lane share one scale group (group % VEC == 0)
+            float sc[KM];
+    #pragma unroll
+            for (int j = 0; j < KM; j++) {
+                sc[j] = 1.0f;
+                if (j < a.k && a.scales)
+                    sc[j] = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn +
+                                                      j * a.s_sj + d0 / a.group, a.scale_dtype);
+            }
             float c[KM][VEC];
     #pragma unroll
             for (int j = 0; j < KM; j++) {
@@ -383,7 +478,8 @@ jpeg_decode_d128_kernel(DecArgs a) {
             load_vec_f32<CT, 4>(cb + j * a.c_sj, c[j]);
             if (a.scales) {
                 // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
-                const float sc = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn + j, a.scale_dtype);
+                const float sc = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn +
+                                                           j * a.s_sj + d0 / a.group, a.scale_dtype);
                 const float2 s2 = make_float2(sc, sc);
                 const float2 p01 = __fmul2_rn(make_float2(c[j][0], c[j][1]), s2);
                 const float2 p23 = __fmul2_rn(make_float2(c[j][2], c[j][3]), s2);
@@ -599,13 +695,12 @@ int launch_typed(int dt, F &&f) {
 
 using namespace fc;
 
-extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,
-                              int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss,
-                              const float *basis, int r, int k, void *out, int64_t o_sb,
-                              int64_t o_sh, int64_t o_sn, int64_t o_sj, void *scales,
-                              int scale_dtype, int64_t s_sb, int64_t s_sh, int64_t s_sn,
-                              int *err, void *stream) {
-    clear_error();
+static int jpeg_encode_impl(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,
+                            int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss,
+                            const float *basis, int r, int k, void *out, int64_t o_sb,
+                            int64_t o_sh, int64_t o_sn, int64_t o_sj, void *scales,
+                            int scale_dtype, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                            int64_t s_sj, int group, int *err, void *stream) {
     if (!is_float_dtype(x_dtype)) { set_error("jpeg_encode: x dtype must be f32/bf16/f16"); return FC_EINVAL; }
     if (B < 0 || H < 0 || S < 0 || D <= 0) { set_error("jpeg_encode: bad shape"); return FC_EINVAL; }
     if (r < 1 || r > kMaxR || k < 1 || k > r) { set_error("jpeg_encode: need 1 <= k <= r <= %d", kMaxR); return FC_EINVAL; }
@@ -622,7 +717,7 @@ extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, 
     v4 = v4 && aligned(out, scales ? 4 : 4 * es) && (o_sb % 4 == 0) && (o_sh % 4 == 0) &&
          (o_sn % 4 == 0) && (o_sj % 4 == 0);
     EncArgs a{x, B, H, S, D, nblk, x_sb, x_sh, x_ss, basis, r, k, out, o_sb, o_sh, o_sn, o_sj,
-              scales, scale_dtype, s_sb, s_sh, s_sn, err};
+              scales, scale_dtype, s_sb, s_sh, s_sn, s_sj, err, 1, group};
     const size_t smem = (size_t)kWarpsPerCta * kEncTile * D * sizeof(float);
     if (smem > 160 * 1024) { set_error("jpeg_encode: head dim too large"); return FC_ENOTSUP; }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -631,7 +726,11 @@ extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, 
         if constexpr (std::is_same<T, int8_t>::value) {
             return FC_EINVAL;
         } else {
-            if (v4 && D == 128 && (r == 8 || r == 16) && k <= 8) {
+            // fast path: one lane group of group / 4 lanes per scale group and
+            // every (frequency, group) scale computed by its own lane
+            const bool gfast = !scales || (group % 4 == 0 && 128 % group == 0 &&
+                                           (int64_t)k * (128 / group) <= 32);
+            if (v4 && D == 128 && (r == 8 || r == 16) && k <= 8 && gfast) {
                 // a launch smaller than one wave at kEncBlocks per warp (a decode
                 // step archives one block per stream) spreads its blocks, one per warp
                 const int64_t total = B * H * nblk;
@@ -656,13 +755,42 @@ extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, 
     });
 }
 
-extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64_t H, int64_t n,
-                              int64_t D, int k, int64_t c_sb, int64_t c_sh, int64_t c_sn,
-                              int64_t c_sj, const void *scales, int scale_dtype, int64_t s_sb,
-                              int64_t s_sh, int64_t s_sn, const float *basis, int r, void *out,
-                              int out_dtype, int64_t out_len, int64_t o_sb, int64_t o_sh,
-                              int64_t o_ss, void *stream) {
+extern "C" int fc_jpeg_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,
+                              int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss,
+                              const float *basis, int r, int k, void *out, int64_t o_sb,
+                              int64_t o_sh, int64_t o_sn, int64_t o_sj, void *scales,
+                              int scale_dtype, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                              int *err, void *stream) {
     clear_error();
+    return jpeg_encode_impl(x, x_dtype, B, H, S, D, x_sb, x_sh, x_ss, basis, r, k, out, o_sb,
+                            o_sh, o_sn, o_sj, scales, scale_dtype, s_sb, s_sh, s_sn, 1,
+                            (int)std::max<int64_t>(D, 1), err, stream);
+}
+
+extern "C" int fc_jpeg_encode_grouped(const void *x, int x_dtype, int64_t B, int64_t H,
+                                      int64_t S, int64_t D, int64_t x_sb, int64_t x_sh,
+                                      int64_t x_ss, const float *basis, int r, int k, void *out,
+                                      int64_t o_sb, int64_t o_sh, int64_t o_sn, int64_t o_sj,
+                                      void *scales, int scale_dtype, int group, int64_t s_sb,
+                                      int64_t s_sh, int64_t s_sn, int64_t s_sj, int *err,
+                                      void *stream) {
+    clear_error();
+    if (!scales || group < 1 || D % group != 0 || group % 4 != 0) {
+        set_error("jpeg_encode_grouped: needs scales and a group size that is a multiple of 4 "
+                  "dividing the head dim (got group %d, D %lld)", group, (long long)D);
+        return FC_EINVAL;
+    }
+    return jpeg_encode_impl(x, x_dtype, B, H, S, D, x_sb, x_sh, x_ss, basis, r, k, out, o_sb,
+                            o_sh, o_sn, o_sj, scales, scale_dtype, s_sb, s_sh, s_sn, s_sj, group,
+                            err, stream);
+}
+
+static int jpeg_decode_impl(const void *coef, int coef_dtype, int64_t B, int64_t H, int64_t n,
+                            int64_t D, int k, int64_t c_sb, int64_t c_sh, int64_t c_sn,
+                            int64_t c_sj, const void *scales, int scale_dtype, int64_t s_sb,
+                            int64_t s_sh, int64_t s_sn, int64_t s_sj, int group,
+                            const float *basis, int r, void *out, int out_dtype, int64_t out_len,
+                            int64_t o_sb, int64_t o_sh, int64_t o_ss, void *stream) {
     if (dtype_size(coef_dtype) == 0 || !is_float_dtype(out_dtype)) { set_error("jpeg_decode: bad dtype"); return FC_EINVAL; }
     if (coef_dtype == FC_I8 && !scales) { set_error("jpeg_decode: int8 codes need scales"); return FC_EINVAL; }
     if (scales && scale_dtype != FC_F32 && scale_dtype != FC_F16) { set_error("jpeg_decode: scale dtype must be f32 or f16"); return FC_EINVAL; }
@@ -673,9 +801,9 @@ extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64
     if (!coef || !basis || !out) { set_error("jpeg_decode: null pointer"); return FC_EINVAL; }
     const int es = dtype_size(coef_dtype);
     const bool v4 = (D % 4 == 0) && aligned(coef, 4 * es) && (c_sb % 4 == 0) && (c_sh % 4 == 0) &&
-                    (c_sn % 4 == 0) && (c_sj % 4 == 0);
+                    (c_sn % 4 == 0) && (c_sj % 4 == 0) && (group % 4 == 0);
     DecArgs a{coef, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales, scale_dtype, s_sb, s_sh, s_sn,
-              basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss};
+              s_sj, basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss, group};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned grid = grid_stride_for(B * H * n);
     // vector stores of 4 outputs when the output rows allow them
@@ -716,6 +844,35 @@ extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64
         }
         return check_launch("jpeg_decode");
     });
+}
+
+extern "C" int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64_t H, int64_t n,
+                              int64_t D, int k, int64_t c_sb, int64_t c_sh, int64_t c_sn,
+                              int64_t c_sj, const void *scales, int scale_dtype, int64_t s_sb,
+                              int64_t s_sh, int64_t s_sn, const float *basis, int r, void *out,
+                              int out_dtype, int64_t out_len, int64_t o_sb, int64_t o_sh,
+                              int64_t o_ss, void *stream) {
+    clear_error();
+    return jpeg_decode_impl(coef, coef_dtype, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales,
+                            scale_dtype, s_sb, s_sh, s_sn, 1, (int)std::max<int64_t>(D, 1), basis,
+                            r, out, out_dtype, out_len, o_sb, o_sh, o_ss, stream);
+}
+
+extern "C" int fc_jpeg_decode_grouped(const void *coef, int64_t B, int64_t H, int64_t n,
+                                      int64_t D, int k, int64_t c_sb, int64_t c_sh, int64_t c_sn,
+                                      int64_t c_sj, const void *scales, int scale_dtype,
+                                      int group, int64_t s_sb, int64_t s_sh, int64_t s_sn,
+                                      int64_t s_sj, const float *basis, int r, void *out,
+                                      int out_dtype, int64_t out_len, int64_t o_sb, int64_t o_sh,
+                                      int64_t o_ss, void *stream) {
+    clear_error();
+    if (!scales || group < 1 || D % group != 0) {
+        set_error("jpeg_decode_grouped: needs scales and a group size dividing the head dim");
+        return FC_EINVAL;
+    }
+    return jpeg_decode_impl(coef, FC_I8, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales,
+                            scale_dtype, s_sb, s_sh, s_sn, s_sj, group, basis, r, out, out_dtype,
+                            out_len, o_sb, o_sh, o_ss, stream);
 }
 
 extern "C" int fc_png_encode(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,

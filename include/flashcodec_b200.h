@@ -103,6 +103,42 @@ FC_API int fc_jpeg_decode(const void *coef, int coef_dtype, int64_t B, int64_t H
                    int64_t o_sb, int64_t o_sh, int64_t o_ss, void *stream);
 
 /*
+ * Per-group coefficient quantizer (the "per-32" format): fc_jpeg_encode with
+ * int8 codes and one scale per `group` channels of every (block, frequency)
+ * row instead of one per row -- the quantizer of
+ * docs/llama-cpp-kv-quantization.md:179-234 (absmax / 127 over each group of
+ * 32 coefficients, fed with the coefficients instead of raw rows), which the
+ * reference measured but ships no code for.  Within a group the arithmetic is
+ * quantize_coeffs' (codecs/jpeg.py:85-100): scale = x_dtype(amax / 127), 1
+ * if zero, code = clamp(rint(c / scale), +-127).
+ * group   channels per scale: a multiple of 4 that divides D (32 for per-32).
+ * scales  (B, H, n, k, D / group) of scale_dtype; strides s_sb, s_sh, s_sn,
+ *         s_sj (frequency); the group stride is 1.
+ * Other arguments as fc_jpeg_encode (codes only: `scales` is required).
+ */
+FC_API int fc_jpeg_encode_grouped(const void *x, int x_dtype, int64_t B, int64_t H, int64_t S,
+                                  int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_ss,
+                                  const float *basis, int r, int k,
+                                  void *out, int64_t o_sb, int64_t o_sh, int64_t o_sn,
+                                  int64_t o_sj, void *scales, int scale_dtype, int group,
+                                  int64_t s_sb, int64_t s_sh, int64_t s_sn, int64_t s_sj,
+                                  int *err, void *stream);
+
+/*
+ * Read path of the per-group format: fc_jpeg_decode of int8 codes whose
+ * scales are (B, H, n, k, D / group) (strides s_sb, s_sh, s_sn, s_sj; group
+ * stride 1); each code is dequantized with the scale of its group.  No
+ * counterpart in the reference (see fc_jpeg_encode_grouped).
+ */
+FC_API int fc_jpeg_decode_grouped(const void *coef, int64_t B, int64_t H, int64_t n, int64_t D,
+                                  int k, int64_t c_sb, int64_t c_sh, int64_t c_sn, int64_t c_sj,
+                                  const void *scales, int scale_dtype, int group, int64_t s_sb,
+                                  int64_t s_sh, int64_t s_sn, int64_t s_sj,
+                                  const float *basis, int r, void *out, int out_dtype,
+                                  int64_t out_len, int64_t o_sb, int64_t o_sh, int64_t o_ss,
+                                  void *stream);
+
+/*
  * png archive / filter.
  * Replaces flashcodec/codecs/png.py:36-60 (png_filter) and the png branch of
  * flashcodec/cache.py:137-140.
@@ -182,6 +218,32 @@ FC_API int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int
                    const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
                    const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
                    int scale_dtype,
+                   const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
+                   const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+                   int raw_dtype, int64_t n_raw,
+                   const float *A, float softmax_scale,
+                   void *out, int out_dtype, int64_t o_sb, int64_t o_sh,
+                   void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Decode attention over a per-group int8 archive (fc_jpeg_encode_grouped):
+ * the math of fc_decode_attn with every code dequantized by the scale of its
+ * group of `scale_group` channels -- the attention side of the per-32
+ * coefficient format (docs/llama-cpp-kv-quantization.md:179-234, no code in
+ * the reference).  k_scales / v_scales are (B, Hk, n_blocks, s, D /
+ * scale_group) with strides *_sb, *_sh, *_sn, *_sj (frequency) and group
+ * stride 1; scale_group must divide D.  The workspace is the one
+ * fc_decode_attn_workspace_size reports for the same sizes.  Runs the
+ * CUDA-core kernel (the tensor-core kernel takes one scale per row).
+ */
+FC_API int fc_decode_attn_grouped(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                   int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int s, int r,
+                   const void *k_rows, int64_t k_sb, int64_t k_sh, int64_t k_sn, int64_t k_sj,
+                   const void *v_rows, int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t v_sj,
+                   const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                   int64_t ks_sj,
+                   const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                   int64_t vs_sj, int scale_dtype, int scale_group,
                    const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
                    const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
                    int raw_dtype, int64_t n_raw,
@@ -277,6 +339,8 @@ typedef struct fc_append_stream {
                                 `scales` is non-NULL, else coefficients of the token dtype */
     void *scales;            /* (B, H, capacity, k) scales of scale_dtype, or NULL */
     int64_t capacity;        /* archive capacity in blocks */
+    int *err;                /* optional device int, set to 1 when an F16 scale of this
+                                stream cannot hold its value (as fc_jpeg_encode's err) */
 } fc_append_stream;
 
 /* Append one token to many jpeg streams in one launch: replaces the
@@ -288,14 +352,12 @@ typedef struct fc_append_stream {
  * `slot` (0 .. r-1) the token goes to.  When slot == r - 1 the completed
  * block -- raw rows 0 .. r-2 and the new token -- is written to archive
  * block `block` (< capacity) of every stream, bit-identical to
- * fc_jpeg_encode; `err` (optional device int) is set when an F16 scale
- * cannot hold its value.  The table is read on the host and passed to the
+ * fc_jpeg_encode.  The table is read on the host and passed to the
  * kernel by value (no device table); streams must not share buffers.
  * No counterpart in the reference beyond the per-stream calls it fuses. */
 FC_API int fc_append_tokens(const fc_append_stream *streams, int n_streams, int dtype,
                             int64_t B, int64_t H, int64_t D, int r, int k, int64_t slot,
-                            int64_t block, const float *basis, int scale_dtype, int *err,
-                            void *stream);
+                            int64_t block, const float *basis, int scale_dtype, void *stream);
 
 /* Batch gather for beam-search reordering: replaces the index_select +
  * copy-back of every stream tensor in _CodecStream.select_batch

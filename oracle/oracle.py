@@ -325,3 +325,25 @@ def reference_attention_int8_mt(q, kcodes, kscales, vcodes, vscales, kraw, vraw,
     if t:
         out += np.einsum("bhgt,bhtd->bhgd", logits[..., n * r:], vraw)
     return out.reshape(B, Hq, 1, D)
+
+
+# ------------------------------------------------------- per-group scale format
+def jpeg_quantize_grouped(coef: np.ndarray, group: int, dtype: str = "f32"):
+    """Per-group variant of quantize_coeffs (the per-32 coefficient quantizer
+    of docs/llama-cpp-kv-quantization.md:179-234, which the reference
+    measured but ships no code for): every run of ``group`` channels of a
+    (block, frequency) row is quantized exactly as quantize_coeffs
+    (flashcodec/codecs/jpeg.py:85-100) quantizes a whole row.  Returns int8
+    codes (..., D) and fp32 scales (..., D // group)."""
+    c = _f32(coef)
+    D = c.shape[-1]
+    assert D % group == 0
+    codes, scales = jpeg_quantize(c.reshape(*c.shape[:-1], D // group, group), dtype)
+    return codes.reshape(c.shape), scales.reshape(*c.shape[:-1], D // group)
+
+
+def dequantize_grouped(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """fp32 rows of a per-group archive: code * scale of its group (the fp32
+    product dequantize_coeffs forms, jpeg.py:103-105)."""
+    g = codes.shape[-1] // scales.shape[-1]
+    return _f32(codes.astype(np.float32) * np.repeat(_f32(scales), g, axis=-1))

@@ -130,6 +130,32 @@ def test_new_entry_points_validate_on_the_host(lib):
     assert lib.fc_selftest_noalloc_wait(0, None) == _lib.FC_EINVAL
 
 
+def test_grouped_entry_points_validate_on_the_host(lib):
+    """The per-group format's entry points refuse a group size that does not
+    divide the head dim (or is not a multiple of 4 for the archive) and a
+    missing scale tensor before any CUDA call."""
+    from flashcodec_b200 import _lib
+    d = ctypes.c_void_p(0x1000)
+    for group, sc in ((24, d), (6, d), (32, None)):
+        rc = lib.fc_jpeg_encode_grouped(d, _lib.FC_BF16, 1, 2, 64, 128, 0, 0, 128, d, 8, 2,
+                                        d, 0, 0, 0, 0, sc, _lib.FC_F32, group, 0, 0, 0, 0,
+                                        None, None)
+        assert rc == _lib.FC_EINVAL, group
+    assert lib.fc_jpeg_decode_grouped(d, 1, 2, 8, 128, 2, 0, 0, 0, 0, d, _lib.FC_F32, 48,
+                                      0, 0, 0, 0, d, 8, d, _lib.FC_BF16, 64, 0, 0, 0,
+                                      None) == _lib.FC_EINVAL
+
+    def attn(group, rows_scales=d):
+        return lib.fc_decode_attn_grouped(
+            d, _lib.FC_BF16, 1, 4, 128, 512, 128, 2, 8, 2, 8, d, 0, 0, 0, 0, d, 0, 0, 0, 0,
+            rows_scales, 0, 0, 0, 0, rows_scales, 0, 0, 0, 0, _lib.FC_F32, group,
+            None, 0, 0, 0, None, 0, 0, 0, _lib.FC_BF16, 0, d, 0.1, d, _lib.FC_BF16, 512, 128,
+            None, 0, None)
+    assert attn(0) == _lib.FC_EINVAL
+    assert attn(48) == _lib.FC_EINVAL          # does not divide D
+    assert attn(32, None) == _lib.FC_EINVAL    # int8 rows need scales
+
+
 def test_rope_kv_append_validates_on_the_host(lib):
     """fc_rope_kv_append refuses odd head dims, integer dtypes, a v without
     v_out and outputs overlapping an input or each other before any CUDA call; empty work is a no-op."""

@@ -253,3 +253,60 @@ def test_gather_batch_more_than_65535_slabs():
     odd = src[..., :5].contiguous()  # 5-byte rows: the byte-copy kernel
     dst = K.gather_batch(odd, idx, 3)
     assert torch.equal(dst, odd.index_select(0, idx))
+
+
+@pytest.mark.parametrize("dt,D,kw", [
+    (torch.bfloat16, 128, dict(keep_freqs=4, quant_bits=8)),
+    (torch.float32, 64, dict(keep_freqs=2, quant_bits=8)),
+    (torch.float16, 256, dict(keep_freqs=8, quant_bits=8, scale_dtype=torch.float16)),
+    (torch.bfloat16, 128, dict(keep_freqs=2)),                  # unquantized coefficients
+    (torch.float32, 36, dict(keep_freqs=3, quant_bits=8, block_size=16)),
+])
+def test_one_launch_append_equals_one_shot_archive(dt, D, kw):
+    """fc_append_tokens (append_layers: K and V of every layer in one launch,
+    block archive included) leaves every stream bit-identical to archiving
+    the whole sequence at once, through capacity doublings."""
+    import flashcodec_b200 as fc
+    kw = dict(kw)
+    r = kw.pop("block_size", 8)
+    L, Bb, Hh, S = 3, 2, 4, r * 40 + 5
+    g = torch.Generator(device=DEV).manual_seed(D)
+    ks = [torch.randn(Bb, Hh, S, D, generator=g, device=DEV).cumsum(-2).to(dt) for _ in range(L)]
+    vs = [torch.randn(Bb, Hh, S, D, generator=g, device=DEV).to(dt) for _ in range(L)]
+    c = fc.CodecKVCache("jpeg", block_size=r, **kw)
+    c.append_layers([k[:, :, :1] for k in ks], [v[:, :, :1] for v in vs])
+    for t in range(1, S):
+        c.append_layers([k[:, :, t:t + 1] for k in ks], [v[:, :, t:t + 1] for v in vs])
+    one = fc.CodecKVCache("jpeg", block_size=r, **kw)
+    for i in range(L):
+        one.append(ks[i], vs[i], i)
+    for i in range(L):
+        for a, b in ((c._keys[i], one._keys[i]), (c._values[i], one._values[i])):
+            n = b.n_blocks
+            assert a.n_blocks == n and a.n_archived == b.n_archived and a.seq_len == S
+            for x, y in zip(a._archive_tensors(), b._archive_tensors()):
+                assert torch.equal(x[:, :, :n], y[:, :, :n])
+            assert torch.equal(a.raw, b.raw)
+            assert a.scale_range_errors() == b.scale_range_errors()
+        assert torch.equal(c._keys[i].read(), one._keys[i].read())
+
+
+def test_one_launch_append_falls_back_when_layouts_differ():
+    """Streams at different raw positions cannot share a launch: append_layers
+    appends layer by layer and the result is unchanged."""
+    import flashcodec_b200 as fc
+    g = torch.Generator(device=DEV).manual_seed(2)
+    k = torch.randn(2, 4, 43, 64, generator=g, device=DEV).to(torch.bfloat16)
+    c = fc.CodecKVCache("jpeg", block_size=8, keep_freqs=2, quant_bits=8)
+    c.append(k[:, :, :5], k[:, :, :5], 0)
+    c.append(k[:, :, :3], k[:, :, :3], 1)           # layer 1 three tokens behind
+    for t in range(5, 40):
+        c.append_layers([k[:, :, t:t + 1], k[:, :, t - 2:t - 1]],
+                        [k[:, :, t:t + 1], k[:, :, t - 2:t - 1]])
+    one = fc.CodecKVCache("jpeg", block_size=8, keep_freqs=2, quant_bits=8)
+    one.append(k[:, :, :40], k[:, :, :40], 0)
+    one.append(k[:, :, :38], k[:, :, :38], 1)
+    for i in (0, 1):
+        assert torch.equal(c._keys[i].read(), one._keys[i].read())
+        n = one._keys[i].n_blocks
+        assert torch.equal(c._keys[i]._coeffs[:, :, :n], one._keys[i]._coeffs[:, :, :n])

@@ -153,16 +153,18 @@ def test_noalloc_status_reports_a_wait_that_gave_up():
 
 
 def test_noalloc_refuses_oversized_plans():
+    """A plan whose split partials exceed the fixed scratch is refused with
+    FC_ERANGE before any launch (64 sequences x 8 KV heads x 32768 blocks:
+    256 splits per unit, ~270 MB of partials)."""
     from flashcodec_b200 import _lib
     lib = _lib.load()
     dummy = ctypes.c_void_p(0x1000)
-    # a plan whose split partials exceed the fixed scratch: refused on the host
-    need = lib.fc_decode_attn_workspace_size(1024, 64, 8, 128, 1 << 20, 2, 8, 0)
-    assert need > (16 << 20)
+    B, Hq, Hk, n = 64, 32, 8, 32768
+    assert lib.fc_decode_attn_workspace_size(B, Hq, Hk, 128, n, 2, 8, 0) > (16 << 20)
     rc = lib.fc_decode_attn_noalloc(
-        dummy, _lib.FC_BF16, 1024, 64, 128, 64 * 128, 128, 8, 1 << 20, 2, 8, _lib.FC_I8,
+        dummy, _lib.FC_BF16, B, Hq, 128, Hq * 128, 128, Hk, n, 2, 8, _lib.FC_I8,
         dummy, 0, 0, 0, 0, dummy, 0, 0, 0, 0, dummy, 0, 0, 0, dummy, 0, 0, 0, _lib.FC_F32,
         None, 0, 0, 0, None, 0, 0, 0, _lib.FC_BF16, 0, dummy, 0.1, dummy, _lib.FC_BF16,
-        64 * 128, 128, None)
-    assert rc == _lib.FC_ERANGE
+        Hq * 128, 128, None)
+    assert rc == _lib.FC_ERANGE, lib.fc_last_error_string()
     assert b"scratch" in lib.fc_last_error_string()
