@@ -642,7 +642,7 @@ def run_decode_step(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     cfg = dict(CFG2, layers=args.layers or CFG2["layers"], B=args.batch or CFG2["B"])
-    layers = build_layers(cfg, 0, dev)
+    layers = build_layers(cfg, dev, (0, cfg["B"]))
     B, Hq, Hk, D = cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"]
     steps = args.steps
     for ks, vs, _ in layers:

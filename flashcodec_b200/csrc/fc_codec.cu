@@ -214,8 +214,25 @@ struct RawRows {  // R rows of 4 elements of T, as loaded (8 or 16 bytes per row
     W w[R];
 };
 
-template <typename T, int R, int KM>
-__global__ void __launch_bounds__(kWarpsPerCta * 32)
+// Round two fp32 values to T (bf16 / fp16: one paired conversion) and back.
+template <typename T>
+__device__ __forceinline__ void round_pair(float &a, float &b) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+        a = __low2float(p);
+        b = __high2float(p);
+    } else if constexpr (std::is_same<T, __half>::value) {
+        const __half2 p = __floats2half2_rn(a, b);
+        a = __low2float(p);
+        b = __high2float(p);
+    }
+}
+
+// DENSE: block rows are contiguous (x_ss == 128, the cache's layouts), so
+// the row offsets inside a block are compile-time constants.  EXACT: k == KM
+// (no per-frequency guards); ROWSCALE: one scale per row (group == 128).
+template <typename T, int R, int KM, bool DENSE, bool EXACT, bool ROWSCALE>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, (R == 8 && KM <= 4 && sizeof(T) == 2) ? 3 : 1)
 jpeg_encode_d128_kernel(EncArgs a) {
     using Rows = RawRows<T, R>;
     using W = typename Rows::W;
@@ -227,22 +244,36 @@ jpeg_encode_d128_kernel(EncArgs a) {
     constexpr int dt = Elem<T>::code;
     const bool quant = a.scales != nullptr;
     const int d0 = lane * 4;
-    // block counts are < 2^31 (host check): 32-bit index math
-    auto locate = [&](int64_t gw, int64_t &b, int64_t &h, int64_t &blk) {
-        const unsigned bh = (unsigned)gw / (unsigned)a.nblk;
-        blk = (int64_t)((unsigned)gw - bh * (unsigned)a.nblk);
-        b = bh / (unsigned)a.H;
-        h = bh % (unsigned)a.H;
+    const int64_t xs = DENSE ? 128 : a.x_ss;
+    const int kk = EXACT ? KM : a.k;  // kept frequencies
+    // (b, h, block) of this warp's first block (block counts are < 2^31,
+    // checked on the host: 32-bit index math); later blocks advance it
+    unsigned cb, ch, cblk;
+    {
+        const unsigned bh = (unsigned)g0 / (unsigned)a.nblk;
+        cblk = (unsigned)g0 - bh * (unsigned)a.nblk;
+        cb = bh / (unsigned)a.H;
+        ch = bh - cb * (unsigned)a.H;
+    }
+    auto advance = [&](unsigned &b, unsigned &h, unsigned &blk) {
+        if (++blk == (unsigned)a.nblk) {
+            blk = 0;
+            if (++h == (unsigned)a.H) { h = 0; ++b; }
+        }
     };
-    auto load_rows = [&](int64_t gw, Rows &rw) {
-        int64_t b, h, blk;
-        locate(gw, b, h, blk);
-        const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh + blk * R * a.x_ss + d0;
-        const int rows = (int)min((int64_t)R, a.S - blk * R);
+    auto load_rows = [&](unsigned b, unsigned h, unsigned blk, Rows &rw) {
+        const T *xb = static_cast<const T *>(a.x) + b * a.x_sb + h * a.x_sh +
+                      (int64_t)blk * R * xs + d0;
+        if ((int64_t)(blk + 1) * R <= a.S) {  // a whole block (every one but a ragged last)
 #pragma unroll
-        for (int i = 0; i < R; i++) {
-            if (i < rows) rw.w[i] = *reinterpret_cast<const W *>(xb + i * a.x_ss);
-            else rw.w[i] = W{};  // zero padding past S
+            for (int i = 0; i < R; i++) rw.w[i] = *reinterpret_cast<const W *>(xb + i * xs);
+        } else {
+            const int rows = (int)(a.S - (int64_t)blk * R);
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                if (i < rows) rw.w[i] = *reinterpret_cast<const W *>(xb + i * xs);
+                else rw.w[i] = W{};  // zero padding past S
+            }
         }
     };
     // the k x R basis in registers for all of this warp's blocks
@@ -250,17 +281,25 @@ jpeg_encode_d128_kernel(EncArgs a) {
 #pragma unroll
     for (int j = 0; j < KM; j++)
 #pragma unroll
-        for (int i = 0; i < R; i++) mb[j][i] = j < a.k ? __ldg(a.basis + j * R + i) : 0.0f;
+        for (int i = 0; i < R; i++) mb[j][i] = j < kk ? __ldg(a.basis + j * R + i) : 0.0f;
+    // scale groups: a group spans gl = group / 4 aligned lanes; lane p owns the
+    // scale of (frequency p / G, group p % G)
+    const int gl = ROWSCALE ? 32 : a.group >> 2, G = 32 / gl, mygrp = lane / gl;
+    const int pj = lane / G, pg = lane - pj * G;
     Rows next;
-    load_rows(g0, next);
+    unsigned nbb = cb, nbh = ch, nbk = cblk;  // block being loaded
+    load_rows(nbb, nbh, nbk, next);
     for (int e = 0; e < nb; e++) {
         const Rows cur = next;
-        if (e + 1 < nb) load_rows(g0 + e + 1, next);
+        if (e + 1 < nb) {
+            advance(nbb, nbh, nbk);
+            load_rows(nbb, nbh, nbk, next);
+        }
         float xv[R][4];
 #pragma unroll
         for (int i = 0; i < R; i++) load_vec_f32<T, 4>(reinterpret_cast<const T *>(&cur.w[i]), xv[i]);
-        int64_t b, h, blk;
-        locate(g0 + e, b, h, blk);
+        const int64_t b = cb, h = ch, blk = cblk;
+        advance(cb, ch, cblk);
         // coefficients of every kept frequency: sequential fp32 FMA chain
         // over the R samples, rounded to the input dtype (jpeg.py:66-67)
         float c[KM][4];
@@ -268,33 +307,33 @@ jpeg_encode_d128_kernel(EncArgs a) {
         for (int j = 0; j < KM; j++) {
 #pragma unroll
             for (int v = 0; v < 4; v++) c[j][v] = 0.0f;
-            if (j >= a.k) continue;
+            if (j >= kk) continue;
 #pragma unroll
             for (int i = 0; i < R; i++)
 #pragma unroll
                 for (int v = 0; v < 4; v++) c[j][v] = __fmaf_rn(xv[i][v], mb[j][i], c[j][v]);
-#pragma unroll
-            for (int v = 0; v < 4; v++) c[j][v] = round_to_dtype(c[j][v], dt);
+            round_pair<T>(c[j][0], c[j][1]);
+            round_pair<T>(c[j][2], c[j][3]);
         }
         const int64_t obase = b * a.o_sb + h * a.o_sh + blk * a.o_sn + d0;
         if (!quant) {
 #pragma unroll
             for (int j = 0; j < KM; j++)
-                if (j < a.k) store_vec_from_f32<T, 4>(static_cast<T *>(a.out) + obase + j * a.o_sj, c[j]);
+                if (j < kk) store_vec_from_f32<T, 4>(static_cast<T *>(a.out) + obase + j * a.o_sj, c[j]);
             continue;
         }
         // amax of each frequency row over each scale group of its channels
         // (the head dim when group == D): |c| bit patterns order like the
         // values (a NaN pattern is above every number, so NaN propagates like
-        // torch.amax).  A group spans gl = group / 4 aligned lanes.
-        const int gl = a.group >> 2, G = 32 / gl, mygrp = lane / gl;
+        // torch.amax)
         float amax[KM];
 #pragma unroll
         for (int j = 0; j < KM; j++) {
-            unsigned ab = 0u;
-#pragma unroll
-            for (int v = 0; v < 4; v++) ab = max(ab, __float_as_uint(c[j][v]) & 0x7fffffffu);
-            if (gl == 32) {
+            unsigned ab = max(max(__float_as_uint(c[j][0]) & 0x7fffffffu,
+                                  __float_as_uint(c[j][1]) & 0x7fffffffu),
+                              max(__float_as_uint(c[j][2]) & 0x7fffffffu,
+                                  __float_as_uint(c[j][3]) & 0x7fffffffu));
+            if (ROWSCALE || gl == 32) {
                 ab = __reduce_max_sync(0xffffffffu, ab);
             } else {
                 for (int o = 1; o < gl; o <<= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
@@ -302,10 +341,8 @@ jpeg_encode_d128_kernel(EncArgs a) {
             amax[j] = __uint_as_float(ab);
         }
         // scale = amax / 127 in the coefficient dtype, 1 where it is 0
-        // (jpeg.py:96-97): lane p computes the scale of (frequency p / G,
-        // group p % G) and its reciprocal once, every lane takes the ones it
-        // needs by shuffle
-        const int pj = lane / G, pg = lane - pj * G;
+        // (jpeg.py:96-97): each lane computes one (frequency, group) scale and
+        // its reciprocal, every lane takes the ones it needs by shuffle
         float mine = 0.0f;
 #pragma unroll
         for (int j = 0; j < KM; j++) {
@@ -315,33 +352,43 @@ jpeg_encode_d128_kernel(EncArgs a) {
         float sl = round_to_dtype(__fdiv_rn(mine, 127.0f), dt);
         if (!(sl > 0.0f)) sl = 1.0f;
         const float rl = __frcp_rn(sl);
-        // q = clamp(rint(c / scale), -127, 127) with the IEEE quotient: c * (1/scale)
-        // is within 2^-23 relative (|q| <= 128: 3e-5 absolute) of it, so both
-        // round to the same integer unless the product lies within 1e-4 of a
-        // half-integer.  Clamping before rounding is exact (the bounds are
-        // integers); adding 1.5 * 2^23 rounds half to even and leaves the
-        // code's two's-complement byte in the low byte of the sum.  A warp
-        // with any element near a half-integer (or a NaN / infinite product)
-        // redoes its block's rows with the IEEE quotient.
+        // q = clamp(rint(c / scale), -127, 127) with the IEEE quotient.  With
+        // y = c * (1/scale): |y - fl(c / scale)| <= 2^-23 |y| + half an ulp of
+        // the quotient <= 1.9e-5 for |y| <= 128, so both round to the same
+        // integer unless y lies within 3e-5 of a half-integer.  The row's
+        // largest |y| is 127 within the scale's rounding (2^-9 relative for a
+        // bf16 scale), and every |y| < 127.5 rounds to a code within +-127, so
+        // no clamp applies; adding 1.5 * 2^23 rounds half to even and leaves
+        // the code's two's-complement byte in the low byte of the sum.  A warp
+        // with any element near a half-integer, at or beyond 127.49 (a
+        // subnormal scale) or not finite redoes its block's rows with the IEEE
+        // quotient and the clamp.
         constexpr float kRound = 12582912.0f;
+        const float2 kR2 = make_float2(kRound, kRound), kNR2 = make_float2(-kRound, -kRound);
+        const float2 kM1 = make_float2(-1.0f, -1.0f);
         uint32_t packed[KM];
-        bool near_tie = false;
+        float tmax = 0.0f;   // largest |y - rint(y)| of this lane's elements
+        bool redo = false;
 #pragma unroll
         for (int j = 0; j < KM; j++) {
             const float rs = __shfl_sync(0xffffffffu, rl, j * G + mygrp);
-            uint32_t bytes[4];
-#pragma unroll
-            for (int v = 0; v < 4; v++) {
-                const float y = fminf(fmaxf(__fmul_rn(c[j][v], rs), -127.0f), 127.0f);
-                const float u = __fadd_rn(y, kRound);
-                const float t = __fsub_rn(y, __fsub_rn(u, kRound));   // in [-0.5, 0.5]
-                near_tie |= !(fabsf(t) < 0.4999f);
-                bytes[v] = __float_as_uint(u);
-            }
-            packed[j] = __byte_perm(__byte_perm(bytes[0], bytes[1], 0x0040),
-                                    __byte_perm(bytes[2], bytes[3], 0x0040), 0x5410);
+            // the largest |y| of the group is its amax times 1/scale (rounding
+            // is monotonic); NaN or infinite amax makes it NaN
+            redo |= !(__fmul_rn(amax[j], rs) < 127.49f);
+            const float2 r2 = make_float2(rs, rs);
+            const float2 y01 = __fmul2_rn(make_float2(c[j][0], c[j][1]), r2);
+            const float2 y23 = __fmul2_rn(make_float2(c[j][2], c[j][3]), r2);
+            const float2 u01 = __fadd2_rn(y01, kR2), u23 = __fadd2_rn(y23, kR2);
+            const float2 q01 = __fadd2_rn(u01, kNR2), q23 = __fadd2_rn(u23, kNR2);
+            const float2 t01 = __ffma2_rn(q01, kM1, y01), t23 = __ffma2_rn(q23, kM1, y23);  // exact
+            tmax = fmaxf(fmaxf(tmax, fabsf(t01.x)), fabsf(t01.y));
+            tmax = fmaxf(fmaxf(tmax, fabsf(t23.x)), fabsf(t23.y));
+            packed[j] = __byte_perm(__byte_perm(__float_as_uint(u01.x), __float_as_uint(u01.y), 0x0040),
+                                    __byte_perm(__float_as_uint(u23.x), __float_as_uint(u23.y), 0x0040),
+                                    0x5410);
         }
-        if (__any_sync(0xffffffffu, near_tie)) {
+        redo |= !(tmax < 0.49997f);
+        if (__any_sync(0xffffffffu, redo)) {
 #pragma unroll
             for (int j = 0; j < KM; j++) {
                 const float sc = __shfl_sync(0xffffffffu, sl, j * G + mygrp);
@@ -357,9 +404,9 @@ jpeg_encode_d128_kernel(EncArgs a) {
         }
 #pragma unroll
         for (int j = 0; j < KM; j++)
-            if (j < a.k)
+            if (j < kk)
                 *reinterpret_cast<uint32_t *>(static_cast<int8_t *>(a.out) + obase + j * a.o_sj) = packed[j];
-        if (pj < a.k) {
+        if (pj < kk) {
             const int64_t si = b * a.s_sb + h * a.s_sh + blk * a.s_sn + pj * a.s_sj + pg;
             if (a.scale_dtype == FC_F16) {
                 const __half hs = __float2half_rn(sl);
@@ -385,7 +432,8 @@ struct DecArgs {
     void *out;
     int out_dtype;
     int64_t out_len, o_sb, o_sh, o_ss;
-    int group;  // channels sharing one scale (D: one per row)
+    int group;        // channels sharing one scale (D: one per row)
+    int group_shift;  // log2(group) when group is a power of two (the d128 fast path)
 };
 
 // coefficients (B,H,n,k,D) -> (B,H,out_len,D); KM >= k coefficient registers.
@@ -479,7 +527,8 @@ jpeg_decode_d128_kernel(DecArgs a) {
             if (a.scales) {
                 // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
                 const float sc = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn +
-                                                           j * a.s_sj + d0 / a.group, a.scale_dtype);
+                                                           j * a.s_sj + (d0 >> a.group_shift),
+                                             a.scale_dtype);
                 const float2 s2 = make_float2(sc, sc);
                 const float2 p01 = __fmul2_rn(make_float2(c[j][0], c[j][1]), s2);
                 const float2 p23 = __fmul2_rn(make_float2(c[j][2], c[j][3]), s2);
@@ -736,10 +785,27 @@ static int jpeg_encode_impl(const void *x, int x_dtype, int64_t B, int64_t H, in
                 const int64_t total = B * H * nblk;
                 a.bpw = total >= (int64_t)kEncBlocks * kWarpsPerCta * num_sms() ? kEncBlocks : 1;
                 const unsigned g = grid_for((total + a.bpw - 1) / a.bpw);
-                if (r == 8 && k <= 4) jpeg_encode_d128_kernel<T, 8, 4><<<g, kWarpsPerCta * 32, 0, st>>>(a);
-                else if (r == 8) jpeg_encode_d128_kernel<T, 8, 8><<<g, kWarpsPerCta * 32, 0, st>>>(a);
-                else if (k <= 4) jpeg_encode_d128_kernel<T, 16, 4><<<g, kWarpsPerCta * 32, 0, st>>>(a);
-                else jpeg_encode_d128_kernel<T, 16, 8><<<g, kWarpsPerCta * 32, 0, st>>>(a);
+                // the common shapes (contiguous rows, one scale per row, k a
+                // power of two) get guard-free instantiations
+                const bool rowscale = !scales || group == 128;
+                auto go = [&](auto rr, auto km, auto exact, auto dense, auto rowsc) {
+                    jpeg_encode_d128_kernel<T, decltype(rr)::value, decltype(km)::value,
+                                            decltype(dense)::value, decltype(exact)::value,
+                                            decltype(rowsc)::value>
+                        <<<g, kWarpsPerCta * 32, 0, st>>>(a);
+                };
+                using I8 = std::integral_constant<int, 8>;
+                using I16 = std::integral_constant<int, 16>;
+                using I2 = std::integral_constant<int, 2>;
+                using I4 = std::integral_constant<int, 4>;
+                const std::true_type yes{};
+                const std::false_type no{};
+                if (x_ss == 128 && rowscale && r == 8 && k == 4) go(I8{}, I4{}, yes, yes, yes);
+                else if (x_ss == 128 && rowscale && r == 8 && k == 2) go(I8{}, I2{}, yes, yes, yes);
+                else if (r == 8 && k <= 4) go(I8{}, I4{}, no, no, no);
+                else if (r == 8) go(I8{}, I8{}, no, no, no);
+                else if (k <= 4) go(I16{}, I4{}, no, no, no);
+                else go(I16{}, I8{}, no, no, no);
                 return check_launch("jpeg_encode");
             }
             auto kern = !v4 ? jpeg_encode_kernel<T, 1, 0>
@@ -802,8 +868,10 @@ static int jpeg_decode_impl(const void *coef, int coef_dtype, int64_t B, int64_t
     const int es = dtype_size(coef_dtype);
     const bool v4 = (D % 4 == 0) && aligned(coef, 4 * es) && (c_sb % 4 == 0) && (c_sh % 4 == 0) &&
                     (c_sn % 4 == 0) && (c_sj % 4 == 0) && (group % 4 == 0);
+    int gshift = 0;
+    while ((1 << gshift) < group) gshift++;
     DecArgs a{coef, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales, scale_dtype, s_sb, s_sh, s_sn,
-              s_sj, basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss, group};
+              s_sj, basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss, group, gshift};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned grid = grid_stride_for(B * H * n);
     // vector stores of 4 outputs when the output rows allow them
