@@ -48,7 +48,7 @@ class FlashCodecLayer(_HFDynamicLayer):
     (flashcodec/cache.py:446-562)."""
 
     def __init__(self, mode="jpeg", block_size=8, keep_freqs=2, keep_ratio=1.0,
-                 quant_bits=0, scale_dtype=torch.float32):
+                 quant_bits=0, scale_dtype=torch.float32, group_size=None):
         if HAS_HF_CACHE:
             super().__init__()
         else:
@@ -56,7 +56,8 @@ class FlashCodecLayer(_HFDynamicLayer):
             self.is_initialized = False
         self.mode = mode
         self.codec = make_codec(mode, block_size, keep_freqs, keep_ratio,
-                                quant_bits=quant_bits, scale_dtype=scale_dtype)
+                                quant_bits=quant_bits, scale_dtype=scale_dtype,
+                                group_size=group_size)
         self._key_stream = _CodecStream(self.codec)
         self._value_stream = _CodecStream(self.codec)
 
@@ -193,16 +194,17 @@ class FlashCodecCache(_HFCache):
     """
 
     def __init__(self, mode="jpeg", block_size=8, keep_freqs=2, keep_ratio=1.0,
-                 quant_bits=0, scale_dtype=torch.float32):
+                 quant_bits=0, scale_dtype=torch.float32, group_size=None):
         if not HAS_HF_CACHE:
             raise ImportError("FlashCodecCache needs the transformers 5.x Cache "
                               "classes; use CodecKVCache without transformers")
         # a bad configuration raises here rather than at the first update
         make_codec(mode, block_size, keep_freqs, keep_ratio, quant_bits=quant_bits,
-                   scale_dtype=scale_dtype)
+                   scale_dtype=scale_dtype, group_size=group_size)
         super().__init__(layer_class_to_replicate=partial(
             FlashCodecLayer, mode=mode, block_size=block_size, keep_freqs=keep_freqs,
-            keep_ratio=keep_ratio, quant_bits=quant_bits, scale_dtype=scale_dtype))
+            keep_ratio=keep_ratio, quant_bits=quant_bits, scale_dtype=scale_dtype,
+            group_size=group_size))
         self.mode = mode
         self.codec_cfg = dict(block_size=block_size, keep_freqs=keep_freqs,
                               keep_ratio=keep_ratio, quant_bits=quant_bits)
@@ -215,7 +217,7 @@ class FlashCodecCache(_HFCache):
     @classmethod
     def from_config(cls, config, mode="jpeg", block_size=8, keep_freqs=2,
                     keep_ratio=1.0, quant_bits=0, per_layer=None,
-                    scale_dtype=torch.float32):
+                    scale_dtype=torch.float32, group_size=None):
         """One layer per decoder layer: full-attention layers get a codec
         layer, every other type its native transformers layer.  ``per_layer``
         maps a layer index to codec overrides, e.g.
@@ -227,7 +229,8 @@ class FlashCodecCache(_HFCache):
         types, window = _layer_types(decoder)
         per_layer = per_layer or {}
         base = dict(mode=mode, block_size=block_size, keep_freqs=keep_freqs,
-                    keep_ratio=keep_ratio, quant_bits=quant_bits, scale_dtype=scale_dtype)
+                    keep_ratio=keep_ratio, quant_bits=quant_bits, scale_dtype=scale_dtype,
+                    group_size=group_size)
         layers = []
         for i, ltype in enumerate(types):
             if ltype == "full_attention":

@@ -30,8 +30,9 @@ def _cache_factory(mode, block_size, kwargs, sink, config):
     codec = dict(keep_freqs=kwargs.get("keep_freqs", 2),
                  keep_ratio=kwargs.get("keep_ratio", 1.0),
                  quant_bits=kwargs.get("quant_bits", 0))
-    if "scale_dtype" in kwargs:
-        codec["scale_dtype"] = kwargs["scale_dtype"]
+    for opt in ("scale_dtype", "group_size"):
+        if opt in kwargs:
+            codec[opt] = kwargs[opt]
     per_layer = kwargs.get("per_layer")
 
     def make():
@@ -57,7 +58,8 @@ def apply_flash_codec(model, mode="jpeg", block_size=8, materialization_free=Fal
     """Give every ``generate(..., use_cache=True)`` / ``forward(use_cache=True)``
     call without ``past_key_values`` a codec cache.  kwargs: ``keep_freqs``
     (jpeg, default 2), ``quant_bits`` (0 or 8), ``keep_ratio`` (png, default
-    1.0), ``per_layer`` (codec overrides by layer index), ``scale_dtype``.
+    1.0), ``per_layer`` (codec overrides by layer index), ``scale_dtype``,
+    ``group_size`` (per-group scales of the int8 jpeg archive, e.g. 32).
     Returns the model; ``remove_flash_codec`` undoes it."""
     if getattr(model, "_flashcodec", None) is not None:
         warnings.warn("model is already patched with flashcodec, "

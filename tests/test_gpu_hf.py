@@ -277,3 +277,27 @@ def test_decode_step_logits_match_materialized_view(dtype, tol):
         assert torch.equal(lv._key_stream._coeffs[:, :, :3], lf._key_stream._coeffs[:, :, :3])
     err = ((a.float() - b.float()).abs().max() / a.float().abs().max()).item()
     assert err < tol, err
+
+
+def test_per32_decode_step_logits_match_materialized_view():
+    """The per-32 coefficient format (group_size=32) through the model: a
+    decode step on the archive (fc_decode_attn_grouped) gives the logits of
+    the same step over the reconstructed view (fc_jpeg_decode_grouped), from
+    the same archive."""
+    ids = prompt(batch=2, seed=4)
+    ids = torch.cat([ids, ids[:, :5], ids], dim=1)
+    nxt = ids[:, -1:]
+    cfg = dict(hidden=256, heads=2, kv_heads=1, dtype=torch.float32)
+    view_model, free_model = tiny_llama(**cfg), tiny_llama(**cfg)
+    fc.apply_codec_attention(free_model)
+    kw = dict(mode="jpeg", block_size=8, keep_freqs=4, quant_bits=8, group_size=32)
+    c_view, c_free = fc.FlashCodecCache(**kw), fc.FlashCodecCache(**kw)
+    with torch.no_grad():
+        view_model(input_ids=ids, past_key_values=c_view, use_cache=True)
+        free_model(input_ids=ids, past_key_values=c_free, use_cache=True)
+        a = view_model(input_ids=nxt, past_key_values=c_view, use_cache=True).logits[:, -1]
+        b = free_model(input_ids=nxt, past_key_values=c_free, use_cache=True).logits[:, -1]
+    ks = c_free.layers[0]._key_stream
+    assert ks._scales.shape[-1] == 128 // 32 and ks.codec.group_size == 32
+    err = ((a - b).abs().max() / a.abs().max()).item()
+    assert err < 1e-4, err
