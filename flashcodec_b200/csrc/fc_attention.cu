@@ -46,11 +46,8 @@ std::atomic<int> g_attn_kernel{FC_ATTN_AUTO};
 
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
-// bulk-copy ring depth: 4 stages of 8 KB for int8 codes, 3 of 16 KB otherwise
-__host__ __device__ constexpr int stages_for(int es) { return es >= 2 ? 3 : 4; }
-// bytes per ring buffer: 16 KB for 2- and 4-byte rows (each CTA barrier of
-// the ring loop then covers as many rows as an 8 KB stage of int8 codes)
-__host__ __device__ constexpr int stage_bytes_for(int es) { return es >= 2 ? 16384 : 8192; }
+constexpr int kStages = 4;            // bulk-copy ring depth
+constexpr int kStageBytes = 8192;     // bytes per ring buffer
 constexpr int kMaxRS = 64;            // r, s <= 64
 constexpr int kMaxD = 256;
 constexpr int kTargetChunk = 128;     // blocks per split (upper target)
@@ -140,8 +137,6 @@ attn_kernel(AttnArgs a) {
     const RT *kbase = static_cast<const RT *>(a.krows) + b * a.k_sb + hk * a.k_sh + n0 * a.k_sn;
     const RT *vbase = static_cast<const RT *>(a.vrows) + b * a.v_sb + hk * a.v_sh + n0 * a.v_sn;
     const int64_t row_elems = a.D;  // contiguous row length in the bulk layout
-    constexpr int kSB = stage_bytes_for((int)sizeof(RT));
-    constexpr int kST = stages_for((int)sizeof(RT));
     const unsigned blk_bytes = (unsigned)(s * a.D * sizeof(RT));
     const int ntiles = BULK ? (nb + a.tb - 1) / a.tb : 0;
     const int ttot = 2 * ntiles;
@@ -151,9 +146,9 @@ attn_kernel(AttnArgs a) {
         const int tt = t < ntiles ? t : t - ntiles;
         const int blocks = min(a.tb, nb - tt * a.tb);
         const RT *src = (t < ntiles ? kbase : vbase) + (int64_t)tt * a.tb * s * row_elems;
-        uint64_t *bar = bars + (t % kST);
+        uint64_t *bar = bars + (t % kStages);
         mbar_expect_tx(bar, blocks * blk_bytes);
-        bulk_g2s(ring + (t % kST) * kSB, src, blocks * blk_bytes, bar);
+        bulk_g2s(ring + (t % kStages) * kStageBytes, src, blocks * blk_bytes, bar);
     };
     // Tiles [0, issued) have been requested (only thread 0 tracks this).  On
     // an abort, thread 0 waits -- bounded again -- for the copies still in
@@ -162,20 +157,20 @@ attn_kernel(AttnArgs a) {
     auto drain = [&](int from) {
         if (tid != 0) return;
         for (int u = from; u < issued; u++) {
-            uint64_t *bar = bars + (u % kST);
+            uint64_t *bar = bars + (u % kStages);
             const uint64_t t0 = global_ns();
-            while (!mbar_try_wait(bar, (u / kST) & 1) && global_ns() - t0 < kWaitNs) {
+            while (!mbar_try_wait(bar, (u / kStages) & 1) && global_ns() - t0 < kWaitNs) {
             }
         }
     };
 
     if (BULK && tid == 0) {
-        for (int i = 0; i < kST; i++) mbar_init(bars + i, 1);
+        for (int i = 0; i < kStages; i++) mbar_init(bars + i, 1);
         fence_mbar_init();
     }
     __syncthreads();
     if (BULK && tid == 0)
-        for (; issued < min(kST, ttot); issued++) issue(issued);
+        for (; issued < min(kStages, ttot); issued++) issue(issued);
 
     // small per-CTA operands: A, the chunk's scales
     for (int i = tid; i < r * s; i += kThreads) sA[i] = a.A ? a.A[i] : 0.0f;
@@ -386,10 +381,10 @@ attn_kernel(AttnArgs a) {
     int t_cur = 0;  // next ring tile to consume
     if (BULK) {
         for (int t = 0; t < ntiles; t++, t_cur++) {
-            const bool ok = mbar_wait_bounded(bars + (t % kST), (t / kST) & 1, a.status,
+            const bool ok = mbar_wait_bounded(bars + (t % kStages), (t / kStages) & 1, a.status,
                                               a.epoch);
             if (__syncthreads_or(!ok)) { drain(t); return; }
-            const RT *tile = reinterpret_cast<const RT *>(ring + (t % kST) * kSB);
+            const RT *tile = reinterpret_cast<const RT *>(ring + (t % kStages) * kStageBytes);
             const int trows = min(a.tb, nb - t * a.tb) * s;
             for (int base = 0; base < trows; base += rows_per_pass * U) {
                 float x[U][NCH][VEC];
@@ -412,7 +407,7 @@ attn_kernel(AttnArgs a) {
                 store_scores(v, off, base, trows, t * a.tb * s);
             }
             __syncthreads();
-            if (tid == 0 && t + kST < ttot) issue(issued++);
+            if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
     } else if (s % U == 0) {
         // block-major: each lane group takes whole blocks, U of its rows at a
@@ -581,10 +576,10 @@ attn_kernel(AttnArgs a) {
 
     if (BULK) {
         for (int t = ntiles; t < ttot; t++) {
-            const bool ok = mbar_wait_bounded(bars + (t % kST), (t / kST) & 1, a.status,
+            const bool ok = mbar_wait_bounded(bars + (t % kStages), (t / kStages) & 1, a.status,
                                               a.epoch);
             if (__syncthreads_or(!ok)) { drain(t); return; }
-            const RT *tile = reinterpret_cast<const RT *>(ring + (t % kST) * kSB);
+            const RT *tile = reinterpret_cast<const RT *>(ring + (t % kStages) * kStageBytes);
             const int tv = t - ntiles;
             const int trows = min(a.tb, nb - tv * a.tb) * s;
             for (int base = 0; base < trows; base += rows_per_pass) {
@@ -592,7 +587,7 @@ attn_kernel(AttnArgs a) {
                 if (row < trows) accum_typed(tile + (int64_t)row * row_elems, tv * a.tb * s + row);
             }
             __syncthreads();
-            if (tid == 0 && t + kST < ttot) issue(issued++);
+            if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
     } else if (s % U == 0) {
         // block-major, as in pass 1
@@ -823,7 +818,7 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     {
         const size_t fixed = (size_t)r * s * 4 + (size_t)kWarps * p.GT * D * 4 +
                              (size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4 +
-                             (vec_mode == 2 ? (size_t)stages_for(es) * (stage_bytes_for(es) + 8) : 0) +
+                             (vec_mode == 2 ? (size_t)kStages * (kStageBytes + 8) : 0) +
                              (size_t)2 * (n_raw + 1) * p.GT * 4 + 8 * 128;
         const size_t per_block = ((size_t)2 * s + (size_t)(s + r) * p.GT) * 4;
         const size_t cap = fixed < kSmemBudget ? (kSmemBudget - fixed) / per_block : 1;
@@ -834,7 +829,7 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
         }
     }
     const int64_t blk_bytes = (int64_t)s * D * es;
-    p.tb = (int)std::max<int64_t>(1, std::min<int64_t>(stage_bytes_for(es) / blk_bytes, p.chunk > 0 ? p.chunk : 1));
+    p.tb = (int)std::max<int64_t>(1, std::min<int64_t>(kStageBytes / blk_bytes, p.chunk > 0 ? p.chunk : 1));
     // shared memory carve-up
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 128); return (int)o; };
@@ -846,8 +841,8 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     p.off_lg = take(((size_t)std::max(p.chunk, 1) * r + raw_max) * p.GT * 4);
     p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4, (size_t)(p.n_split + 1) * p.GT * 4));
     p.off_stat = take((size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4);
-    p.off_ring = take(vec_mode == 2 ? (size_t)stages_for(es) * stage_bytes_for(es) : 0);
-    p.off_bar = take(vec_mode == 2 ? (size_t)stages_for(es) * 8 : 0);
+    p.off_ring = take(vec_mode == 2 ? (size_t)kStages * kStageBytes : 0);
+    p.off_bar = take(vec_mode == 2 ? (size_t)kStages * 8 : 0);
     p.smem = off;
     // workspace: header | counters | pm | pl | pacc
     p.ws = workspace_for(units, p.n_split, p.GT, D);
@@ -869,7 +864,7 @@ int pick_vec_mode(int64_t D, int es, const void *k, const void *v, int64_t k_sb,
         return 0;
     const bool contig = k_sj == D && k_sn == (int64_t)s * D && v_sj == D && v_sn == (int64_t)s * D;
     // the bulk ring needs every block's rows to fit one stage buffer
-    const bool fits = (int64_t)s * D * es <= stage_bytes_for(es);
+    const bool fits = (int64_t)s * D * es <= kStageBytes;
     return (contig && fits) ? 2 : 1;
 }
 
