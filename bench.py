@@ -875,31 +875,53 @@ def main():
     kern_max = ms_compute / len(layers)
     status = K.attn_status(dev)
 
-    # end to end through the public API with host buffers: H2D of every
-    # layer's query from pinned memory, the attention calls (and the output
-    # gather when heads are split), D2H of the step's outputs
+    # end to end through the public API with host buffers: every step copies
+    # each layer's query from pinned host memory (H2D) and reads each layer's
+    # output back (D2H).  The copies run on two copy streams, layer by layer,
+    # so they overlap the attention launches of the other layers; the timed
+    # region ends when the last output has landed in host memory.
     qh = torch.stack([q for _, _, q in layers]).cpu().pin_memory()
     res = full if gather else outs
     oh = torch.empty((len(layers),) + tuple(res[0].shape), dtype=res[0].dtype).pin_memory()
     qd = torch.empty_like(qh, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    nl = len(layers)
+    ev_in = [torch.cuda.Event() for _ in range(nl)]
+    ev_done = [torch.cuda.Event() for _ in range(nl)]
+    first = [True]
 
     def e2e_step():
-        qd.copy_(qh, non_blocking=True)
+        for i in range(nl):
+            with torch.cuda.stream(s_in):
+                if not first[0]:
+                    s_in.wait_event(ev_done[i])     # the last step's attention read qd[i]
+                qd[i].copy_(qh[i], non_blocking=True)
+                ev_in[i].record(s_in)
         for i, (ks, vs, _) in enumerate(layers):
+            stream.wait_event(ev_in[i])
             outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
             if gather:
                 full[i] = sharding.gather_outputs(plan, outs[i])
-        oh.copy_(torch.stack(full if gather else outs), non_blocking=True)
+            r = full[i] if gather else outs[i]
+            ev_done[i].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[i])
+                oh[i].copy_(r, non_blocking=True)
+                r.record_stream(s_out)
+        first[0] = False
 
     for _ in range(2):
         e2e_step()
+    torch.cuda.synchronize()
     barrier(world)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_steps = max(1, args.steps // 3)
-    stream = torch.cuda.current_stream(dev)
     e_start.record(stream)
+    s_in.wait_event(e_start)
     for _ in range(e_steps):
         e2e_step()
+    stream.wait_stream(s_out)
     e_end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
