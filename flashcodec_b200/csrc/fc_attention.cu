@@ -839,7 +839,8 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     p.off_vsc = take((size_t)std::max(p.chunk, 1) * s * 4);
     p.off_sc = take(((size_t)std::max(p.chunk, 1) * s + raw_max) * p.GT * 4);
     p.off_lg = take(((size_t)std::max(p.chunk, 1) * r + raw_max) * p.GT * 4);
-    p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4, (size_t)(p.n_split + 1) * p.GT * 4));
+    p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4,
+                              (size_t)merge_scratch_floats(p.n_split, p.GT, kThreads) * 4));
     p.off_stat = take((size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4);
     p.off_ring = take(vec_mode == 2 ? (size_t)kStages * kStageBytes : 0);
     p.off_bar = take(vec_mode == 2 ? (size_t)kStages * 8 : 0);

@@ -743,7 +743,10 @@ int tc_ctas_per_sm(int GT) { return GT <= 4 ? 4 : 3; }
 // drain, and CTAs of a second wave run behind an idle tail, so the plan takes
 // the most splits per (batch, KV head) unit that still fit one wave of
 // resident CTAs, in whole 128-row tiles, and at most 1024 splits per unit (the
-// merge scratch, (n_split + 1) x 8 floats, lives in the 48 KB tile ring).
+// merge scratch, merge_scratch_floats(n_split, 8, 160) floats, lives in the
+// 48 KB tile ring after its first KB).
+static_assert(merge_scratch_floats(1024, 8, kTcThreads) * 4 + 1024 <= kTcStages * kTileBytes,
+              "merge scratch must fit the tile ring");
 void tc_plan(int64_t n, int s, int64_t units, int GT, int &n_split, int &chunk) {
     const int64_t tiles = std::max<int64_t>(1, (n * s + kTileRows - 1) / kTileRows);
     int64_t ct = chunk_tiles_override();

@@ -156,33 +156,74 @@ __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t gr
     __syncthreads();
     if (!*s_flag) return;
     __threadfence();
-    float *fac = scratch;
-    float *Ls = scratch + P.n_split * P.GT;
-    if (tid < P.GT) {
+    // The whole CTA merges: split maxima staged in shared memory, per-thread
+    // partial maxima and sums reduced by shuffles, the output loop over the
+    // splits unrolled so its loads overlap (merge_scratch_floats sizes the
+    // scratch).  Every thread serves head g = tid % GT (nthr % GT == 0).
+    const int n = P.n_split, GT = P.GT, lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+    const int64_t base = grp * (int64_t)n * GT;  // partial slots of this group: [n][GT]
+    float *fac = scratch;                         // [n][GT] split maxima, then factors
+    float *Ms = scratch + n * GT;                 // [GT]
+    float *Ls = Ms + GT;                          // [GT]
+    float *wp = Ls + GT;                          // [nw][GT] per-warp partials
+    const int g = tid % GT;
+    float m = -INFINITY;
+    for (int idx = tid; idx < n * GT; idx += nthr) {
+        const float v = __ldcg(P.pm + base + idx);
+        fac[idx] = v;
+        m = fmaxf(m, v);
+    }
+    for (int off = 16; off >= GT; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if (lane < GT) wp[warp * GT + lane] = m;
+    __syncthreads();
+    if (tid < GT) {
         float M = -INFINITY;
-        for (int i = 0; i < P.n_split; i++)
-            M = fmaxf(M, __ldcg(P.pm + (grp * P.n_split + i) * P.GT + tid));
+        for (int w = 0; w < nw; w++) M = fmaxf(M, wp[w * GT + tid]);
+        Ms[tid] = M;
+    }
+    __syncthreads();
+    const float M = Ms[g];
+    float l = 0.0f;
+    for (int idx = tid; idx < n * GT; idx += nthr) {
+        const float f = M == -INFINITY ? 0.0f : exp2f(fac[idx] - M);
+        fac[idx] = f;
+        l = fmaf(__ldcg(P.pl + base + idx), f, l);
+    }
+    for (int off = 16; off >= GT; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (lane < GT) wp[nw * GT + warp * GT + lane] = l;
+    __syncthreads();
+    if (tid < GT) {
         float L = 0.0f;
-        for (int i = 0; i < P.n_split; i++) {
-            const int64_t si = (grp * P.n_split + i) * P.GT + tid;
-            const float f = M == -INFINITY ? 0.0f : exp2f(__ldcg(P.pm + si) - M);
-            fac[i * P.GT + tid] = f;
-            L += __ldcg(P.pl + si) * f;
-        }
+        for (int w = 0; w < nw; w++) L += wp[nw * GT + w * GT + tid];
         Ls[tid] = L;
     }
     __syncthreads();
-    for (int idx = tid; idx < P.GT * P.D; idx += nthr) {
-        const int g = idx / (int)P.D;
+    const int64_t step = (int64_t)GT * P.D;  // between the slots of one (head, channel)
+    for (int idx = tid; idx < GT * P.D; idx += nthr) {
+        const int gg = idx / (int)P.D;
         const int64_t d = idx % P.D;
-        if (g >= grun) continue;
-        float o = 0.0f;
-        for (int i = 0; i < P.n_split; i++)
-            o = fmaf(__ldcg(P.pacc + ((grp * P.n_split + i) * P.GT + g) * P.D + d), fac[i * P.GT + g], o);
+        if (gg >= grun) continue;
+        const float *pa = P.pacc + (base + gg) * P.D + d;
+        float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
+        int i = 0;
+        for (; i + 4 <= n; i += 4) {
+            o0 = fmaf(__ldcg(pa + (int64_t)i * step), fac[i * GT + gg], o0);
+            o1 = fmaf(__ldcg(pa + (int64_t)(i + 1) * step), fac[(i + 1) * GT + gg], o1);
+            o2 = fmaf(__ldcg(pa + (int64_t)(i + 2) * step), fac[(i + 2) * GT + gg], o2);
+            o3 = fmaf(__ldcg(pa + (int64_t)(i + 3) * step), fac[(i + 3) * GT + gg], o3);
+        }
+        for (; i < n; i++) o0 = fmaf(__ldcg(pa + (int64_t)i * step), fac[i * GT + gg], o0);
+        const float o = (o0 + o1) + (o2 + o3);
         // Ls == 0 only when every position of the group was masked out
-        store_from_f32(out, o_base + (hq0 + g) * o_sh + d, out_dtype, Ls[g] > 0.0f ? o / Ls[g] : 0.0f);
+        store_from_f32(out, o_base + (hq0 + gg) * o_sh + d, out_dtype, Ls[gg] > 0.0f ? o / Ls[gg] : 0.0f);
     }
     if (tid == 0) P.cnt[grp] = 0;  // ready for the next launch
+}
+
+// Floats of shared scratch merge_last_arriver needs for n_split splits, GT
+// heads and nthr threads.
+__host__ __device__ constexpr int64_t merge_scratch_floats(int64_t n_split, int GT, int nthr) {
+    return (n_split + 2 + 2 * (nthr / 32)) * GT;
 }
 
 }  // namespace fc

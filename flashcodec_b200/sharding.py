@@ -89,11 +89,15 @@ def gather_outputs(plan: ShardPlan, out_local: torch.Tensor, group=None) -> torc
     import torch.distributed as dist
     world = plan.world
     if plan.mode == "heads":
-        pieces = [torch.empty_like(out_local) for _ in range(world)]
-        dist.all_gather(pieces, out_local.contiguous(), group=group)
-        per_row = world // plan.B
-        rows = [torch.cat(pieces[b * per_row:(b + 1) * per_row], dim=1) for b in range(plan.B)]
-        return torch.cat(rows, dim=0)
+        # ranks are ordered batch row first, then KV-head group, and a rank's
+        # query heads are one contiguous range, so the rank-major gather of
+        # the (1, Hq_local, 1, D) pieces *is* the (B, Hq, 1, D) output: one
+        # collective into one buffer, no copies afterwards
+        piece = out_local.contiguous()
+        full = torch.empty((world,) + tuple(piece.shape[1:]), dtype=piece.dtype,
+                           device=piece.device)
+        dist.all_gather_into_tensor(full, piece, group=group)
+        return full.view(plan.B, plan.Hq, *piece.shape[2:])
     sizes = [plan.batch_range(r)[1] - plan.batch_range(r)[0] for r in range(world)]
     cap = max(sizes)
     padded = torch.zeros((cap,) + tuple(out_local.shape[1:]), dtype=out_local.dtype,
