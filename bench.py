@@ -783,6 +783,10 @@ def main():
                     help="archive format of the attention workload: jpeg-int8 (default, the "
                          "headline), jpeg-fp (quant_bits=0, bf16 coefficients) or png "
                          "(r=8, lossless; 4 layers by default)")
+    ap.add_argument("--graph", action="store_true",
+                    help="time the step as a CUDA graph replay of its attention launches "
+                         "(captured once after warm-up; not with split heads); the oracle "
+                         "check and e2e stay eager")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true",
                     help="skip the post-timing oracle check (profiling runs only)")
@@ -841,13 +845,18 @@ def main():
             if with_gather:
                 full[i] = sharding.gather_outputs(plan, outs[i])
 
+    graph = None
+
     def timed(steps, with_gather=gather):
         stream = torch.cuda.current_stream(dev)
         barrier(world)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(steps):
-            step(with_gather)
+            if graph is not None:
+                graph.replay()
+            else:
+                step(with_gather)
         end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
@@ -855,6 +864,16 @@ def main():
 
     for _ in range(args.warmup):
         step()
+    if args.graph and not gather:
+        # one step's launches captured once (the kernels' shared-memory
+        # opt-ins were set by the warm-up) and replayed as one graph per step
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(False)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
     sampler = ClockSampler(list(range(max(world, 1)))) if rank == 0 else None
     if sampler:
         sampler.start()
@@ -873,7 +892,8 @@ def main():
     ms_max = max_over_ranks(ms, world)
     ms_compute = max_over_ranks(timed(max(1, args.steps // 2), False), world) if gather else ms_max
     kern_max = ms_compute / len(layers)
-    status = K.attn_status(dev)
+    # status words of every workspace used (the graph's capture stream has its own)
+    status = max([int(w[:4].view(torch.int32).item()) for w in K._workspaces.values()] or [0])
 
     # end to end through the public API with host buffers: every step copies
     # each layer's query from pinned host memory (H2D) and reads each layer's
@@ -916,7 +936,7 @@ def main():
     torch.cuda.synchronize()
     barrier(world)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_steps = max(1, args.steps // 3)
+    e_steps = max(5, args.steps // 2)
     e_start.record(stream)
     s_in.wait_event(e_start)
     for _ in range(e_steps):
@@ -964,7 +984,10 @@ def main():
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": "strong" if plan is not None else "weak",
             "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic", "config": workload_config(cfg, world, plan, Bg),
+            "data": "synthetic",
+            "config": dict(workload_config(cfg, world, plan, Bg),
+                           timed_as="CUDA graph replay of the step" if graph is not None
+                           else "eager launches"),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": per_launch,
