@@ -845,7 +845,7 @@ def main():
             if with_gather:
                 full[i] = sharding.gather_outputs(plan, outs[i])
 
-    graph = None
+    graphs = {}   # with_gather -> CUDA graph of one step (--graph)
 
     def timed(steps, with_gather=gather):
         stream = torch.cuda.current_stream(dev)
@@ -853,8 +853,8 @@ def main():
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(steps):
-            if graph is not None:
-                graph.replay()
+            if with_gather in graphs:
+                graphs[with_gather].replay()
             else:
                 step(with_gather)
         end.record(stream)
@@ -864,16 +864,22 @@ def main():
 
     for _ in range(args.warmup):
         step()
-    if args.graph and not gather:
-        # one step's launches captured once (the kernels' shared-memory
-        # opt-ins were set by the warm-up) and replayed as one graph per step
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step(False)
-        for _ in range(2):
-            graph.replay()
-        torch.cuda.synchronize()
+    if args.graph:
+        # one step's launches (and, with split heads, its NCCL all-gathers)
+        # captured once after the warm-up -- the kernels' shared-memory
+        # opt-ins and the communicator exist by then -- and replayed as one
+        # graph per step; every rank captures the same collectives in order
+        for wg in ([True, False] if gather else [False]):
+            torch.cuda.synchronize()
+            barrier(world)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                step(wg)
+            graphs[wg] = g
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+        barrier(world)
     sampler = ClockSampler(list(range(max(world, 1)))) if rank == 0 else None
     if sampler:
         sampler.start()
@@ -986,7 +992,7 @@ def main():
             "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic",
             "config": dict(workload_config(cfg, world, plan, Bg),
-                           timed_as="CUDA graph replay of the step" if graph is not None
+                           timed_as="CUDA graph replay of the step" if graphs
                            else "eager launches"),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": kind,
@@ -1011,6 +1017,8 @@ def main():
                 "allgather_bytes_per_rank_per_layer": outs[0].numel() * outs[0].element_size(),
                 "note": "all_gather time = step time with the gather minus the step without it"}
         print(json.dumps(line), flush=True)
+    graphs.clear()           # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

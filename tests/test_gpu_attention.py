@@ -298,3 +298,25 @@ def test_png_attention_reads_archive_in_place(dt, r, keep, tail):
     out = fc.codec_decode_attention(q.to(DEV), ks, vs)
     assert out.dtype == dt
     check_close(out, oracle_attention(q, ks, vs), dt)
+
+
+def test_decode_attention_replays_in_a_cuda_graph():
+    """A decode step's attention calls can be captured once and replayed as
+    a CUDA graph (what a serving loop does to remove per-call host work): the
+    replay gives bit-identical outputs to eager calls, also after the static
+    query buffer is refilled."""
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(2, 32, 8, 8 * 300 + 5, 128, 0.95, 9, device=DEV,
+                               dtype=torch.bfloat16)
+    ks, vs = build("jpeg", dict(keep_freqs=4, quant_bits=8), k, v)
+    q_static = q.clone()
+    fc.codec_decode_attention(q_static, ks, vs)          # warm-up outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = fc.codec_decode_attention(q_static, ks, vs)
+    for seed in (10, 11):
+        q_static.copy_(bench.synth_query(2, 32, 128, seed, device=DEV, dtype=torch.bfloat16))
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, fc.codec_decode_attention(q_static, ks, vs))
