@@ -434,6 +434,7 @@ struct DecArgs {
     int64_t out_len, o_sb, o_sh, o_ss;
     int group;        // channels sharing one scale (D: one per row)
     int group_shift;  // log2(group) when group is a power of two (the d128 fast path)
+    int bpw;          // blocks per warp of the d128 fast path
 };
 
 // coefficients (B,H,n,k,D) -> (B,H,out_len,D); KM >= k coefficient registers.
@@ -511,25 +512,53 @@ jpeg_decode_kernel(DecArgs a) {
 template <typename CT, int R, int KM, typename OT>
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 jpeg_decode_d128_kernel(DecArgs a) {
+    // a.bpw consecutive blocks per warp (one in launches smaller than a
+    // wave); the next block's codes and scales are loaded while the current
+    // one is synthesised and stored
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t gw = (int64_t)blockIdx.x * kWarpsPerCta + warp;
-    if (gw >= a.B * a.H * a.n) return;
+    const int64_t total = a.B * a.H * a.n;
+    const int64_t g0 = ((int64_t)blockIdx.x * kWarpsPerCta + warp) * a.bpw;
+    if (g0 >= total) return;
+    const int nb = (int)min((int64_t)a.bpw, total - g0);
     const int d0 = lane * 4;
-    const unsigned bh = (unsigned)gw / (unsigned)a.n;  // < 2^31 blocks (host check)
-    const int64_t blk = (int64_t)((unsigned)gw - bh * (unsigned)a.n);
-    const int64_t b = bh / (unsigned)a.H, h = bh % (unsigned)a.H;
-    const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh + blk * a.c_sn + d0;
-    float c[KM][4];
+    using W = typename std::conditional<sizeof(CT) == 1, uint32_t,
+              typename std::conditional<sizeof(CT) == 2, uint2, uint4>::type>::type;
+    // (b, h, block) of the block being loaded (< 2^31 blocks, host check)
+    unsigned lb, lh, lk;
+    {
+        const unsigned bh = (unsigned)g0 / (unsigned)a.n;
+        lk = (unsigned)g0 - bh * (unsigned)a.n;
+        lb = bh / (unsigned)a.H;
+        lh = bh - lb * (unsigned)a.H;
+    }
+    W wnext[KM];
+    float snext[KM];
+    auto load = [&](unsigned b, unsigned h, unsigned blk) {
+        const CT *cb = static_cast<const CT *>(a.coef) + b * a.c_sb + h * a.c_sh +
+                       (int64_t)blk * a.c_sn + d0;
 #pragma unroll
-    for (int j = 0; j < KM; j++) {
-        if (j < a.k) {
-            load_vec_f32<CT, 4>(cb + j * a.c_sj, c[j]);
+        for (int j = 0; j < KM; j++) {
+            wnext[j] = W{};
+            snext[j] = 1.0f;
+            if (j < a.k) {
+                wnext[j] = *reinterpret_cast<const W *>(cb + j * a.c_sj);
+                if (a.scales)
+                    snext[j] = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + (int64_t)blk * a.s_sn +
+                                                         j * a.s_sj + (d0 >> a.group_shift),
+                                           a.scale_dtype);
+            }
+        }
+    };
+    load(lb, lh, lk);
+    for (int e = 0; e < nb; e++) {
+        const unsigned b = lb, h = lh, blk = lk;
+        float c[KM][4];
+#pragma unroll
+        for (int j = 0; j < KM; j++) {
+            load_vec_f32<CT, 4>(reinterpret_cast<const CT *>(&wnext[j]), c[j]);
             if (a.scales) {
                 // dequantize_coeffs: q.float() * scale.float() (jpeg.py:105)
-                const float sc = load_as_f32(a.scales, b * a.s_sb + h * a.s_sh + blk * a.s_sn +
-                                                           j * a.s_sj + (d0 >> a.group_shift),
-                                             a.scale_dtype);
-                const float2 s2 = make_float2(sc, sc);
+                const float2 s2 = make_float2(snext[j], snext[j]);
                 const float2 p01 = __fmul2_rn(make_float2(c[j][0], c[j][1]), s2);
                 const float2 p23 = __fmul2_rn(make_float2(c[j][2], c[j][3]), s2);
                 c[j][0] = p01.x;
@@ -538,26 +567,33 @@ jpeg_decode_d128_kernel(DecArgs a) {
                 c[j][3] = p23.y;
             }
         }
-    }
-    OT *ob = static_cast<OT *>(a.out) + b * a.o_sb + h * a.o_sh + blk * R * a.o_ss + d0;
-    const int nrow = (int)min((int64_t)R, a.out_len - blk * R);
-#pragma unroll
-    for (int i = 0; i < R; i++) {
-        if (i >= nrow) break;
-        // sequential chains over the coefficients, channel pairs in one
-        // paired fp32 FMA (each half an ordinary fma.rn)
-        float2 o01 = make_float2(0.0f, 0.0f), o23 = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int j = 0; j < KM; j++) {
-            if (j < a.k) {
-                const float m = __ldg(a.basis + j * R + i);
-                const float2 m2 = make_float2(m, m);
-                o01 = __ffma2_rn(make_float2(c[j][0], c[j][1]), m2, o01);
-                o23 = __ffma2_rn(make_float2(c[j][2], c[j][3]), m2, o23);
+        if (e + 1 < nb) {
+            if (++lk == (unsigned)a.n) {
+                lk = 0;
+                if (++lh == (unsigned)a.H) { lh = 0; ++lb; }
             }
+            load(lb, lh, lk);
         }
-        const float o[4] = {o01.x, o01.y, o23.x, o23.y};
-        store_vec_from_f32<OT, 4>(ob + i * a.o_ss, o);
+        OT *ob = static_cast<OT *>(a.out) + b * a.o_sb + h * a.o_sh + (int64_t)blk * R * a.o_ss + d0;
+        const int nrow = (int)min((int64_t)R, a.out_len - (int64_t)blk * R);
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            if (i >= nrow) break;
+            // sequential chains over the coefficients, channel pairs in one
+            // paired fp32 FMA (each half an ordinary fma.rn)
+            float2 o01 = make_float2(0.0f, 0.0f), o23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < KM; j++) {
+                if (j < a.k) {
+                    const float m = __ldg(a.basis + j * R + i);
+                    const float2 m2 = make_float2(m, m);
+                    o01 = __ffma2_rn(make_float2(c[j][0], c[j][1]), m2, o01);
+                    o23 = __ffma2_rn(make_float2(c[j][2], c[j][3]), m2, o23);
+                }
+            }
+            const float o[4] = {o01.x, o01.y, o23.x, o23.y};
+            store_vec_from_f32<OT, 4>(ob + i * a.o_ss, o);
+        }
     }
 }
 
@@ -871,7 +907,7 @@ static int jpeg_decode_impl(const void *coef, int coef_dtype, int64_t B, int64_t
     int gshift = 0;
     while ((1 << gshift) < group) gshift++;
     DecArgs a{coef, B, H, n, D, k, c_sb, c_sh, c_sn, c_sj, scales, scale_dtype, s_sb, s_sh, s_sn,
-              s_sj, basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss, group, gshift};
+              s_sj, basis, r, out, out_dtype, out_len, o_sb, o_sh, o_ss, group, gshift, 1};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned grid = grid_stride_for(B * H * n);
     // vector stores of 4 outputs when the output rows allow them
@@ -883,7 +919,9 @@ static int jpeg_decode_impl(const void *coef, int coef_dtype, int64_t B, int64_t
         auto fast = [&](auto rr) {  // k <= 4, r in {8, 16}, vector loads and stores
             constexpr int RR = decltype(rr)::value;
             if (D == 128) {
-                const unsigned grid = grid_for(B * H * n);
+                // 8 blocks per warp once the launch fills a wave of such warps
+                a.bpw = B * H * n >= (int64_t)8 * kWarpsPerCta * num_sms() ? 8 : 1;
+                const unsigned grid = grid_for((B * H * n + a.bpw - 1) / a.bpw);
                 switch (out_dtype) {
                     case FC_F32: jpeg_decode_d128_kernel<CT, RR, 4, float><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
                     case FC_BF16: jpeg_decode_d128_kernel<CT, RR, 4, __nv_bfloat16><<<grid, kWarpsPerCta * 32, 0, st>>>(a); break;
