@@ -35,10 +35,10 @@
 
 namespace fc {
 
-void tc_plan(int64_t n, int s, int64_t units, int GT, int &n_split, int &chunk);
-bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype);
-int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows,
-                   int64_t krows_total, int64_t vrows_total, cudaStream_t st);
+void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk);
+bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled);
+int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, bool bf,
+                   cudaStream_t st);
 
 namespace {
 
@@ -927,9 +927,11 @@ extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
         for (int vm : {0, 1, 2})
             w = std::max(w, make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm).ws);
     if (n_blocks > 0 && r == 8 && s <= 8 && (8 % s) == 0 && Hq / Hk <= 8) {
-        int ns, chunk;
-        tc_plan(n_blocks, s, B * Hk, pick_gt(Hq / Hk), ns, chunk);
-        w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
+        for (int es : {1, 2}) {  // int8 codes, bf16 coefficients
+            int ns, chunk;
+            tc_plan(n_blocks, s, B * Hk, pick_gt(Hq / Hk), es, ns, chunk);
+            w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
+        }
     }
     return w;
 }
@@ -994,14 +996,15 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     }
     if (n_blocks > 0 && sel != FC_ATTN_CUDA_CORE) {
         const int64_t G = Hq / Hk, row = (int64_t)s * D;
-        const bool contig = tc_supported(D, s, r, G, rows_dtype) && k_sj == D && k_sn == row &&
+        const bool contig = tc_supported(D, s, r, G, rows_dtype, k_scales || v_scales) &&
+                            (rows_dtype != FC_I8 || (k_scales && v_scales)) && k_sj == D && k_sn == row &&
                             v_sj == D && v_sn == row && k_sh % row == 0 && v_sh % row == 0 &&
                             k_sb == Hk * k_sh && v_sb == Hk * v_sh && aligned(k_rows, 16) &&
                             aligned(v_rows, 16) && n_raw < r;
         if (contig) {
             const int GT = pick_gt(G);
             int ns, chunk;
-            tc_plan(n_blocks, s, B * Hk, GT, ns, chunk);
+            tc_plan(n_blocks, s, B * Hk, GT, dtype_size(rows_dtype), ns, chunk);
             const size_t need = workspace_for(B * Hk, ns, GT, D);
             if (!workspace || workspace_bytes < need) {
                 set_error("decode_attn: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
@@ -1033,12 +1036,13 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
             t.pl = reinterpret_cast<float *>(wsb + off);
             off = align_up(off + slots * GT * 4, 256);
             t.pacc = reinterpret_cast<float *>(wsb + off);
-            return launch_attn_tc(t, B, k_rows, v_rows, B * Hk * (k_sh / row) * s,
-                                  B * Hk * (v_sh / row) * s, static_cast<cudaStream_t>(stream));
+            return launch_attn_tc(t, B, k_rows, v_rows, rows_dtype == FC_BF16,
+                                  static_cast<cudaStream_t>(stream));
         }
         if (sel == FC_ATTN_TENSOR_CORE) {
-            set_error("decode_attn: the tensor-core kernel needs contiguous int8 (B,H,cap,s,128) "
-                      "archives with block size 8, s in {1,2,4,8} and Hq/Hk <= 8");
+            set_error("decode_attn: the tensor-core kernel needs contiguous (B,H,cap,s,128) archives "
+                      "of int8 codes with row scales or unscaled bf16 coefficients, with block size 8, "
+                      "s in {1,2,4,8} and Hq/Hk <= 8");
             return FC_ENOTSUP;
         }
     }

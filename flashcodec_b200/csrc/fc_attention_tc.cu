@@ -60,12 +60,13 @@ constexpr int kLimbs = 4;
 constexpr int kR = 8;                        // archive block length this kernel takes
 
 // ------------------------------------------------------------ tcgen05 PTX
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+// Tile (x channels, y rows of slab z) of a 3D tensor map into shared memory.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z,
                                             uint64_t *bar) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
         : "memory");
 }
 
@@ -81,11 +82,13 @@ __device__ __forceinline__ void fence_async_smem() {
 
 // Shared-memory matrix descriptor, 128-byte swizzle, Blackwell version bit.
 // K-major and MN-major tiles here both step 1024 bytes between 8-row groups
-// (SBO); the leading offset is unused at these shapes.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// (SBO).  The leading offset (LBO) matters only for an MN-major operand wider
+// than one 128-byte swizzle atom: the bf16 V tile, whose 128 channels are two
+// 64-channel boxes 16 KB apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes = 16) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)(1024 >> 4) << 32;
     d |= (uint64_t)1 << 46;
     d |= (uint64_t)2 << 61;
@@ -96,6 +99,20 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t i8_idesc(int n, int a_mn_major) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) |
            ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+// Instruction descriptor: bf16 x bf16 -> fp32, M = 128, N, A K- or MN-major.
+__host__ __device__ constexpr uint32_t bf16_idesc(int n, int a_mn_major) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) |
+           ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -138,6 +155,26 @@ __device__ __forceinline__ void epi_bar() {  // warps 0-3 only
 __device__ __forceinline__ int sw128_off(int row, int col) {
     return (row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 4) ^ (row & 7)) & 7) << 4) + (col & 15);
 }
+
+// Byte offset of (row, channel c) in a bf16 operand of `rows` rows x 128
+// channels, stored as two 128B-swizzled atoms of 64 channels, `rows` x 128
+// bytes each (channels 64-127 in the second).
+__device__ __forceinline__ int sw128_off_bf(int row, int c, int rows) {
+    return (c >> 6) * rows * 128 + sw128_off(row, (c & 63) * 2);
+}
+
+// x -> three bf16 limbs h0 + h1 + h2 (each the round-to-nearest of what the
+// previous ones left), which carry x to about 2^-24 of |x|: the tensor core's
+// bf16 products then reproduce fp32 dot products.
+__device__ __forceinline__ void bf_limbs3(float x, __nv_bfloat16 h[3]) {
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        h[i] = __float2bfloat16_rn(x);
+        x -= __bfloat162float(h[i]);
+    }
+}
+
+__device__ __forceinline__ float bits_f(int32_t v) { return __int_as_float(v); }
 
 // x (|x| <= 127 after scaling) -> limbs l[0] + l[1]/2^7 + l[2]/2^14 + l[3]/2^21
 // (q, once per CTA).
@@ -191,13 +228,29 @@ constexpr int kMaxLog = 1 << 29;  // clamp of the integer logit maxima
 // sigma = 2^(AX - m - 132), AX = max_w (biased exponent of max|w| + m_w), which
 // keeps |w / sigma| < 64.  The running reference Mref (per head) is the max of
 // the tile maxima; acc and the per-thread partial sums L live in 2^Mref units.
-template <int GT, int S>
-__global__ void __launch_bounds__(kTcThreads, GT <= 4 ? 4 : 3)
+//
+// BF: bf16 coefficient rows (unquantized archives, no row scales) through
+// kind::f16 MMAs with fp32 accumulators.  A 128-row tile is 32 KB, loaded as
+// two 64-channel TMA boxes; q and the weights are three bf16 limbs each
+// (columns 3g..3g+2), the score and output columns are fp32 sums of the limbs,
+// and the weights of a tile are taken relative to the tile max 2^m, so the
+// output of tile t folds into acc with the factor 2^(m_t - Mref).
+template <bool BF, int GT>
+__host__ __device__ constexpr int tc_stages() { return (BF && GT == 8) ? 2 : kTcStages; }
+template <bool BF, int GT>
+__host__ __device__ constexpr int tc_min_ctas() { return BF ? 2 : (GT <= 4 ? 4 : 3); }
+
+template <int GT, int S, bool BF>
+__global__ void __launch_bounds__(kTcThreads, tc_min_ctas<BF, GT>())
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                const TcArgs a) {
-    constexpr int N = GT <= 4 ? 16 : 32;  // B columns: 4 limbs x GT heads, padded
-    constexpr int PP = kR / S;            // positions of a block per lane
-    constexpr int XF = 2 * GT + 1;        // exchange fields per tile (x 4 warps)
+    constexpr int NL = BF ? 3 : kLimbs;           // limbs per head
+    constexpr int N = NL * GT <= 16 ? 16 : 32;    // B columns: NL limbs x GT heads, padded
+    constexpr int PP = kR / S;                    // positions of a block per lane
+    constexpr int XF = 2 * GT + 1;                // exchange fields per tile (x 4 warps)
+    constexpr int TB = BF ? 2 * kTileBytes : kTileBytes;  // bytes per ring stage
+    constexpr int NST = tc_stages<BF, GT>();      // ring stages
+    constexpr int BQ = N * 128 * (BF ? 2 : 1);    // bytes of one B tile (q or weight limbs)
     // Programmatic dependent launch: the next launch in the stream (when it
     // is launched as a dependent) may be scheduled once every CTA of this one
     // has started; it reads nothing before its griddepcontrol.wait.
@@ -206,18 +259,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *ring = smem;
-    unsigned char *bq = smem + a.off_bq;                       // N x 128 q limbs (K-major B)
-    unsigned char *bw = smem + a.off_bw;                       // 2 x N x 128 weight limbs
+    unsigned char *bq = smem + a.off_bq;                       // BQ bytes of q limbs (K-major B)
+    unsigned char *bw = smem + a.off_bw;                       // 2 x BQ weight limbs
     int *xch = reinterpret_cast<int *>(smem + a.off_xch);      // [2][XF][4 warps] exchange, [4] flags
     float *red = reinterpret_cast<float *>(smem + a.off_red);  // small reductions
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
-    uint64_t *full = bars;                    // [kTcStages] TMA landed
-    uint64_t *sdone = bars + kTcStages;       // [2] score MMA done
-    uint64_t *sfree = bars + kTcStages + 2;   // [2] scores read back (4 warps)
-    uint64_t *wready = bars + kTcStages + 4;  // [2] weight limbs written (4 warps)
-    uint64_t *vdone = bars + kTcStages + 6;   // [2] output MMA done
-    uint64_t *vfree = bars + kTcStages + 8;   // [2] output read back (4 warps)
-    uint64_t *xbar = bars + kTcStages + 10;   // [2] tile exchange published (4 warps)
+    uint64_t *full = bars;              // [NST] TMA landed
+    uint64_t *sdone = bars + NST;       // [2] score MMA done
+    uint64_t *sfree = bars + NST + 2;   // [2] scores read back (4 warps)
+    uint64_t *wready = bars + NST + 4;  // [2] weight limbs written (4 warps)
+    uint64_t *vdone = bars + NST + 6;   // [2] output MMA done
+    uint64_t *vfree = bars + NST + 8;   // [2] output read back (4 warps)
+    uint64_t *xbar = bars + NST + 10;   // [2] tile exchange published (4 warps)
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
 
@@ -241,28 +294,32 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     float *s_fin = reinterpret_cast<float *>(ring + 512);     // [16] final M, L per head
     float *scr = reinterpret_cast<float *>(ring + 1024);      // merge scratch
     int *s_badf = xch + 2 * XF * 4;  // [4] abort flags after the last tile
-    const int64_t k_row0 = ((b * a.Hk + hk) * a.k_cap + n0) * S;  // first code row (tensor map y)
-    const int64_t v_row0 = ((b * a.Hk + hk) * a.v_cap + n0) * S;
-    const uint32_t idesc_s = i8_idesc(N, 0), idesc_o = i8_idesc(N, 1);
+    // tensor maps: x channel, y row within the (batch, KV head) slab, z slab;
+    // rows at or past the archive's n blocks read as zeros
+    const int y0 = (int)(n0 * S);
+    const int slab = (int)(b * a.Hk + hk);
+    const uint32_t idesc_s = BF ? bf16_idesc(N, 0) : i8_idesc(N, 0);
+    const uint32_t idesc_o = BF ? bf16_idesc(N, 1) : i8_idesc(N, 1);
     constexpr int kAlloc = N * 4 <= 64 ? 64 : 128;  // TMEM columns: 2 score + 2 output buffers
 
     // ---------------------------------------------------------------- setup
     int issued = 0, consumed = 0;  // producer bookkeeping (lane 0 of warp 4)
     auto issue = [&](int u) {      // ring tile u in consumption order K0, K1, V0, K2, V1, ...
-        const int st = u % kTcStages;
+        const int st = u % NST;
         bool isk;
         int t;
         if (u == 0) { isk = true; t = 0; }
         else if (u <= 2 * T - 3) { isk = (u & 1) != 0; t = isk ? (u + 1) >> 1 : (u >> 1) - 1; }
         else { isk = false; t = u - T; }
-        const int y = (int)((isk ? k_row0 : v_row0) + (int64_t)t * kTileRows);
-        mbar_expect_tx(full + st, kTileBytes);
-        tma_load_2d(ring + st * kTileBytes, isk ? &tmk : &tmv, 0, y, full + st);
+        const int y = y0 + t * kTileRows;
+        mbar_expect_tx(full + st, TB);
+        tma_load_3d(ring + st * TB, isk ? &tmk : &tmv, 0, y, slab, full + st);
+        if (BF) tma_load_3d(ring + st * TB + kTileBytes, isk ? &tmk : &tmv, 64, y, slab, full + st);
     };
     float qv[GT];  // q of the group's heads at d = tid (epilogue threads)
     if (producer) {
         if (lane == 0) {
-            for (int i = 0; i < kTcStages; i++) mbar_init(full + i, 1);
+            for (int i = 0; i < NST; i++) mbar_init(full + i, 1);
             for (int i = 0; i < 2; i++) {
                 mbar_init(sdone + i, 1);
                 mbar_init(sfree + i, 4);
@@ -283,38 +340,62 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         // inputs, archive and workspace may be written by the previous grid
         asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane == 0)
-            for (; issued < min(kTcStages, 2 * T); issued++) issue(issued);
+            for (; issued < min(NST, 2 * T); issued++) issue(issued);
     } else {
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        // q of the group's heads: per-head scale, int8 limbs (K-major B tile)
         const int d = tid;  // head_dim == 128 == epilogue threads
+        if constexpr (BF) {
+            // q of the group's heads as three bf16 limbs (K-major B tile), no scale
+            __nv_bfloat16 *bq16 = reinterpret_cast<__nv_bfloat16 *>(bq);
+            const __nv_bfloat16 zero = __float2bfloat16_rn(0.0f);
 #pragma unroll
-        for (int g = 0; g < GT; g++) {
-            float v = 0.0f;
-            if (g < G) v = load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype);
-            qv[g] = v;
-            float m = fabsf(v);
-            for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            if (lane == 0) red[warp * 8 + g] = m;
-        }
-        epi_bar();
-        if (tid < GT) {
-            const float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
-            s_sq[tid] = m > 0.0f ? m / 127.0f : 1.0f;
-        }
-        epi_bar();
+            for (int g = 0; g < GT; g++) {
+                float v = 0.0f;
+                if (g < G) v = load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype);
+                __nv_bfloat16 h[3];
+                bf_limbs3(v, h);
 #pragma unroll
-        for (int g = 0; g < GT; g++) {  // one limb split per head
-            int lq[kLimbs] = {0, 0, 0, 0};
-            if (g < G) limbs4(qv[g] / s_sq[g], lq);
+                for (int l = 0; l < 3; l++) bq16[sw128_off_bf(3 * g + l, d, N) / 2] = h[l];
+            }
+            if (tid < GT) s_sq[tid] = 1.0f;
+            __nv_bfloat16 *bw16 = reinterpret_cast<__nv_bfloat16 *>(bw);
 #pragma unroll
-            for (int l = 0; l < kLimbs; l++) bq[sw128_off(kLimbs * g + l, d)] = (unsigned char)(int8_t)lq[l];
-        }
+            for (int row = 0; row < N; row++) {
+                if (row >= 3 * GT) bq16[sw128_off_bf(row, d, N) / 2] = zero;
+                bw16[sw128_off_bf(row, d, N) / 2] = zero;
+                bw16[(BQ + sw128_off_bf(row, d, N)) / 2] = zero;
+            }
+            epi_bar();
+        } else {
+            // q of the group's heads: per-head scale, int8 limbs (K-major B tile)
 #pragma unroll
-        for (int row = 0; row < N; row++) {
-            if (row >= kLimbs * GT) bq[sw128_off(row, d)] = 0;
-            bw[sw128_off(row, d)] = 0;
-            bw[N * 128 + sw128_off(row, d)] = 0;
+            for (int g = 0; g < GT; g++) {
+                float v = 0.0f;
+                if (g < G) v = load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype);
+                qv[g] = v;
+                float m = fabsf(v);
+                for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+                if (lane == 0) red[warp * 8 + g] = m;
+            }
+            epi_bar();
+            if (tid < GT) {
+                const float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
+                s_sq[tid] = m > 0.0f ? m / 127.0f : 1.0f;
+            }
+            epi_bar();
+#pragma unroll
+            for (int g = 0; g < GT; g++) {  // one limb split per head
+                int lq[kLimbs] = {0, 0, 0, 0};
+                if (g < G) limbs4(qv[g] / s_sq[g], lq);
+#pragma unroll
+                for (int l = 0; l < kLimbs; l++) bq[sw128_off(kLimbs * g + l, d)] = (unsigned char)(int8_t)lq[l];
+            }
+#pragma unroll
+            for (int row = 0; row < N; row++) {
+                if (row >= kLimbs * GT) bq[sw128_off(row, d)] = 0;
+                bw[sw128_off(row, d)] = 0;
+                bw[N * 128 + sw128_off(row, d)] = 0;
+            }
         }
         fence_async_smem();
     }
@@ -332,18 +413,29 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         // soon as the MMA that read it has completed.
         if (lane == 0 && T > 0) {
             auto consume_tile = [&](int u, bool isk, int t) -> bool {
-                const int st = u % kTcStages;
-                if (!mbar_wait_bounded(full + st, (u / kTcStages) & 1, a.status, a.epoch)) return false;
-                const uint32_t at = smem_addr(ring + st * kTileBytes);
+                const int st = u % NST;
+                if (!mbar_wait_bounded(full + st, (u / NST) & 1, a.status, a.epoch)) return false;
+                const uint32_t at = smem_addr(ring + st * TB);
                 if (isk) {
                     if (t >= 2 && !mbar_wait_bounded(sfree + (t & 1), ((t - 2) >> 1) & 1, a.status, a.epoch))
                         return false;
                     tc_fence_after();
                     const uint32_t bt = smem_addr(bq);
+                    if constexpr (BF) {
+                        // K = 128 channels in 8 steps of 16: step k reads 32 bytes of
+                        // each row, in atom k / 4 at byte (k % 4) * 32
 #pragma unroll
-                    for (int k = 0; k < 4; k++)
-                        mma_i8(tmem + (t & 1) * N, sw128_desc(at + k * 32), sw128_desc(bt + k * 32),
-                               idesc_s, k > 0);
+                        for (int k = 0; k < 8; k++)
+                            mma_bf16(tmem + (t & 1) * N,
+                                     sw128_desc(at + (k >> 2) * kTileBytes + (k & 3) * 32),
+                                     sw128_desc(bt + (k >> 2) * (N * 128) + (k & 3) * 32), idesc_s,
+                                     k > 0);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            mma_i8(tmem + (t & 1) * N, sw128_desc(at + k * 32), sw128_desc(bt + k * 32),
+                                   idesc_s, k > 0);
+                    }
                     mma_commit(sdone + (t & 1));
                     if (!mbar_wait_bounded(sdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
                 } else {
@@ -351,11 +443,21 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     if (t >= 2 && !mbar_wait_bounded(vfree + (t & 1), ((t - 2) >> 1) & 1, a.status, a.epoch))
                         return false;
                     tc_fence_after();
-                    const uint32_t bt = smem_addr(bw + (t & 1) * (N * 128));
+                    const uint32_t bt = smem_addr(bw + (t & 1) * BQ);
+                    if constexpr (BF) {
+                        // K = 128 rows in 8 steps of 16 (2 KB of the tile each); the
+                        // tile's channels 64-127 lie one box (LBO) further on
 #pragma unroll
-                    for (int k = 0; k < 4; k++)
-                        mma_i8(tmem + (2 + (t & 1)) * N, sw128_desc(at + k * 4096),
-                               sw128_desc(bt + k * 32), idesc_o, k > 0);
+                        for (int k = 0; k < 8; k++)
+                            mma_bf16(tmem + (2 + (t & 1)) * N, sw128_desc(at + k * 2048, kTileBytes),
+                                     sw128_desc(bt + (k >> 2) * (N * 128) + (k & 3) * 32), idesc_o,
+                                     k > 0);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            mma_i8(tmem + (2 + (t & 1)) * N, sw128_desc(at + k * 4096),
+                                   sw128_desc(bt + k * 32), idesc_o, k > 0);
+                    }
                     mma_commit(vdone + (t & 1));
                     if (!mbar_wait_bounded(vdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
                 }
@@ -416,28 +518,35 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             __syncwarp();
             if (lane == 0) mbar_arrive(vfree + (u & 1));
 #pragma unroll
-            for (int g = 0; g < GT; g++)
-                acc[g] = fmaf(limb_value(o, g), pow2_biased(AXp[g] - 5 - Mref[g]), acc[g]);
+            for (int g = 0; g < GT; g++) {
+                if constexpr (BF)  // tile output in 2^m_u units (AXp = m_u)
+                    acc[g] = fmaf(bits_f(o[3 * g]) + (bits_f(o[3 * g + 1]) + bits_f(o[3 * g + 2])),
+                                  pow2_biased(127 + AXp[g] - Mref[g]), acc[g]);
+                else
+                    acc[g] = fmaf(limb_value(o, g), pow2_biased(AXp[g] - 5 - Mref[g]), acc[g]);
+            }
             return true;
         };
         int pend_bad = 0;
         float ks_next = 0.0f, vs_next = 0.0f;
-        if (T > 0 && lrow < R) {
+        if (!BF && T > 0 && lrow < R) {
             ks_next = scale_at(a.ksc, kb0, kidx);
             vs_next = scale_at(a.vsc, vb0, vidx);
         }
         for (int t = 0; t < T; t++) {
             const int par = t & 1;
             const int row = t * kTileRows + lrow;
-            const float ks = ks_next, vsr = vs_next;
-            kidx += kstep;
-            vidx += vstep;
-            if (row + kTileRows < R) {  // the next tile's row scales
-                ks_next = scale_at(a.ksc, kb0, kidx);
-                vs_next = scale_at(a.vsc, vb0, vidx);
-            } else {
-                ks_next = 0.0f;
-                vs_next = 0.0f;
+            const float ks = BF ? 1.0f : ks_next, vsr = BF ? 1.0f : vs_next;
+            if constexpr (!BF) {
+                kidx += kstep;
+                vidx += vstep;
+                if (row + kTileRows < R) {  // the next tile's row scales
+                    ks_next = scale_at(a.ksc, kb0, kidx);
+                    vs_next = scale_at(a.vsc, vb0, vidx);
+                } else {
+                    ks_next = 0.0f;
+                    vs_next = 0.0f;
+                }
             }
             int mw[GT], wx[GT];
             float w[GT], lsum[GT];
@@ -455,7 +564,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 const float nb = row >= R ? -INFINITY : 0.0f;  // rows past the split
 #pragma unroll
                 for (int g = 0; g < GT; g++) {
-                    const float sg = limb_value(v, g) * (cq[g] * ks);
+                    const float sg =
+                        BF ? (bits_f(v[3 * g]) + (bits_f(v[3 * g + 1]) + bits_f(v[3 * g + 2]))) * cq[g]
+                           : limb_value(v, g) * (cq[g] * ks);
                     float lg[PP];
 #pragma unroll
                     for (int k = 0; k < PP; k++) lg[k] = fmaf(Ar[k][0], sg, nb);
@@ -489,10 +600,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 #pragma unroll
                         for (int x = 0; x < h; x++) c[x] += __shfl_xor_sync(0xffffffffu, c[x + h], h);
                     w[g] = c[0] * vsr;
-                    const unsigned wb =
-                        __reduce_max_sync(0xffffffffu, __float_as_uint(w[g]) & 0x7fffffffu);
                     mw[g] = mi;
-                    wx[g] = (int)(wb >> 23) + mi;
+                    if constexpr (BF) {
+                        wx[g] = 0;  // bf16 limbs need no common exponent
+                    } else {
+                        const unsigned wb =
+                            __reduce_max_sync(0xffffffffu, __float_as_uint(w[g]) & 0x7fffffffu);
+                        wx[g] = (int)(wb >> 23) + mi;
+                    }
                     lsum[g] = ls;
                 }
             }
@@ -528,7 +643,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 AX[g] = __shfl_sync(0xffffffffu, fmx, GT + g);
             }
             // weight limbs of this row (column lrow of the B tile)
-            unsigned char *bwt = bw + par * (N * 128);
+            unsigned char *bwt = bw + par * BQ;
+            if constexpr (BF) {
+                // w relative to the tile max 2^m (an exact power-of-two factor)
+                __nv_bfloat16 *bw16 = reinterpret_cast<__nv_bfloat16 *>(bwt);
+#pragma unroll
+                for (int g = 0; g < GT; g++) {
+                    __nv_bfloat16 h[3];
+                    bf_limbs3(w[g] * pow2_biased(127 + mw[g] - m[g]), h);
+#pragma unroll
+                    for (int l = 0; l < 3; l++) bw16[sw128_off_bf(3 * g + l, lrow, N) / 2] = h[l];
+                }
+            } else {
 #pragma unroll
             for (int g = 0; g < GT; g++) {
                 // x = w * 2^(132 + m_w - AX), |x| < 64.  The factor's exponent is
@@ -547,6 +673,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 bwt[sw128_off(4 * g + 2, lrow)] = (unsigned char)__float_as_uint(y2);
                 bwt[sw128_off(4 * g + 3, lrow)] = (unsigned char)__float_as_uint(y3);
             }
+            }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(wready + par);
@@ -560,7 +687,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     Mref[g] = m[g];
                 }
                 Ls[g] = fmaf(lsum[g], pow2_biased(127 + mw[g] - Mref[g]), Ls[g]);
-                AXp[g] = AX[g];
+                AXp[g] = BF ? m[g] : AX[g];
             }
         }
         float M[GT], L[GT];
@@ -657,7 +784,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             // bounded drain of the tile copies still in flight
             for (int u = consumed; u < issued; u++) {
                 const uint64_t t0 = global_ns();
-                while (!mbar_try_wait(full + (u % kTcStages), (u / kTcStages) & 1) &&
+                while (!mbar_try_wait(full + (u % NST), (u / NST) & 1) &&
                        global_ns() - t0 < kWaitNs) {
                 }
             }
@@ -692,16 +819,24 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
-// 2D view of a contiguous (B, Hk, cap, s, 128) int8 archive: rows of 128 bytes,
-// boxes of 128 x 128 with the 128-byte swizzle the MMA descriptors expect.
-bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows) {
+// 3D view of a contiguous (B, Hk, cap, s, 128) archive: 128 channels x the
+// n * s rows written so far x B * Hk slabs, cap * s rows apart.  Rows of the
+// capacity past the archive's end are outside the map and load as zeros, so a
+// tile that runs past the end never reads unwritten memory (for bf16 rows that
+// could hold Inf or NaN patterns, which no mask removes from a product).
+// Boxes are 128 int8 codes x 128 rows, or 64 bf16 channels x 128 rows (two
+// per tile), with the 128-byte swizzle the MMA descriptors expect.
+bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows, int64_t slabs,
+                     int64_t slab_rows, bool bf) {
     auto fn = get_encode();
     if (!fn) return false;
-    cuuint64_t dims[2] = {128, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {128};
-    cuuint32_t box[2] = {128, (cuuint32_t)kTileRows};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+    const int64_t rb = bf ? 256 : 128;
+    cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)slabs};
+    cuuint64_t strides[2] = {(cuuint64_t)rb, (cuuint64_t)(slab_rows * rb)};
+    cuuint32_t box[3] = {(cuuint32_t)(bf ? 64 : 128), (cuuint32_t)kTileRows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+              const_cast<void *>(base), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -719,9 +854,9 @@ bool pdl_enabled() {
     return on;
 }
 
-// Dynamic shared memory already opted in, per kernel variant (GT x s) and device.
+// Dynamic shared memory already opted in, per kernel variant (rows x GT x s) and device.
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_smem_opted[16][kMaxDevices];
+std::atomic<int> g_smem_opted[32][kMaxDevices];
 
 // Tiles per split forced by FLASHCODEC_TC_CHUNK_TILES (tuning), 0 when unset.
 int chunk_tiles_override() {
@@ -736,8 +871,9 @@ int chunk_tiles_override() {
 }  // namespace
 
 // Resident CTAs per SM of the tensor-core kernel (its launch bounds and
-// shared-memory footprint): 4 for GT <= 4, 3 for GT = 8.
-int tc_ctas_per_sm(int GT) { return GT <= 4 ? 4 : 3; }
+// shared-memory footprint): int8 rows 4 for GT <= 4, 3 for GT = 8; bf16 rows
+// (32 KB tiles) 2.
+int tc_ctas_per_sm(int GT, int es) { return es == 2 ? 2 : (GT <= 4 ? 4 : 3); }
 
 // Split plan of the tensor-core kernel.  Every CTA pays a pipeline fill and
 // drain, and CTAs of a second wave run behind an idle tail, so the plan takes
@@ -747,11 +883,14 @@ int tc_ctas_per_sm(int GT) { return GT <= 4 ? 4 : 3; }
 // 48 KB tile ring after its first KB).
 static_assert(merge_scratch_floats(1024, 8, kTcThreads) * 4 + 1024 <= kTcStages * kTileBytes,
               "merge scratch must fit the tile ring");
-void tc_plan(int64_t n, int s, int64_t units, int GT, int &n_split, int &chunk) {
+static_assert(merge_scratch_floats(1024, 8, kTcThreads) * 4 + 1024 <=
+                  tc_stages<true, 8>() * 2 * kTileBytes,
+              "merge scratch must fit the bf16 tile ring");
+void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk) {
     const int64_t tiles = std::max<int64_t>(1, (n * s + kTileRows - 1) / kTileRows);
     int64_t ct = chunk_tiles_override();
     if (ct == 0) {
-        const int64_t slots = (int64_t)num_sms() * tc_ctas_per_sm(GT);
+        const int64_t slots = (int64_t)num_sms() * tc_ctas_per_sm(GT, es);
         const int64_t want = std::max<int64_t>(1, slots / std::max<int64_t>(units, 1));
         ct = (tiles + want - 1) / want;
         // at least 4 tiles per split: in launches smaller than a wave of such
@@ -765,31 +904,42 @@ void tc_plan(int64_t n, int s, int64_t units, int GT, int &n_split, int &chunk) 
     chunk = (int)std::min<int64_t>(blocks, n);
 }
 
-bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype) {
-    return D == 128 && rows_dtype == FC_I8 && r == kR && (s == 1 || s == 2 || s == 4 || s == 8) &&
+// int8 codes with one scale per row, or bf16 coefficients without scales
+bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled) {
+    const bool rows_ok = (rows_dtype == FC_I8 && scaled) || (rows_dtype == FC_BF16 && !scaled);
+    return D == 128 && rows_ok && r == kR && (s == 1 || s == 2 || s == 4 || s == 8) &&
            G >= 1 && G <= 8 && get_encode() != nullptr;
 }
 
-int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, int64_t krows_total,
-                   int64_t vrows_total, cudaStream_t st) {
+int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, bool bf,
+                   cudaStream_t st) {
     CUtensorMap mk, mv;
-    if (!encode_rows_map(&mk, krows, krows_total) || !encode_rows_map(&mv, vrows, vrows_total)) {
+    const int64_t rows = a.n * a.s, slabs = B * a.Hk;
+    if (rows >= (int64_t)1 << 31 || slabs >= (int64_t)1 << 31) {
+        set_error("decode_attn: archive of %lld rows x %lld slabs is beyond the tensor-core "
+                  "kernel's 32-bit tile coordinates", (long long)rows, (long long)slabs);
+        return FC_ENOTSUP;
+    }
+    if (!encode_rows_map(&mk, krows, rows, slabs, a.k_cap * a.s, bf) ||
+        !encode_rows_map(&mv, vrows, rows, slabs, a.v_cap * a.s, bf)) {
         set_error("decode_attn: tensor map encoding failed");
         return FC_ECUDA;
     }
-    const int N = a.GT <= 4 ? 16 : 32;
-    size_t off = (size_t)kTcStages * kTileBytes;
+    const int N = a.GT <= 4 ? 16 : 32;  // 4 int8 or 3 bf16 limbs x GT heads, padded
+    const int stages = bf ? (a.GT == 8 ? tc_stages<true, 8>() : tc_stages<true, 4>()) : kTcStages;
+    const size_t bq_bytes = (size_t)N * 128 * (bf ? 2 : 1);
+    size_t off = (size_t)stages * kTileBytes * (bf ? 2 : 1);
     a.off_bq = (int)off;
-    off = align_to(off + (size_t)N * 128, 1024);
+    off = align_to(off + bq_bytes, 1024);
     a.off_bw = (int)off;
-    off += (size_t)2 * N * 128;
+    off += 2 * bq_bytes;
     a.off_xch = (int)off;
     off = align_to(off + (size_t)(2 * 4 * (2 * a.GT + 1) + 4) * 4, 16);
     a.off_red = (int)off;
     off = align_to(off + (size_t)40 * 4, 16);
     a.off_scr = 0;  // merge scratch lives in the ring after the last tile
     a.off_bar = (int)align_to(off, 8);
-    off = a.off_bar + (kTcStages + 12) * 8;
+    off = a.off_bar + (stages + 12) * 8;
     const size_t smem = off + 1024;  // room to align the dynamic base to 1024
     dim3 grid((unsigned)(B * a.Hk * a.n_split));
     int dev = 0;
@@ -817,11 +967,20 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
     };
     auto by_s = [&](auto gt, int gi) {
         constexpr int GT = decltype(gt)::value;
+        if (bf) {
+            switch (a.s) {
+                case 1: go(attn_tc_kernel<GT, 1, true>, 16 + gi * 4 + 0); break;
+                case 2: go(attn_tc_kernel<GT, 2, true>, 16 + gi * 4 + 1); break;
+                case 4: go(attn_tc_kernel<GT, 4, true>, 16 + gi * 4 + 2); break;
+                default: go(attn_tc_kernel<GT, 8, true>, 16 + gi * 4 + 3); break;
+            }
+            return;
+        }
         switch (a.s) {
-            case 1: go(attn_tc_kernel<GT, 1>, gi * 4 + 0); break;
-            case 2: go(attn_tc_kernel<GT, 2>, gi * 4 + 1); break;
-            case 4: go(attn_tc_kernel<GT, 4>, gi * 4 + 2); break;
-            default: go(attn_tc_kernel<GT, 8>, gi * 4 + 3); break;
+            case 1: go(attn_tc_kernel<GT, 1, false>, gi * 4 + 0); break;
+            case 2: go(attn_tc_kernel<GT, 2, false>, gi * 4 + 1); break;
+            case 4: go(attn_tc_kernel<GT, 4, false>, gi * 4 + 2); break;
+            default: go(attn_tc_kernel<GT, 8, false>, gi * 4 + 3); break;
         }
     };
     switch (a.GT) {

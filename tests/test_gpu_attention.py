@@ -219,6 +219,72 @@ def test_tensor_core_and_cuda_core_kernels_vs_oracle(kernel_choice, G, K, dt, S,
     assert Kn.attn_status(q.to(DEV).device) == 0
 
 
+@pytest.mark.parametrize("G,K,S,tail,B,Hk", [
+    (4, 4, 8 * 2000, 5, 2, 4),      # config-2 layer shape (jpeg-fp line)
+    (8, 2, 8 * 300, 3, 2, 4),       # N = 32 columns, 2 ring stages
+    (1, 1, 8 * 70, 0, 2, 4),        # s = 1
+    (3, 8, 8 * 90, 7, 2, 4),        # s = 8, G not a power of 2
+    (2, 4, 8 * 20, 4, 2, 4),        # one split, partial tile
+    (4, 4, 8 * 9000, 1, 1, 1),      # one unit, many splits merged
+])
+def test_tensor_core_bf16_coefficients_vs_oracle(kernel_choice, G, K, S, tail, B, Hk):
+    """Unquantized jpeg archives (bf16 coefficients, no scales): the
+    tensor-core kernel's bf16 path and the CUDA-core kernel against the
+    oracle, within the bf16 output tolerance."""
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as Kn
+    k, v, q = bench.synth_case(B, Hk * G, Hk, S + tail, 128, 0.95, 29, dtype=torch.bfloat16)
+    ks, vs = build("jpeg", dict(keep_freqs=K, quant_bits=0), k.to(DEV), v.to(DEV))
+    assert ks._coeffs.dtype == torch.bfloat16
+    ref = oracle_attention(q, ks, vs)
+    outs = {}
+    for which in ("tensor-core", "cuda-core"):
+        kernel_choice(which)
+        outs[which] = fc.codec_decode_attention(q.to(DEV), ks, vs)
+        check_close(outs[which], ref, torch.bfloat16)
+    kernel_choice("auto")
+    auto = fc.codec_decode_attention(q.to(DEV), ks, vs)
+    assert torch.equal(auto, outs["tensor-core"])
+    assert Kn.attn_status(q.to(DEV).device) == 0
+
+
+@pytest.mark.parametrize("quant", [0, 8])
+def test_unwritten_capacity_is_never_read(kernel_choice, quant):
+    """The archive's capacity past its last block holds whatever the
+    allocator left there; for bf16 rows that can be NaN or Inf, which no mask
+    removes from a product.  With that region filled with NaN (K) and Inf (V),
+    both kernels still match the oracle: the last tile of a split never reads
+    past the archive's end."""
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(2, 8, 2, 8 * 300 + 3, 128, 0.95, 11, dtype=torch.bfloat16)
+    ks, vs = build("jpeg", dict(keep_freqs=4, quant_bits=quant), k.to(DEV), v.to(DEV))
+    n = ks.n_blocks
+    assert ks._coeffs.shape[2] > n
+    if quant:
+        ks._coeffs[:, :, n:] = 127
+        vs._coeffs[:, :, n:] = -127
+        ks._scales[:, :, n:] = float("nan")
+        vs._scales[:, :, n:] = float("inf")
+    else:
+        ks._coeffs[:, :, n:] = float("nan")
+        vs._coeffs[:, :, n:] = float("inf")
+    ref = oracle_attention(q, ks, vs)
+    for which in ("tensor-core", "cuda-core"):
+        kernel_choice(which)
+        check_close(fc.codec_decode_attention(q.to(DEV), ks, vs), ref, torch.bfloat16)
+
+
+def test_tensor_core_refuses_fp16_coefficients(kernel_choice):
+    """fp16 coefficient rows stay on the CUDA-core kernel: forcing the
+    tensor-core kernel on them fails loudly."""
+    import flashcodec_b200 as fc
+    k, v, q = bench.synth_case(1, 8, 2, 8 * 40, 128, 0.95, 3, dtype=torch.float16)
+    ks, vs = build("jpeg", dict(keep_freqs=4, quant_bits=0), k.to(DEV), v.to(DEV))
+    kernel_choice("tensor-core")
+    with pytest.raises(NotImplementedError):
+        fc.codec_decode_attention(q.to(DEV), ks, vs)
+
+
 def test_tensor_core_refuses_unsupported_layout(kernel_choice):
     """Forcing the tensor-core kernel on a layout it does not take fails
     loudly instead of silently using another kernel."""
