@@ -24,10 +24,18 @@ SYMBOLS = ("fc_version", "fc_last_error_string", "fc_jpeg_encode", "fc_jpeg_deco
            "fc_decode_attn_noalloc",
            "fc_decode_attn_noalloc_status", "fc_append_tokens", "fc_gather_batch", "fc_rope_kv_append", "fc_decode_attn_masked",
            "fc_set_attn_kernel",
-           "fc_selftest_bounded_wait", "fc_selftest_noalloc_wait")
+           "fc_selftest_bounded_wait", "fc_selftest_noalloc_wait", "fc_decode_attn_peers",
+           "fc_peers_wait", "fc_ipc_get_handle", "fc_ipc_open_handle", "fc_ipc_close_handle")
+FC_MAX_PEERS, FC_IPC_HANDLE_BYTES = 8, 64
 FC_ATTN_AUTO, FC_ATTN_CUDA_CORE, FC_ATTN_TENSOR_CORE = 0, 1, 2
 
 _I64, _I32, _P, _F32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float
+
+
+class PeerOut(ctypes.Structure):
+    """fc_peer_out: every rank's output buffer and flag array of a split-head step."""
+    _fields_ = [("out", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
+                ("world", ctypes.c_int), ("rank", ctypes.c_int), ("epoch", ctypes.c_int)]
 
 
 class AppendStream(ctypes.Structure):
@@ -125,6 +133,23 @@ _SIGS = {
     "fc_set_attn_kernel": ([_I32], _I32),
     "fc_selftest_bounded_wait": ([_P, _I32, _P], _I32),
     "fc_selftest_noalloc_wait": ([_I32, _P], _I32),
+    "fc_decode_attn_peers": ([_P, _I32, _I64, _I64, _I64, _I64, _I64,
+                              _I64, _I64, _I32, _I32, _I32,
+                              _P, _I64, _I64, _I64, _I64,
+                              _P, _I64, _I64, _I64, _I64,
+                              _P, _I64, _I64, _I64,
+                              _P, _I64, _I64, _I64,
+                              _I32,
+                              _P, _I64, _I64, _I64,
+                              _P, _I64, _I64, _I64,
+                              _I32, _I64,
+                              _P, _F32,
+                              _I32, _I64, _I64, _P,
+                              _P, ctypes.c_size_t, _P], _I32),
+    "fc_peers_wait": ([_P, _I32, _I32, _P, _P], _I32),
+    "fc_ipc_get_handle": ([_P, _P, _P], _I32),
+    "fc_ipc_open_handle": ([_P, _P], _I32),
+    "fc_ipc_close_handle": ([_P], _I32),
 }
 
 _lock = threading.Lock()

@@ -959,7 +959,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
                               void *stream,
                             const PngAnchors *png, const unsigned char *vis = nullptr,
                             int64_t vis_sb = 0, int sgrp = 0, int64_t ks_sj = 1,
-                            int64_t vs_sj = 1) {
+                            int64_t vs_sj = 1, const fc_peer_out *peers = nullptr) {
     clear_error();
     if (B < 0 || Hq <= 0 || Hk <= 0 || D <= 0) { set_error("decode_attn: bad shape"); return FC_EINVAL; }
     if (Hq % Hk != 0) { set_error("decode_attn: Hq (%lld) must be a multiple of Hk (%lld)", (long long)Hq, (long long)Hk); return FC_EINVAL; }
@@ -990,6 +990,11 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     // png rows come from two tensors (the CUDA-core kernel's direct-load path);
     // a visibility mask is applied by the CUDA-core kernel
     const int sel = (png || vis || sgrp) ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
+    if (peers && (sel == FC_ATTN_CUDA_CORE || n_blocks == 0)) {
+        set_error("decode_attn_peers: peer outputs need the tensor-core kernel (an archive of "
+                  "at least one block in one of its layouts)");
+        return FC_ENOTSUP;
+    }
     if (sgrp && g_attn_kernel.load() == FC_ATTN_TENSOR_CORE) {
         set_error("decode_attn: the tensor-core kernel takes one scale per row only");
         return FC_ENOTSUP;
@@ -1036,10 +1041,20 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
             t.pl = reinterpret_cast<float *>(wsb + off);
             off = align_up(off + slots * GT * 4, 256);
             t.pacc = reinterpret_cast<float *>(wsb + off);
+            if (peers) {
+                for (int p = 0; p < peers->world; p++) {
+                    if (p != peers->rank) t.pout[t.npout++] = peers->out[p];
+                    t.pflag[p] = peers->flags[p];
+                }
+                t.pworld = peers->world;
+                t.prank = peers->rank;
+                t.pepoch = peers->epoch;
+                t.done = reinterpret_cast<int *>(wsb + kWsDoneOffset);
+            }
             return launch_attn_tc(t, B, k_rows, v_rows, rows_dtype == FC_BF16,
                                   static_cast<cudaStream_t>(stream));
         }
-        if (sel == FC_ATTN_TENSOR_CORE) {
+        if (sel == FC_ATTN_TENSOR_CORE || peers) {
             set_error("decode_attn: the tensor-core kernel needs contiguous (B,H,cap,s,128) archives "
                       "of int8 codes with row scales or unscaled bf16 coefficients, with block size 8, "
                       "s in {1,2,4,8} and Hq/Hk <= 8");
@@ -1136,6 +1151,38 @@ extern "C" int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq,
                               int64_t o_sh, void *workspace, size_t workspace_bytes,
                               void *stream) {
     return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype, k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj, k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn, scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st, raw_dtype, n_raw, A, softmax_scale, out, out_dtype, o_sb, o_sh, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int fc_decode_attn_peers(
+    const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D, int64_t q_sb, int64_t q_sh,
+    int64_t Hk, int64_t n_blocks, int s, int r, int rows_dtype, const void *k_rows, int64_t k_sb,
+    int64_t k_sh, int64_t k_sn, int64_t k_sj, const void *v_rows, int64_t v_sb, int64_t v_sh,
+    int64_t v_sn, int64_t v_sj, const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+    const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn, int scale_dtype,
+    const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st, const void *v_raw,
+    int64_t vr_sb, int64_t vr_sh, int64_t vr_st, int raw_dtype, int64_t n_raw, const float *A,
+    float softmax_scale, int out_dtype, int64_t o_sb, int64_t o_sh, const fc_peer_out *peers,
+    void *workspace, size_t workspace_bytes, void *stream) {
+    clear_error();
+    if (!peers || peers->world < 1 || peers->world > FC_MAX_PEERS || peers->rank < 0 ||
+        peers->rank >= peers->world || peers->epoch <= 0) {
+        set_error("decode_attn_peers: need 1 <= world <= %d, 0 <= rank < world and epoch > 0",
+                  FC_MAX_PEERS);
+        return FC_EINVAL;
+    }
+    for (int p = 0; p < peers->world; p++) {
+        if (!peers->out[p] || !peers->flags[p]) {
+            set_error("decode_attn_peers: null output or flag pointer of rank %d", p);
+            return FC_EINVAL;
+        }
+    }
+    return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype,
+                            k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj,
+                            k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn,
+                            scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st,
+                            raw_dtype, n_raw, A, softmax_scale, peers->out[peers->rank], out_dtype,
+                            o_sb, o_sh, workspace, workspace_bytes, stream, nullptr, nullptr, 0, 0,
+                            1, 1, peers);
 }
 
 extern "C" int fc_decode_attn_grouped(

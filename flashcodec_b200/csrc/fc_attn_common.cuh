@@ -12,6 +12,7 @@ namespace fc {
 
 constexpr uint64_t kWaitNs = 100000000ull;  // 100 ms bound on any wait
 constexpr int kWsHeader = 256;              // workspace bytes before the counters
+constexpr int kWsDoneOffset = 64;           // header int: launch completion count (peer outputs)
 
 // Launch epochs: a positive, increasing tag per call (wraps after 2^31 - 1).
 int next_epoch();
@@ -129,6 +130,13 @@ struct TcArgs {
     float *pm, *pl, *pacc;
     // shared memory carve-up (bytes from a 1024-aligned base)
     int off_bq, off_bw, off_xch, off_red, off_scr, off_bar;
+    // split KV heads (fc_decode_attn_peers): every output row is also stored
+    // to pout[0 .. npout) (the other ranks' buffers), and the CTA that stores
+    // the launch's last rows publishes pepoch in pflag[p][prank], p < pworld
+    void *pout[FC_MAX_PEERS];
+    int *pflag[FC_MAX_PEERS];
+    int npout, pworld, prank, pepoch;
+    int *done;  // launch completion counter (workspace header), left at zero
 };
 
 // Partials of one split of one (batch, KV head, head group): running max m,
@@ -145,11 +153,14 @@ struct Partials {
 // and writes the output rows of heads [hq0, hq0 + grun).  `scratch` holds at
 // least (n_split + 1) * GT floats of shared memory; every thread of the CTA
 // calls this (it contains barriers).  The counter is left at zero.
+// `xout[0 .. nx)` receive the same output rows as `out` (other ranks' buffers
+// of a split-head step).
 __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t grp, int split,
                                                    const float *s_m, const float *s_l,
                                                    float *scratch, int *s_flag, void *out,
                                                    int out_dtype, int64_t o_base, int64_t o_sh,
-                                                   int64_t hq0, int grun, int tid, int nthr) {
+                                                   int64_t hq0, int grun, int tid, int nthr,
+                                                   void *const *xout = nullptr, int nx = 0) {
     __threadfence();
     __syncthreads();
     if (tid == 0) *s_flag = (atomicAdd(P.cnt + grp, 1) == P.n_split - 1);
@@ -215,7 +226,10 @@ __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t gr
         for (; i < n; i++) o0 = fmaf(__ldcg(pa + (int64_t)i * step), fac[i * GT + gg], o0);
         const float o = (o0 + o1) + (o2 + o3);
         // Ls == 0 only when every position of the group was masked out
-        store_from_f32(out, o_base + (hq0 + gg) * o_sh + d, out_dtype, Ls[gg] > 0.0f ? o / Ls[gg] : 0.0f);
+        const float val = Ls[gg] > 0.0f ? o / Ls[gg] : 0.0f;
+        const int64_t oi = o_base + (hq0 + gg) * o_sh + d;
+        store_from_f32(out, oi, out_dtype, val);
+        for (int p = 0; p < nx; p++) store_from_f32(xout[p], oi, out_dtype, val);
     }
     if (tid == 0) P.cnt[grp] = 0;  // ready for the next launch
 }

@@ -421,10 +421,11 @@ FC_API int fc_decode_attn_masked(const void *q, int q_dtype, int64_t B, int64_t 
                                  const unsigned char *visible, int64_t vis_sb, void *stream);
 
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
- * AUTO uses the tcgen05 int8 tensor-core kernel whenever the archive allows
- * it (contiguous (B, Hk, cap, s, 128) int8 codes, block size 8 with
- * s in {1, 2, 4, 8} stored rows per block, Hq/Hk <= 8) and the
- * CUDA-core kernel otherwise.  CUDA_CORE forces the CUDA-core kernel;
+ * AUTO uses the tcgen05 tensor-core kernel whenever the archive allows it
+ * (contiguous (B, Hk, cap, s, 128) rows of int8 codes with one scale per row,
+ * or of bf16 coefficients without scales; block size 8 with s in
+ * {1, 2, 4, 8} stored rows per block, Hq/Hk <= 8) and the CUDA-core kernel
+ * otherwise.  CUDA_CORE forces the CUDA-core kernel;
  * TENSOR_CORE makes unsupported layouts fail with FC_ENOTSUP instead of
  * falling back.  Returns the previous setting, or -1 for an unknown value.
  * No counterpart in the reference (it has one GPU kernel). */
@@ -447,6 +448,78 @@ FC_API int fc_selftest_bounded_wait(int *status, int epoch, void *stream);
  * fc_decode_attn_noalloc_status can be shown to report a wait that gave up.
  * No counterpart in the reference. */
 FC_API int fc_selftest_noalloc_wait(int epoch, void *stream);
+
+/* ---- split KV heads over several GPUs: outputs stored into peer memory ----
+ *
+ * When a batch row's KV heads are split over ranks (one process per GPU), every
+ * rank needs the full (B, Hq, D) output.  Instead of a collective after the
+ * kernel, fc_decode_attn_peers stores each output row into every rank's output
+ * buffer over NVLink (plain peer stores; no multicast), and the CTA that stores
+ * the launch's last rows publishes `epoch` in slot `rank` of every rank's flag
+ * array (a system-scope release).  fc_peers_wait, queued on the consumer's
+ * stream, returns once every rank's epoch has arrived.  Buffers of other ranks
+ * are opened with fc_ipc_open_handle from the handles fc_ipc_get_handle gives.
+ * The reference runs on one device; the collective this replaces is the one
+ * all-gather of (B, Hq_local, D) outputs per layer a head-split step needs. */
+#define FC_MAX_PEERS 8
+#define FC_IPC_HANDLE_BYTES 64
+
+typedef struct fc_peer_out {
+    void *out[FC_MAX_PEERS];   /* rank p's output buffer, pre-offset to this rank's piece:
+                                  the element (b, h, d) of this call lands at
+                                  out[p] + b * o_sb + h * o_sh + d, as `out` of
+                                  fc_decode_attn; out[rank] is this rank's own buffer */
+    int *flags[FC_MAX_PEERS];  /* rank p's flag array (FC_MAX_PEERS ints, zeroed once) */
+    int world;                 /* ranks, 1 .. FC_MAX_PEERS */
+    int rank;                  /* this rank, 0 .. world - 1 */
+    int epoch;                 /* > 0, larger than every earlier epoch on these flags */
+} fc_peer_out;
+
+/* fc_decode_attn with the outputs placed as above (`out` of fc_decode_attn is
+ * peers->out[peers->rank]).  The tensor-core kernel's layouts only; others
+ * return FC_ENOTSUP.  The workspace's header holds the launch's completion
+ * counter, so calls on one workspace are ordered by its stream as usual.
+ * A rank's buffers must not be read by their owner while another rank's call
+ * may still store into them: give each layer (or each step in flight) its
+ * own output buffer.  If any CTA's bounded wait gives up, the launch stores
+ * no output and publishes nothing; the peers' fc_peers_wait then gives up
+ * too and records its epoch. */
+FC_API int fc_decode_attn_peers(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
+                                int64_t q_sb, int64_t q_sh,
+                                int64_t Hk, int64_t n_blocks, int s, int r, int rows_dtype,
+                                const void *k_rows, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                                int64_t k_sj,
+                                const void *v_rows, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                                int64_t v_sj,
+                                const void *k_scales, int64_t ks_sb, int64_t ks_sh, int64_t ks_sn,
+                                const void *v_scales, int64_t vs_sb, int64_t vs_sh, int64_t vs_sn,
+                                int scale_dtype,
+                                const void *k_raw, int64_t kr_sb, int64_t kr_sh, int64_t kr_st,
+                                const void *v_raw, int64_t vr_sb, int64_t vr_sh, int64_t vr_st,
+                                int raw_dtype, int64_t n_raw,
+                                const float *A, float softmax_scale,
+                                int out_dtype, int64_t o_sb, int64_t o_sh,
+                                const fc_peer_out *peers,
+                                void *workspace, size_t workspace_bytes, void *stream);
+
+/* Wait, on `stream`, until flags[p] has reached `epoch` for every p < world
+ * (the local flag array of fc_peer_out).  One small kernel: each of `world`
+ * threads polls one flag with system-scope acquire loads, sleeping between
+ * polls, and gives up after 100 ms of %globaltimer time, recording `epoch`
+ * in the device int *status (for instance the workspace status word) and
+ * returning; kernels queued after it see every output stored before the
+ * flags it observed.  No counterpart in the reference. */
+FC_API int fc_peers_wait(const int *flags, int world, int epoch, int *status, void *stream);
+
+/* CUDA IPC for the peer buffers (no counterpart in the reference).
+ * fc_ipc_get_handle: the FC_IPC_HANDLE_BYTES handle of the allocation that
+ * holds the device pointer `ptr`, and ptr's byte offset in it.
+ * fc_ipc_open_handle: maps another process's allocation on the current device
+ * (peer access enabled lazily) and returns its base; fc_ipc_close_handle
+ * unmaps it. */
+FC_API int fc_ipc_get_handle(const void *ptr, void *handle, int64_t *offset);
+FC_API int fc_ipc_open_handle(const void *handle, void **base);
+FC_API int fc_ipc_close_handle(void *base);
 
 #ifdef __cplusplus
 }
