@@ -783,6 +783,11 @@ def main():
                     help="archive format of the attention workload: jpeg-int8 (default, the "
                          "headline), jpeg-fp (quant_bits=0, bf16 coefficients) or png "
                          "(r=8, lossless; 4 layers by default)")
+    ap.add_argument("--gather", default="peer", choices=("peer", "nccl"),
+                    help="with split KV heads: peer (default) -- the attention kernel stores "
+                         "every output row into each rank's buffer over NVLink and publishes an "
+                         "epoch flag, one bounded wait per layer (fc_decode_attn_peers); nccl -- "
+                         "the kernel, then one NCCL all_gather per layer")
     ap.add_argument("--graph", action="store_true",
                     help="time the step as a CUDA graph replay of its attention launches "
                          "(captured once after warm-up; not with split heads); the oracle "
@@ -831,7 +836,16 @@ def main():
     else:
         rows, heads = (rank * cfg["B"], (rank + 1) * cfg["B"]), (0, Hk)
     gather = plan is not None and plan.needs_gather()
+    peer = gather and args.gather == "peer"
+    if peer and args.graph:
+        raise SystemExit("--graph times NCCL gathers; the peer path publishes a new epoch per "
+                         "call and runs eager (use --gather nccl with --graph)")
     layers = build_layers(cfg, dev, rows, heads, Bg=Bg or world * cfg["B"])
+    # peer outputs: two slots per layer, alternating by step, so a rank never
+    # stores into a buffer a peer may still be copying out from the step before
+    po = (sharding.PeerOutputs(plan, rank, 2 * len(layers), cfg["D"], layers[0][2].dtype, dev)
+          if peer else None)
+    parity = [0]
     n = layers[0][0].n_blocks
     local_cfg = dict(cfg, B=rows[1] - rows[0], Hk=heads[1] - heads[0],
                      Hq=(heads[1] - heads[0]) * G)
@@ -840,6 +854,12 @@ def main():
     full = [None] * len(layers)
 
     def step(with_gather=gather):
+        if with_gather and peer:
+            base = parity[0] * len(layers)
+            for i, (ks, vs, q) in enumerate(layers):
+                full[i] = po.decode(q, ks, vs, slot=base + i)
+            parity[0] ^= 1
+            return
         for i, (ks, vs, q) in enumerate(layers):
             outs[i] = fc.codec_decode_attention(q, ks, vs)
             if with_gather:
@@ -915,6 +935,7 @@ def main():
     nl = len(layers)
     ev_in = [torch.cuda.Event() for _ in range(nl)]
     ev_done = [torch.cuda.Event() for _ in range(nl)]
+    ev_copied = [torch.cuda.Event() for _ in range(nl)]
     first = [True]
 
     def e2e_step():
@@ -924,17 +945,27 @@ def main():
                     s_in.wait_event(ev_done[i])     # the last step's attention read qd[i]
                 qd[i].copy_(qh[i], non_blocking=True)
                 ev_in[i].record(s_in)
+        base = parity[0] * nl
         for i, (ks, vs, _) in enumerate(layers):
             stream.wait_event(ev_in[i])
-            outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
-            if gather:
-                full[i] = sharding.gather_outputs(plan, outs[i])
+            if peer:
+                if not first[0]:
+                    # this rank publishes layer i only after its copy of the
+                    # last step's layer-i output has left the other slot
+                    stream.wait_event(ev_copied[i])
+                full[i] = po.decode(qd[i], ks, vs, slot=base + i)
+            else:
+                outs[i] = fc.codec_decode_attention(qd[i], ks, vs)
+                if gather:
+                    full[i] = sharding.gather_outputs(plan, outs[i])
             r = full[i] if gather else outs[i]
             ev_done[i].record(stream)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_done[i])
                 oh[i].copy_(r, non_blocking=True)
                 r.record_stream(s_out)
+                ev_copied[i].record(s_out)
+        parity[0] ^= 1
         first[0] = False
 
     for _ in range(2):
@@ -959,6 +990,9 @@ def main():
     check = None
     if not args.no_check:
         step()
+        if peer:   # this rank's pieces from the plain kernel, to check the placement
+            for i, (ks, vs, q) in enumerate(layers):
+                outs[i] = fc.codec_decode_attention(q, ks, vs)
         torch.cuda.synchronize()
         check = check_outputs(layers, outs, sorted({0, len(layers) - 1}))
         if gather:
@@ -1006,19 +1040,25 @@ def main():
                     "d2h_bytes_per_step": oh.numel() * oh.element_size(),
                     "ms_per_step": e_ms},
             "check": check,
-            "gpu_launches": args.steps * len(layers),
+            "gpu_launches": args.steps * len(layers) * (2 if peer else 1),
             "clocks": clocks,
         }
         if gather:
             g_ms = (ms_max - ms_compute) / len(layers)
             line["head_split"] = {
+                "gather": ("peer stores from the attention kernel + one bounded flag wait per "
+                           "layer (fc_decode_attn_peers, fc_peers_wait)" if peer
+                           else "one NCCL all_gather per layer"),
                 "allgather_ms_per_layer": g_ms, "allgather_share": (ms_max - ms_compute) / ms_max,
                 "attention_ms_per_layer": kern_max,
-                "allgather_bytes_per_rank_per_layer": outs[0].numel() * outs[0].element_size(),
-                "note": "all_gather time = step time with the gather minus the step without it"}
+                "allgather_bytes_per_rank_per_layer":
+                    local_cfg["B"] * local_cfg["Hq"] * cfg["D"] * layers[0][2].element_size(),
+                "note": "gather time = step time with the gather minus the step without it"}
         print(json.dumps(line), flush=True)
     graphs.clear()           # graphs holding NCCL calls go before the process group
     torch.cuda.synchronize()
+    if po is not None:
+        po.close()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -369,12 +369,10 @@ def selftest_bounded_wait(status: torch.Tensor, epoch: int) -> None:
     _lib.check(rc, "selftest_bounded_wait")
 
 
-def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
-                ws: torch.Tensor | None = None, vis=None) -> None:
-    """q (B,Hq,1,D); krows/vrows (B,Hk,n,s,D) or None; k/vscales (B,Hk,n,s,1)
-    or None; kraw/vraw (B,Hk,t,D) or None; A (r,s) fp32; out (B,Hq,1,D);
-    vis: optional (B, n*r + t) key visibility (fc_decode_attn_masked)."""
-    require_cuda(q, krows, vrows, kscales, vscales, kraw, vraw, A, out)
+def _attn_args(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, ws):
+    """The arguments every decode-attention entry point shares, up to the
+    softmax scale, and the workspace to pass (cached one when ws is None)."""
+    require_cuda(q, krows, vrows, kscales, vscales, kraw, vraw, A)
     B, Hq, _, D = q.shape
     n = krows.shape[2] if krows is not None else 0
     s = krows.shape[3] if krows is not None else 1
@@ -385,7 +383,6 @@ def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
     if ws is None:
         ws = workspace(q.device, need)
     z = (0, 0, 0, 0)
-    st = _stream(q.device)
     args = (_p(q), dtype_code(q), B, Hq, D, q.stride(0), q.stride(1),
             Hk, n, s, r, dtype_code(krows) if krows is not None else 0,
             _p(krows), *(_s(krows, 0, 1, 2, 3) if krows is not None else z),
@@ -396,9 +393,20 @@ def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
             _p(kraw), *(_s(kraw, 0, 1, 2) if kraw is not None else z[:3]),
             _p(vraw), *(_s(vraw, 0, 1, 2) if vraw is not None else z[:3]),
             dtype_code(kraw) if kraw is not None else 0, t,
-            _p(A), float(scale),
-            _p(out), dtype_code(out), out.stride(0), out.stride(1),
-            _p(ws), ws.numel())
+            _p(A), float(scale))
+    return args, ws, n, r, t
+
+
+def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
+                ws: torch.Tensor | None = None, vis=None) -> None:
+    """q (B,Hq,1,D); krows/vrows (B,Hk,n,s,D) or None; k/vscales (B,Hk,n,s,1)
+    or None; kraw/vraw (B,Hk,t,D) or None; A (r,s) fp32; out (B,Hq,1,D);
+    vis: optional (B, n*r + t) key visibility (fc_decode_attn_masked)."""
+    require_cuda(out)
+    B = q.shape[0]
+    head, ws, n, r, t = _attn_args(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, ws)
+    args = head + (_p(out), dtype_code(out), out.stride(0), out.stride(1), _p(ws), ws.numel())
+    st = _stream(q.device)
     with torch.cuda.device(q.device):
         if vis is None:
             rc = _lib.load().fc_decode_attn(*args, st)
@@ -409,6 +417,59 @@ def decode_attn(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out,
     if rc != _lib.FC_OK:
         reset_workspace(q.device)
     _lib.check(rc, "decode_attn")
+
+
+def decode_attn_peers(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, out_dtype,
+                      o_sb: int, o_sh: int, peers, ws: torch.Tensor | None = None) -> None:
+    """fc_decode_attn_peers: the decode attention of this rank's KV heads with
+    every output row stored into each rank's buffer (peers: a _lib.PeerOut
+    whose out[p] are pre-offset to this rank's piece, strides o_sb, o_sh in
+    elements); the launch then publishes peers.epoch in every rank's flags."""
+    head, ws, _, _, _ = _attn_args(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, ws)
+    with torch.cuda.device(q.device):
+        rc = _lib.load().fc_decode_attn_peers(*head, DTYPE_CODE[out_dtype], o_sb, o_sh,
+                                              ctypes.byref(peers), _p(ws), ws.numel(),
+                                              _stream(q.device))
+    if rc != _lib.FC_OK:
+        reset_workspace(q.device)
+    _lib.check(rc, "decode_attn_peers")
+
+
+def peers_wait(flags: torch.Tensor, world: int, epoch: int, status: torch.Tensor | None) -> None:
+    """Queue fc_peers_wait on the current stream: flags[p] >= epoch for every
+    p < world, bounded; a wait that gives up writes epoch to status."""
+    require_cuda(flags)
+    with torch.cuda.device(flags.device):
+        rc = _lib.load().fc_peers_wait(_p(flags), world, epoch, _p(status),
+                                       _stream(flags.device))
+    _lib.check(rc, "peers_wait")
+
+
+def ipc_get_handle(t: torch.Tensor) -> tuple[bytes, int]:
+    """(CUDA IPC handle of the allocation holding t, t's byte offset in it)."""
+    require_cuda(t)
+    h = ctypes.create_string_buffer(_lib.FC_IPC_HANDLE_BYTES)
+    off = ctypes.c_int64(0)
+    with torch.cuda.device(t.device):
+        rc = _lib.load().fc_ipc_get_handle(_p(t), h, ctypes.byref(off))
+    _lib.check(rc, "ipc_get_handle")
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes, device: torch.device) -> int:
+    """Map another process's allocation on `device`; returns its base address."""
+    base = ctypes.c_void_p(0)
+    with torch.cuda.device(device):
+        rc = _lib.load().fc_ipc_open_handle(ctypes.create_string_buffer(handle, len(handle)),
+                                            ctypes.byref(base))
+    _lib.check(rc, "ipc_open_handle")
+    return int(base.value)
+
+
+def ipc_close(base: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        rc = _lib.load().fc_ipc_close_handle(ctypes.c_void_p(base))
+    _lib.check(rc, "ipc_close_handle")
 
 
 # ------------------------------------------------------------ one-launch append

@@ -106,3 +106,107 @@ def gather_outputs(plan: ShardPlan, out_local: torch.Tensor, group=None) -> torc
     full = [torch.empty_like(padded) for _ in range(world)]
     dist.all_gather(full, padded, group=group)
     return torch.cat([f[:n] for f, n in zip(full, sizes)], dim=0)
+
+
+class PeerOutputs:
+    """Output buffers of a split-KV-head decode step that every rank stores
+    into directly: the kernel-fused replacement for gather_outputs'
+    all-gather (fc_decode_attn_peers, csrc/fc_attention_tc.cu).
+
+    Each rank holds `slots` full (B, Hq, 1, D) outputs (one per layer, so a
+    layer's buffer is never overwritten while it may still be read) and a flag
+    array; CUDA IPC handles are exchanged once over the process group.  A call
+    of decode() runs this rank's KV heads, stores every output row into all
+    ranks' slot buffers over NVLink, publishes a new epoch, and queues a
+    bounded wait for every rank's epoch on the current stream, after which the
+    slot holds the full output.  Every rank calls decode() for the same slots
+    in the same order.  A wait that gives up records its epoch in the stream's
+    attention workspace status word (attention_status).  close() unmaps the
+    peers' buffers (collective)."""
+
+    def __init__(self, plan: ShardPlan, rank: int, slots: int, D: int, dtype: torch.dtype,
+                 device, group=None):
+        import torch.distributed as dist
+        from . import _kernels as K
+        from . import _lib
+        if plan.mode != "heads":
+            raise ValueError("PeerOutputs serves split KV heads (plan mode 'heads')")
+        if not 1 <= plan.world <= _lib.FC_MAX_PEERS:
+            raise ValueError(f"at most {_lib.FC_MAX_PEERS} ranks")
+        self.plan, self.rank, self.world, self.group = plan, rank, plan.world, group
+        self.device = torch.device(device)
+        self.bufs = torch.zeros((slots, plan.B, plan.Hq, 1, D), dtype=dtype, device=self.device)
+        self.flags = torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        torch.cuda.synchronize(self.device)
+        mine = (K.ipc_get_handle(self.bufs), K.ipc_get_handle(self.flags))
+        infos = [None] * self.world
+        dist.all_gather_object(infos, mine, group=group)
+        self._opened: dict = {}          # handle -> mapped base
+        es = self.bufs.element_size()
+        b0 = plan.batch_range(rank)[0]
+        h0 = plan.q_head_range(rank)[0]
+        piece = (b0 * plan.Hq + h0) * D * es   # this rank's rows inside a slot
+        slot_bytes = plan.B * plan.Hq * D * es
+        out_base, flag_base = [], []
+        for p, ((hb, ob), (hf, of)) in enumerate(infos):
+            if p == rank:
+                out_base.append(self.bufs.data_ptr())
+                flag_base.append(self.flags.data_ptr())
+            else:
+                out_base.append(self._open(hb) + ob)
+                flag_base.append(self._open(hf) + of)
+        self._tables = []
+        for s in range(slots):
+            t = _lib.PeerOut()
+            for p in range(self.world):
+                t.out[p] = out_base[p] + s * slot_bytes + piece
+                t.flags[p] = flag_base[p]
+            t.world, t.rank = self.world, rank
+            self._tables.append(t)
+
+    def _open(self, handle: bytes) -> int:
+        from . import _kernels as K
+        if handle not in self._opened:
+            self._opened[handle] = K.ipc_open(handle, self.device)
+        return self._opened[handle]
+
+    def decode(self, query: torch.Tensor, key_stream, value_stream, slot: int, scale=None):
+        """This rank's (1, Hq_local, 1, D) query against its KV-head streams;
+        returns slot `slot`'s full (B, Hq, 1, D) output, complete once the
+        queued wait has run (later work on the current stream sees it)."""
+        from . import _kernels as K
+        from .attention import _device_A, _rows
+        ks, vs = key_stream, value_stream
+        if ks.codec.name != "jpeg" or getattr(ks.codec, "group_size", None) is not None \
+                or ks.n_blocks == 0:
+            raise NotImplementedError("peer outputs take jpeg archives with one scale per "
+                                      "row and at least one archived block")
+        if query.dtype != self.bufs.dtype:
+            raise ValueError("query and output buffers must share a dtype")
+        D = query.shape[-1]
+        scale = D ** -0.5 if scale is None else scale
+        krows, kscales = _rows(ks)
+        vrows, vscales = _rows(vs)
+        A = _device_A(ks.codec, ks.block_size, query.device)
+        self.epoch += 1
+        t = self._tables[slot]
+        t.epoch = self.epoch
+        full = self.bufs[slot]
+        K.decode_attn_peers(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale,
+                            full.dtype, full.stride(0), full.stride(1), t)
+        ws = K.workspace(query.device, 0)
+        K.peers_wait(self.flags, self.world, self.epoch, ws)
+        return full
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers once every rank has finished with
+        them (collective: every rank calls it)."""
+        import torch.distributed as dist
+        from . import _kernels as K
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for base in self._opened.values():
+            K.ipc_close(base, self.device)
+        self._opened.clear()
+        dist.barrier(group=self.group)
