@@ -789,8 +789,9 @@ def main():
                          "epoch flag, one bounded wait per layer (fc_decode_attn_peers); nccl -- "
                          "the kernel, then one NCCL all_gather per layer")
     ap.add_argument("--graph", action="store_true",
-                    help="time the step as a CUDA graph replay of its attention launches "
-                         "(captured once after warm-up; not with split heads); the oracle "
+                    help="time the step as a CUDA graph replay of its launches (captured once "
+                         "after warm-up, with split heads including the gathers: NCCL calls, or "
+                         "the peer waits, whose epochs come from a device counter); the oracle "
                          "check and e2e stay eager")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true",
@@ -837,9 +838,6 @@ def main():
         rows, heads = (rank * cfg["B"], (rank + 1) * cfg["B"]), (0, Hk)
     gather = plan is not None and plan.needs_gather()
     peer = gather and args.gather == "peer"
-    if peer and args.graph:
-        raise SystemExit("--graph times NCCL gathers; the peer path publishes a new epoch per "
-                         "call and runs eager (use --gather nccl with --graph)")
     layers = build_layers(cfg, dev, rows, heads, Bg=Bg or world * cfg["B"])
     # peer outputs: two slots per layer, alternating by step, so a rank never
     # stores into a buffer a peer may still be copying out from the step before

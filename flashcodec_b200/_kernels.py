@@ -435,12 +435,15 @@ def decode_attn_peers(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, o
     _lib.check(rc, "decode_attn_peers")
 
 
-def peers_wait(flags: torch.Tensor, world: int, epoch: int, status: torch.Tensor | None) -> None:
-    """Queue fc_peers_wait on the current stream: flags[p] >= epoch for every
-    p < world, bounded; a wait that gives up writes epoch to status."""
-    require_cuda(flags)
+def peers_wait(flags: torch.Tensor, world: int, epoch: int, status: torch.Tensor | None,
+               counter: torch.Tensor | None = None) -> None:
+    """Queue fc_peers_wait on the current stream: flags[p] >= the epoch for
+    every p < world, bounded; a wait that gives up writes the epoch to
+    status.  With `counter` (device int32) the epoch is counter + 1, read on
+    the device, and the wait advances the counter."""
+    require_cuda(flags, counter)
     with torch.cuda.device(flags.device):
-        rc = _lib.load().fc_peers_wait(_p(flags), world, epoch, _p(status),
+        rc = _lib.load().fc_peers_wait(_p(flags), world, epoch, _p(counter), _p(status),
                                        _stream(flags.device))
     _lib.check(rc, "peers_wait")
 

@@ -1049,6 +1049,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
                 t.pworld = peers->world;
                 t.prank = peers->rank;
                 t.pepoch = peers->epoch;
+                t.pctr = peers->counter;
                 t.done = reinterpret_cast<int *>(wsb + kWsDoneOffset);
             }
             return launch_attn_tc(t, B, k_rows, v_rows, rows_dtype == FC_BF16,
@@ -1165,9 +1166,9 @@ extern "C" int fc_decode_attn_peers(
     void *workspace, size_t workspace_bytes, void *stream) {
     clear_error();
     if (!peers || peers->world < 1 || peers->world > FC_MAX_PEERS || peers->rank < 0 ||
-        peers->rank >= peers->world || peers->epoch <= 0) {
-        set_error("decode_attn_peers: need 1 <= world <= %d, 0 <= rank < world and epoch > 0",
-                  FC_MAX_PEERS);
+        peers->rank >= peers->world || (peers->epoch <= 0 && !peers->counter)) {
+        set_error("decode_attn_peers: need 1 <= world <= %d, 0 <= rank < world and an epoch > 0 "
+                  "or a counter", FC_MAX_PEERS);
         return FC_EINVAL;
     }
     for (int p = 0; p < peers->world; p++) {

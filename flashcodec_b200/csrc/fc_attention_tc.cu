@@ -250,9 +250,12 @@ __device__ __forceinline__ void peer_publish(const TcArgs &a, int tid, int units
     __syncthreads();
     if (tid == 0 && atomicAdd(a.done, 1) == units - 1) {
         __threadfence_system();
+        // the counter was last written by the previous fc_peers_wait on this
+        // stream, which completed before this grid passed griddepcontrol.wait
+        const int epoch = a.pctr ? *reinterpret_cast<const volatile int *>(a.pctr) + 1 : a.pepoch;
         for (int p = 0; p < a.pworld; p++)
             asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.pflag[p] + a.prank),
-                         "r"(a.pepoch)
+                         "r"(epoch)
                          : "memory");
         atomicExch(a.done, 0);
     }

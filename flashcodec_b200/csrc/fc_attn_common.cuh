@@ -136,6 +136,7 @@ struct TcArgs {
     void *pout[FC_MAX_PEERS];
     int *pflag[FC_MAX_PEERS];
     int npout, pworld, prank, pepoch;
+    const int *pctr;  // when set, the epoch is *pctr + 1 (read when publishing)
     int *done;  // launch completion counter (workspace header), left at zero
 };
 

@@ -27,20 +27,29 @@ __device__ __forceinline__ int ld_acquire_sys(const int *p) {
 }
 
 // One thread per rank; epochs only grow, so "arrived" is flag - epoch >= 0
-// (wrap-safe over the int range).
-__global__ void peers_wait_kernel(const int *flags, int world, int epoch, int *status) {
+// (wrap-safe over the int range).  With a counter the epoch is *counter + 1,
+// stored back once every thread is done (also after a wait that gave up, so
+// the ranks' epochs stay in step).
+__global__ void peers_wait_kernel(const int *flags, int world, int epoch, int *counter,
+                                  int *status) {
+    __shared__ int s_epoch;
+    if (threadIdx.x == 0) s_epoch = counter ? *counter + 1 : epoch;
+    __syncthreads();
+    const int e = s_epoch;
     const int p = threadIdx.x;
-    if (p >= world) return;
-    if (ld_acquire_sys(flags + p) - epoch >= 0) return;
-    const uint64_t t0 = global_ns();
-    while (true) {
-        __nanosleep(200);
-        if (ld_acquire_sys(flags + p) - epoch >= 0) return;
-        if (global_ns() - t0 > kWaitNs) {
-            if (status) atomicExch(status, epoch);
-            return;
+    if (p < world && ld_acquire_sys(flags + p) - e < 0) {
+        const uint64_t t0 = global_ns();
+        while (true) {
+            __nanosleep(200);
+            if (ld_acquire_sys(flags + p) - e >= 0) break;
+            if (global_ns() - t0 > kWaitNs) {
+                if (status) atomicExch(status, e);
+                break;
+            }
         }
     }
+    __syncthreads();
+    if (threadIdx.x == 0 && counter) *counter = e;
 }
 
 PFN_cuMemGetAddressRange_v3020 get_range_fn() {
@@ -64,13 +73,16 @@ using namespace fc;
 
 static_assert(sizeof(cudaIpcMemHandle_t) <= FC_IPC_HANDLE_BYTES, "IPC handle size");
 
-extern "C" int fc_peers_wait(const int *flags, int world, int epoch, int *status, void *stream) {
+extern "C" int fc_peers_wait(const int *flags, int world, int epoch, int *counter, int *status,
+                             void *stream) {
     clear_error();
-    if (!flags || world < 1 || world > FC_MAX_PEERS || epoch <= 0) {
-        set_error("peers_wait: need flags, 1 <= world <= %d and epoch > 0", FC_MAX_PEERS);
+    if (!flags || world < 1 || world > FC_MAX_PEERS || (epoch <= 0 && !counter)) {
+        set_error("peers_wait: need flags, 1 <= world <= %d and an epoch > 0 or a counter",
+                  FC_MAX_PEERS);
         return FC_EINVAL;
     }
-    peers_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, epoch, status);
+    peers_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, epoch, counter,
+                                                                        status);
     return check_launch("peers_wait");
 }
 

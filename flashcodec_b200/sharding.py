@@ -120,7 +120,9 @@ class PeerOutputs:
     ranks' slot buffers over NVLink, publishes a new epoch, and queues a
     bounded wait for every rank's epoch on the current stream, after which the
     slot holds the full output.  Every rank calls decode() for the same slots
-    in the same order.  A wait that gives up records its epoch in the stream's
+    in the same order.  Epochs come from a device counter that each wait
+    advances, so decode() calls captured in a CUDA graph publish a new epoch
+    on every replay.  A wait that gives up records its epoch in the stream's
     attention workspace status word (attention_status).  close() unmaps the
     peers' buffers (collective)."""
 
@@ -137,7 +139,7 @@ class PeerOutputs:
         self.device = torch.device(device)
         self.bufs = torch.zeros((slots, plan.B, plan.Hq, 1, D), dtype=dtype, device=self.device)
         self.flags = torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=self.device)
-        self.epoch = 0
+        self.counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
         mine = (K.ipc_get_handle(self.bufs), K.ipc_get_handle(self.flags))
         infos = [None] * self.world
@@ -163,6 +165,7 @@ class PeerOutputs:
                 t.out[p] = out_base[p] + s * slot_bytes + piece
                 t.flags[p] = flag_base[p]
             t.world, t.rank = self.world, rank
+            t.counter = self.counter.data_ptr()
             self._tables.append(t)
 
     def _open(self, handle: bytes) -> int:
@@ -189,14 +192,11 @@ class PeerOutputs:
         krows, kscales = _rows(ks)
         vrows, vscales = _rows(vs)
         A = _device_A(ks.codec, ks.block_size, query.device)
-        self.epoch += 1
-        t = self._tables[slot]
-        t.epoch = self.epoch
         full = self.bufs[slot]
         K.decode_attn_peers(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale,
-                            full.dtype, full.stride(0), full.stride(1), t)
+                            full.dtype, full.stride(0), full.stride(1), self._tables[slot])
         ws = K.workspace(query.device, 0)
-        K.peers_wait(self.flags, self.world, self.epoch, ws)
+        K.peers_wait(self.flags, self.world, 0, ws, counter=self.counter)
         return full
 
     def close(self) -> None:

@@ -472,7 +472,13 @@ typedef struct fc_peer_out {
     int *flags[FC_MAX_PEERS];  /* rank p's flag array (FC_MAX_PEERS ints, zeroed once) */
     int world;                 /* ranks, 1 .. FC_MAX_PEERS */
     int rank;                  /* this rank, 0 .. world - 1 */
-    int epoch;                 /* > 0, larger than every earlier epoch on these flags */
+    int epoch;                 /* > 0, larger than every earlier epoch on these flags;
+                                  ignored when `counter` is set */
+    int *counter;              /* optional device int of this rank (zeroed once): the launch
+                                  publishes *counter + 1, read on the device, and the
+                                  fc_peers_wait given the same counter advances it -- so a
+                                  captured CUDA graph of the calls publishes a new epoch on
+                                  every replay */
 } fc_peer_out;
 
 /* fc_decode_attn with the outputs placed as above (`out` of fc_decode_attn is
@@ -502,14 +508,18 @@ FC_API int fc_decode_attn_peers(const void *q, int q_dtype, int64_t B, int64_t H
                                 const fc_peer_out *peers,
                                 void *workspace, size_t workspace_bytes, void *stream);
 
-/* Wait, on `stream`, until flags[p] has reached `epoch` for every p < world
- * (the local flag array of fc_peer_out).  One small kernel: each of `world`
- * threads polls one flag with system-scope acquire loads, sleeping between
- * polls, and gives up after 100 ms of %globaltimer time, recording `epoch`
- * in the device int *status (for instance the workspace status word) and
- * returning; kernels queued after it see every output stored before the
- * flags it observed.  No counterpart in the reference. */
-FC_API int fc_peers_wait(const int *flags, int world, int epoch, int *status, void *stream);
+/* Wait, on `stream`, until flags[p] has reached the epoch for every
+ * p < world (the local flag array of fc_peer_out).  The epoch is `epoch`, or,
+ * when `counter` (the fc_peer_out counter) is non-NULL, *counter + 1 read on
+ * the device, and the kernel stores it back into *counter before it returns.
+ * One small kernel: each of `world` threads polls one flag with system-scope
+ * acquire loads, sleeping between polls, and gives up after 100 ms of
+ * %globaltimer time, recording the epoch in the device int *status (for
+ * instance the workspace status word) and returning; kernels queued after it
+ * see every output stored before the flags it observed.  No counterpart in
+ * the reference. */
+FC_API int fc_peers_wait(const int *flags, int world, int epoch, int *counter, int *status,
+                         void *stream);
 
 /* CUDA IPC for the peer buffers (no counterpart in the reference).
  * fc_ipc_get_handle: the FC_IPC_HANDLE_BYTES handle of the allocation that

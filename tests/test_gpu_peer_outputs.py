@@ -99,6 +99,58 @@ def test_two_ranks_emulated_on_one_gpu(S, quant):
     assert torch.equal(local[0], local[1])
 
 
+def test_two_ranks_emulated_replay_in_a_cuda_graph():
+    """Device-counter epochs: both ranks' peer launches and both waits are
+    captured once in a CUDA graph and replayed three times; every replay
+    publishes a new epoch (flags and counters end at 4 after the eager call
+    and three replays), no wait gives up, and both buffers hold the output of
+    the eager call."""
+    from flashcodec_b200 import _kernels as K
+    from flashcodec_b200 import _lib
+    dev = torch.device(DEV, 0)
+    B, Hq, Hk, D, world = 1, 32, 8, 128, 2
+    G = Hq // Hk
+    k, v, q = bench.synth_case(B, Hq, Hk, 8 * 700 + 2, D, 0.95, 43, dtype=torch.bfloat16)
+    bufs = [torch.zeros(B, Hq, 1, D, dtype=torch.bfloat16, device=dev) for _ in range(world)]
+    flags = [torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=dev) for _ in range(world)]
+    ctrs = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(world)]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    es = bufs[0].element_size()
+    ranks = []
+    for rank in range(world):
+        h0, h1 = rank * Hk // world, (rank + 1) * Hk // world
+        lks, lvs = _streams(k[:, h0:h1], v[:, h0:h1], dev)
+        t = _lib.PeerOut()
+        for p in range(world):
+            t.out[p] = bufs[p].data_ptr() + h0 * G * D * es
+            t.flags[p] = flags[p].data_ptr()
+        t.world, t.rank, t.epoch, t.counter = world, rank, 0, ctrs[rank].data_ptr()
+        ranks.append((q[:, h0 * G:h1 * G].to(dev).contiguous(), lks, lvs, t))
+
+    def step():
+        for ql, lks, lvs, t in ranks:
+            _peer_call(ql, lks, lvs, t, bufs[0].stride(0), bufs[0].stride(1))
+        for rank in range(world):
+            K.peers_wait(flags[rank], world, 0, status, counter=ctrs[rank])
+
+    step()                     # eager: the kernels' one-time set-up happens here
+    torch.cuda.synchronize()
+    eager = bufs[0].clone()
+    for b in bufs:
+        b.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert torch.equal(bufs[0], eager) and torch.equal(bufs[1], eager)
+    # the eager call and three replays (capturing runs nothing)
+    assert [c.item() for c in ctrs] == [4, 4]
+    assert flags[0][:world].tolist() == [4, 4] and flags[1][:world].tolist() == [4, 4]
+
+
 def test_peer_outputs_refuse_cuda_core_layouts():
     """Peer outputs need the tensor-core kernel: head dim 64 is refused
     loudly, before anything is stored or published."""
