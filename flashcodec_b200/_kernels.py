@@ -435,16 +435,19 @@ def decode_attn_peers(q, krows, vrows, kscales, vscales, kraw, vraw, A, scale, o
     _lib.check(rc, "decode_attn_peers")
 
 
-def peers_wait(flags: torch.Tensor, world: int, epoch: int, status: torch.Tensor | None,
+def peers_wait(recv: torch.Tensor, out: torch.Tensor, world: int, rank: int, piece_words: int,
+               epoch: int, status: torch.Tensor | None,
                counter: torch.Tensor | None = None) -> None:
-    """Queue fc_peers_wait on the current stream: flags[p] >= the epoch for
-    every p < world, bounded; a wait that gives up writes the epoch to
+    """Queue fc_peers_wait on the current stream: wait (bounded) for the
+    other ranks' pieces in this rank's receive area `recv` (world pieces of
+    piece_words 8-byte words) and unpack them into `out` (rank p's piece at
+    byte 4 * p * piece_words); a wait that gives up writes the epoch to
     status.  With `counter` (device int32) the epoch is counter + 1, read on
     the device, and the wait advances the counter."""
-    require_cuda(flags, counter)
-    with torch.cuda.device(flags.device):
-        rc = _lib.load().fc_peers_wait(_p(flags), world, epoch, _p(counter), _p(status),
-                                       _stream(flags.device))
+    require_cuda(recv, out, counter)
+    with torch.cuda.device(recv.device):
+        rc = _lib.load().fc_peers_wait(_p(recv), _p(out), world, rank, piece_words, epoch,
+                                       _p(counter), _p(status), _stream(recv.device))
     _lib.check(rc, "peers_wait")
 
 

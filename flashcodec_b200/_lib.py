@@ -33,8 +33,9 @@ _I64, _I32, _P, _F32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_f
 
 
 class PeerOut(ctypes.Structure):
-    """fc_peer_out: every rank's output buffer and flag array of a split-head step."""
-    _fields_ = [("out", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
+    """fc_peer_out: this rank's output piece and every rank's receive area of a
+    split-head step."""
+    _fields_ = [("out", ctypes.c_void_p), ("recv", ctypes.c_void_p * 8),
                 ("world", ctypes.c_int), ("rank", ctypes.c_int), ("epoch", ctypes.c_int),
                 ("counter", ctypes.c_void_p)]
 
@@ -147,7 +148,7 @@ _SIGS = {
                               _P, _F32,
                               _I32, _I64, _I64, _P,
                               _P, ctypes.c_size_t, _P], _I32),
-    "fc_peers_wait": ([_P, _I32, _I32, _P, _P, _P], _I32),
+    "fc_peers_wait": ([_P, _P, _I32, _I32, _I64, _I32, _P, _P, _P], _I32),
     "fc_ipc_get_handle": ([_P, _P, _P], _I32),
     "fc_ipc_open_handle": ([_P, _P], _I32),
     "fc_ipc_close_handle": ([_P], _I32),

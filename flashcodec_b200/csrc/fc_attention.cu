@@ -1042,15 +1042,11 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
             off = align_up(off + slots * GT * 4, 256);
             t.pacc = reinterpret_cast<float *>(wsb + off);
             if (peers) {
-                for (int p = 0; p < peers->world; p++) {
-                    if (p != peers->rank) t.pout[t.npout++] = peers->out[p];
-                    t.pflag[p] = peers->flags[p];
-                }
-                t.pworld = peers->world;
-                t.prank = peers->rank;
+                for (int p = 0; p < peers->world; p++)
+                    if (p != peers->rank)
+                        t.precv[t.nrecv++] = static_cast<unsigned long long *>(peers->recv[p]);
                 t.pepoch = peers->epoch;
                 t.pctr = peers->counter;
-                t.done = reinterpret_cast<int *>(wsb + kWsDoneOffset);
             }
             return launch_attn_tc(t, B, k_rows, v_rows, rows_dtype == FC_BF16,
                                   static_cast<cudaStream_t>(stream));
@@ -1171,17 +1167,22 @@ extern "C" int fc_decode_attn_peers(
                   "or a counter", FC_MAX_PEERS);
         return FC_EINVAL;
     }
+    if (!peers->out) { set_error("decode_attn_peers: null output"); return FC_EINVAL; }
     for (int p = 0; p < peers->world; p++) {
-        if (!peers->out[p] || !peers->flags[p]) {
-            set_error("decode_attn_peers: null output or flag pointer of rank %d", p);
+        if (p != peers->rank && (!peers->recv[p] || !aligned(peers->recv[p], 8))) {
+            set_error("decode_attn_peers: receive area of rank %d is null or not 8-byte aligned", p);
             return FC_EINVAL;
         }
+    }
+    if ((D * dtype_size(out_dtype)) % 4 != 0) {
+        set_error("decode_attn_peers: a head's output row must be a multiple of 4 bytes");
+        return FC_EINVAL;
     }
     return decode_attn_impl(q, q_dtype, B, Hq, D, q_sb, q_sh, Hk, n_blocks, s, r, rows_dtype,
                             k_rows, k_sb, k_sh, k_sn, k_sj, v_rows, v_sb, v_sh, v_sn, v_sj,
                             k_scales, ks_sb, ks_sh, ks_sn, v_scales, vs_sb, vs_sh, vs_sn,
                             scale_dtype, k_raw, kr_sb, kr_sh, kr_st, v_raw, vr_sb, vr_sh, vr_st,
-                            raw_dtype, n_raw, A, softmax_scale, peers->out[peers->rank], out_dtype,
+                            raw_dtype, n_raw, A, softmax_scale, peers->out, out_dtype,
                             o_sb, o_sh, workspace, workspace_bytes, stream, nullptr, nullptr, 0, 0,
                             1, 1, peers);
 }

@@ -240,27 +240,6 @@ __host__ __device__ constexpr int tc_stages() { return (BF && GT == 8) ? 2 : kTc
 template <bool BF, int GT>
 __host__ __device__ constexpr int tc_min_ctas() { return BF ? 2 : (GT <= 4 ? 4 : 3); }
 
-// Split-head step: once this CTA's output rows are stored (locally and into
-// the other ranks' buffers), count the unit; the CTA that counts the launch's
-// last unit publishes the epoch to every rank's flag array (system-scope
-// release after a system-scope fence, so a rank that sees its flag sees every
-// row stored before it) and leaves the counter at zero.  Every thread calls it.
-__device__ __forceinline__ void peer_publish(const TcArgs &a, int tid, int units) {
-    __threadfence_system();
-    __syncthreads();
-    if (tid == 0 && atomicAdd(a.done, 1) == units - 1) {
-        __threadfence_system();
-        // the counter was last written by the previous fc_peers_wait on this
-        // stream, which completed before this grid passed griddepcontrol.wait
-        const int epoch = a.pctr ? *reinterpret_cast<const volatile int *>(a.pctr) + 1 : a.pepoch;
-        for (int p = 0; p < a.pworld; p++)
-            asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.pflag[p] + a.prank),
-                         "r"(epoch)
-                         : "memory");
-        atomicExch(a.done, 0);
-    }
-}
-
 template <int GT, int S, bool BF>
 __global__ void __launch_bounds__(kTcThreads, tc_min_ctas<BF, GT>())
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -782,10 +761,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 #pragma unroll
                 for (int g = 0; g < GT; g++)
                     if (g < G) {
-                        const int64_t oi = b * a.o_sb + (hq0 + g) * a.o_sh + d;
-                        store_from_f32(a.out, oi, a.out_dtype, acc[g] / L[g]);
-                        for (int p = 0; p < a.npout; p++)
-                            store_from_f32(a.pout[p], oi, a.out_dtype, acc[g] / L[g]);
+                        const float val = acc[g] / L[g];
+                        store_from_f32(a.out, b * a.o_sb + (hq0 + g) * a.o_sh + d, a.out_dtype, val);
+                        if (a.nrecv > 0)  // element (b, hq0 + g, d) of the (B, Hk * G, 128) piece
+                            peer_send(a.precv, a.nrecv, peer_epoch(a.pctr, a.pepoch),
+                                      ((b * a.Hk * G + hq0 + g) << 7) + d, val, a.out_dtype);
                     }
             } else {
                 const int64_t slot = unit * a.n_split + split;
@@ -817,12 +797,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         __syncwarp();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kAlloc));
     }
-    if (ab) return;
-    const int units = (int)(gridDim.x / a.n_split);
-    if (a.n_split == 1) {
-        if (a.pworld > 0) peer_publish(a, tid, units);
-        return;
-    }
+    if (ab || a.n_split == 1) return;
 
     // ------------------------------------------- last-arriver merge of splits
     if (tid < GT) {
@@ -831,8 +806,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     }
     const Partials P{a.cnt, a.pm, a.pl, a.pacc, a.n_split, GT, 128};
     merge_last_arriver(P, unit, split, s_fin, s_fin + 8, scr, &s_last, a.out, a.out_dtype,
-                       b * a.o_sb, a.o_sh, hq0, G, tid, kTcThreads, a.pout, a.npout);
-    if (a.pworld > 0 && s_last) peer_publish(a, tid, units);
+                       b * a.o_sb, a.o_sh, hq0, G, tid, kTcThreads, a.precv, a.nrecv,
+                       a.nrecv > 0 ? peer_epoch(a.pctr, a.pepoch) : 0, b * a.Hk * G * 128);
 }
 
 // ----------------------------------------------------------------- host side

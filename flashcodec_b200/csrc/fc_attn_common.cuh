@@ -12,7 +12,6 @@ namespace fc {
 
 constexpr uint64_t kWaitNs = 100000000ull;  // 100 ms bound on any wait
 constexpr int kWsHeader = 256;              // workspace bytes before the counters
-constexpr int kWsDoneOffset = 64;           // header int: launch completion count (peer outputs)
 
 // Launch epochs: a positive, increasing tag per call (wraps after 2^31 - 1).
 int next_epoch();
@@ -130,15 +129,50 @@ struct TcArgs {
     float *pm, *pl, *pacc;
     // shared memory carve-up (bytes from a 1024-aligned base)
     int off_bq, off_bw, off_xch, off_red, off_scr, off_bar;
-    // split KV heads (fc_decode_attn_peers): every output row is also stored
-    // to pout[0 .. npout) (the other ranks' buffers), and the CTA that stores
-    // the launch's last rows publishes pepoch in pflag[p][prank], p < pworld
-    void *pout[FC_MAX_PEERS];
-    int *pflag[FC_MAX_PEERS];
-    int npout, pworld, prank, pepoch;
-    const int *pctr;  // when set, the epoch is *pctr + 1 (read when publishing)
-    int *done;  // launch completion counter (workspace header), left at zero
+    // split KV heads (fc_decode_attn_peers): every output element is also sent
+    // to precv[0 .. nrecv) (the other ranks' receive areas for this rank's
+    // piece) as {4 output bytes, epoch} words; the epoch is *pctr + 1 when pctr
+    // is set, else pepoch
+    unsigned long long *precv[FC_MAX_PEERS];
+    int nrecv, pepoch;
+    const int *pctr;
 };
+
+// The epoch of a split-head launch.  The counter was last written by the
+// fc_peers_wait before this launch on its stream, which completed before the
+// launch passed griddepcontrol.wait.
+__device__ __forceinline__ int peer_epoch(const int *ctr, int epoch) {
+    return ctr ? *reinterpret_cast<const volatile int *>(ctr) + 1 : epoch;
+}
+
+// Send element e of this rank's contiguous output piece (value v, stored as
+// dtype dt) to the other ranks' receive areas as self-validating 8-byte words
+// {4 bytes of the piece, epoch} -- one store each, no fence: a reader accepts a
+// word once its epoch half matches.  For 2-byte outputs the even element of
+// each pair sends both (the odd one's value comes from the neighbouring lane,
+// which must hold element e ^ 1); every lane of the warp calls it together.
+__device__ __forceinline__ void peer_send(unsigned long long *const *recv, int n, int epoch,
+                                          int64_t e, float v, int dt) {
+    uint32_t word;
+    int64_t w;
+    if (dt == FC_F32) {
+        word = __float_as_uint(v);
+        w = e;
+    } else {
+        const float o = __shfl_xor_sync(0xffffffffu, v, 1);
+        if (e & 1) return;
+        const uint32_t lo = dt == FC_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v))
+                                          : __half_as_ushort(__float2half_rn(v));
+        const uint32_t hi = dt == FC_BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o))
+                                          : __half_as_ushort(__float2half_rn(o));
+        word = lo | (hi << 16);
+        w = e >> 1;
+    }
+    for (int p = 0; p < n; p++)
+        asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(recv[p] + w), "r"(word),
+                     "r"(epoch)
+                     : "memory");
+}
 
 // Partials of one split of one (batch, KV head, head group): running max m,
 // sum l (both per head, base-2 logits) and the unnormalised output acc[g][d].
@@ -154,14 +188,17 @@ struct Partials {
 // and writes the output rows of heads [hq0, hq0 + grun).  `scratch` holds at
 // least (n_split + 1) * GT floats of shared memory; every thread of the CTA
 // calls this (it contains barriers).  The counter is left at zero.
-// `xout[0 .. nx)` receive the same output rows as `out` (other ranks' buffers
-// of a split-head step).
+// With nrecv > 0 (a split-head step) every output element is also sent to
+// the other ranks' receive areas (peer_send); element (h, d) of the merged
+// group is element e_base + h * P.D + d of this rank's piece.
 __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t grp, int split,
                                                    const float *s_m, const float *s_l,
                                                    float *scratch, int *s_flag, void *out,
                                                    int out_dtype, int64_t o_base, int64_t o_sh,
                                                    int64_t hq0, int grun, int tid, int nthr,
-                                                   void *const *xout = nullptr, int nx = 0) {
+                                                   unsigned long long *const *recv = nullptr,
+                                                   int nrecv = 0, int epoch = 0,
+                                                   int64_t e_base = 0) {
     __threadfence();
     __syncthreads();
     if (tid == 0) *s_flag = (atomicAdd(P.cnt + grp, 1) == P.n_split - 1);
@@ -228,9 +265,9 @@ __device__ __forceinline__ void merge_last_arriver(const Partials &P, int64_t gr
         const float o = (o0 + o1) + (o2 + o3);
         // Ls == 0 only when every position of the group was masked out
         const float val = Ls[gg] > 0.0f ? o / Ls[gg] : 0.0f;
-        const int64_t oi = o_base + (hq0 + gg) * o_sh + d;
-        store_from_f32(out, oi, out_dtype, val);
-        for (int p = 0; p < nx; p++) store_from_f32(xout[p], oi, out_dtype, val);
+        store_from_f32(out, o_base + (hq0 + gg) * o_sh + d, out_dtype, val);
+        // (whole warps stay together here: D is a multiple of 32 on this path)
+        if (nrecv > 0) peer_send(recv, nrecv, epoch, e_base + (hq0 + gg) * P.D + d, val, out_dtype);
     }
     if (tid == 0) P.cnt[grp] = 0;  // ready for the next launch
 }

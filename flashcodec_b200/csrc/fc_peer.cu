@@ -1,15 +1,15 @@
 // Split KV heads over GPUs without a collective: the consumer-side wait for
 // the peer stores of fc_decode_attn_peers, and the CUDA IPC calls that give
-// each rank the other ranks' output buffers and flag arrays.
+// each rank the other ranks' receive areas.
 //
-// Each rank's attention launch stores its output rows into every rank's
-// buffer over NVLink and then publishes its epoch in slot `rank` of every
-// rank's flag array with a system-scope release (fc_attention_tc.cu,
-// peer_publish).  fc_peers_wait polls the local flag array with system-scope
-// acquire loads; everything a peer stored before its release is visible to the
-// kernels queued after the wait on this rank's stream.  The wait is bounded
-// (100 ms of %globaltimer time, as every wait in the attention kernels): a
-// rank that never publishes leaves an error status, not a hung GPU.
+// Each rank's attention launch sends every element of its output piece to
+// every other rank's receive area as self-validating 8-byte words {4 bytes of
+// the piece, epoch} (peer_send in fc_attn_common.cuh): an 8-byte store lands
+// whole, so a reader that sees the epoch half also sees the data half, and no
+// fence or flag is needed.  fc_peers_wait polls the words of the other ranks'
+// pieces and unpacks them into the local output.  The wait is bounded (100 ms
+// of %globaltimer time, as every wait in the attention kernels): a rank that
+// never sends leaves an error status, not a hung GPU.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -20,32 +20,52 @@
 namespace fc {
 namespace {
 
-__device__ __forceinline__ int ld_acquire_sys(const int *p) {
-    int v;
-    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+constexpr int kWaitThreads = 512;
+
+__device__ __forceinline__ uint2 ld_word(const unsigned long long *p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p)
+                 : "memory");
     return v;
 }
 
-// One thread per rank; epochs only grow, so "arrived" is flag - epoch >= 0
-// (wrap-safe over the int range).  With a counter the epoch is *counter + 1,
-// stored back once every thread is done (also after a wait that gave up, so
-// the ranks' epochs stay in step).
-__global__ void peers_wait_kernel(const int *flags, int world, int epoch, int *counter,
-                                  int *status) {
+// One CTA.  Word w of rank p's piece goes to 32-bit word p * piece_words + w
+// of the output.  Epochs only grow, so a word is current once its epoch half
+// minus the epoch is >= 0 (wrap-safe over the int range).  With a counter the
+// epoch is *counter + 1, stored back once every thread is done (also after a
+// wait that gave up, so the ranks' epochs stay in step).
+__global__ void __launch_bounds__(kWaitThreads)
+peers_wait_kernel(const unsigned long long *recv, uint32_t *out, int world, int rank,
+                  int64_t piece_words, int epoch, int *counter, int *status) {
+    // A following attention launch (a programmatic dependent) may set up its
+    // barriers and TMEM while this wait polls; it reads nothing before its
+    // griddepcontrol.wait, which returns only once this grid has completed.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ int s_epoch;
-    if (threadIdx.x == 0) s_epoch = counter ? *counter + 1 : epoch;
+    __shared__ volatile int s_dead;
+    if (threadIdx.x == 0) {
+        s_epoch = counter ? *counter + 1 : epoch;
+        s_dead = 0;
+    }
     __syncthreads();
     const int e = s_epoch;
-    const int p = threadIdx.x;
-    if (p < world && ld_acquire_sys(flags + p) - e < 0) {
-        const uint64_t t0 = global_ns();
-        while (true) {
-            __nanosleep(200);
-            if (ld_acquire_sys(flags + p) - e >= 0) break;
-            if (global_ns() - t0 > kWaitNs) {
-                if (status) atomicExch(status, e);
-                break;
+    uint64_t t0 = 0;
+    for (int p = 0; p < world; p++) {
+        if (p == rank) continue;
+        const unsigned long long *src = recv + p * piece_words;
+        uint32_t *dst = out + p * piece_words;
+        for (int64_t w = threadIdx.x; w < piece_words; w += kWaitThreads) {
+            uint2 v = ld_word(src + w);
+            while ((int)(v.y - (unsigned)e) < 0 && !s_dead) {
+                if (t0 == 0) t0 = global_ns();
+                __nanosleep(64);
+                v = ld_word(src + w);
+                if (global_ns() - t0 > kWaitNs) {
+                    s_dead = 1;
+                    if (status) atomicExch(status, e);
+                }
             }
+            dst[w] = v.x;
         }
     }
     __syncthreads();
@@ -73,16 +93,22 @@ using namespace fc;
 
 static_assert(sizeof(cudaIpcMemHandle_t) <= FC_IPC_HANDLE_BYTES, "IPC handle size");
 
-extern "C" int fc_peers_wait(const int *flags, int world, int epoch, int *counter, int *status,
-                             void *stream) {
+extern "C" int fc_peers_wait(const void *recv, void *out, int world, int rank, int64_t piece_words,
+                             int epoch, int *counter, int *status, void *stream) {
     clear_error();
-    if (!flags || world < 1 || world > FC_MAX_PEERS || (epoch <= 0 && !counter)) {
-        set_error("peers_wait: need flags, 1 <= world <= %d and an epoch > 0 or a counter",
-                  FC_MAX_PEERS);
+    if (!recv || !out || world < 1 || world > FC_MAX_PEERS || rank < 0 || rank >= world ||
+        piece_words < 0 || (epoch <= 0 && !counter)) {
+        set_error("peers_wait: need recv and out, 1 <= world <= %d, 0 <= rank < world, "
+                  "piece_words >= 0 and an epoch > 0 or a counter", FC_MAX_PEERS);
         return FC_EINVAL;
     }
-    peers_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, world, epoch, counter,
-                                                                        status);
+    if (!aligned(recv, 8) || !aligned(out, 4)) {
+        set_error("peers_wait: recv must be 8-byte and out 4-byte aligned");
+        return FC_EINVAL;
+    }
+    peers_wait_kernel<<<1, kWaitThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const unsigned long long *>(recv), static_cast<uint32_t *>(out), world, rank,
+        piece_words, epoch, counter, status);
     return check_launch("peers_wait");
 }
 

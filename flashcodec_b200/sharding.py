@@ -109,22 +109,23 @@ def gather_outputs(plan: ShardPlan, out_local: torch.Tensor, group=None) -> torc
 
 
 class PeerOutputs:
-    """Output buffers of a split-KV-head decode step that every rank stores
-    into directly: the kernel-fused replacement for gather_outputs'
-    all-gather (fc_decode_attn_peers, csrc/fc_attention_tc.cu).
+    """Output buffers of a split-KV-head decode step that the attention kernel
+    fills on every rank directly: the kernel-fused replacement for
+    gather_outputs' all-gather (fc_decode_attn_peers, csrc/fc_attention_tc.cu).
 
     Each rank holds `slots` full (B, Hq, 1, D) outputs (one per layer, so a
-    layer's buffer is never overwritten while it may still be read) and a flag
-    array; CUDA IPC handles are exchanged once over the process group.  A call
-    of decode() runs this rank's KV heads, stores every output row into all
-    ranks' slot buffers over NVLink, publishes a new epoch, and queues a
-    bounded wait for every rank's epoch on the current stream, after which the
-    slot holds the full output.  Every rank calls decode() for the same slots
-    in the same order.  Epochs come from a device counter that each wait
-    advances, so decode() calls captured in a CUDA graph publish a new epoch
-    on every replay.  A wait that gives up records its epoch in the stream's
-    attention workspace status word (attention_status).  close() unmaps the
-    peers' buffers (collective)."""
+    layer's buffer is never overwritten while it may still be read) and, per
+    slot, a receive area of one piece per rank; CUDA IPC handles of the receive
+    areas are exchanged once over the process group.  A call of decode() runs
+    this rank's KV heads, stores its piece into its own slot and sends it over
+    NVLink into every other rank's receive area as self-validating {4 bytes,
+    epoch} words, then queues a bounded wait that unpacks the other ranks'
+    pieces into the slot; after it the slot holds the full output.  Every
+    rank calls decode() for the same slots in the same order.  Epochs come
+    from a device counter that each wait advances, so decode() calls captured
+    in a CUDA graph use a new epoch on every replay.  A wait that gives up
+    records its epoch in the stream's attention workspace status word
+    (attention_status).  close() unmaps the peers' areas (collective)."""
 
     def __init__(self, plan: ShardPlan, rank: int, slots: int, D: int, dtype: torch.dtype,
                  device, group=None):
@@ -138,32 +139,28 @@ class PeerOutputs:
         self.plan, self.rank, self.world, self.group = plan, rank, plan.world, group
         self.device = torch.device(device)
         self.bufs = torch.zeros((slots, plan.B, plan.Hq, 1, D), dtype=dtype, device=self.device)
-        self.flags = torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=self.device)
+        hq_local = plan.q_head_range(rank)[1] - plan.q_head_range(rank)[0]
+        piece_bytes = hq_local * D * self.bufs.element_size()   # one batch row per rank
+        if piece_bytes % 4:
+            raise ValueError("a rank's output piece must be a multiple of 4 bytes")
+        self.piece_words = piece_bytes // 4
+        self.recv = torch.zeros((slots, self.world, self.piece_words), dtype=torch.int64,
+                                device=self.device)
         self.counter = torch.zeros(1, dtype=torch.int32, device=self.device)
         torch.cuda.synchronize(self.device)
-        mine = (K.ipc_get_handle(self.bufs), K.ipc_get_handle(self.flags))
         infos = [None] * self.world
-        dist.all_gather_object(infos, mine, group=group)
+        dist.all_gather_object(infos, K.ipc_get_handle(self.recv), group=group)
         self._opened: dict = {}          # handle -> mapped base
-        es = self.bufs.element_size()
-        b0 = plan.batch_range(rank)[0]
-        h0 = plan.q_head_range(rank)[0]
-        piece = (b0 * plan.Hq + h0) * D * es   # this rank's rows inside a slot
-        slot_bytes = plan.B * plan.Hq * D * es
-        out_base, flag_base = [], []
-        for p, ((hb, ob), (hf, of)) in enumerate(infos):
-            if p == rank:
-                out_base.append(self.bufs.data_ptr())
-                flag_base.append(self.flags.data_ptr())
-            else:
-                out_base.append(self._open(hb) + ob)
-                flag_base.append(self._open(hf) + of)
+        bases = [self.recv.data_ptr() if p == rank else self._open(h) + off
+                 for p, (h, off) in enumerate(infos)]
+        # ranks own consecutive pieces of a slot (batch row, then KV-head group)
+        slot_bytes = plan.B * plan.Hq * D * self.bufs.element_size()
         self._tables = []
         for s in range(slots):
             t = _lib.PeerOut()
+            t.out = self.bufs.data_ptr() + s * slot_bytes + rank * piece_bytes
             for p in range(self.world):
-                t.out[p] = out_base[p] + s * slot_bytes + piece
-                t.flags[p] = flag_base[p]
+                t.recv[p] = bases[p] + ((s * self.world + rank) * self.piece_words) * 8
             t.world, t.rank = self.world, rank
             t.counter = self.counter.data_ptr()
             self._tables.append(t)
@@ -196,12 +193,13 @@ class PeerOutputs:
         K.decode_attn_peers(query, krows, vrows, kscales, vscales, ks.raw, vs.raw, A, scale,
                             full.dtype, full.stride(0), full.stride(1), self._tables[slot])
         ws = K.workspace(query.device, 0)
-        K.peers_wait(self.flags, self.world, 0, ws, counter=self.counter)
+        K.peers_wait(self.recv[slot], full, self.world, self.rank, self.piece_words, 0, ws,
+                     counter=self.counter)
         return full
 
     def close(self) -> None:
-        """Unmap the other ranks' buffers once every rank has finished with
-        them (collective: every rank calls it)."""
+        """Unmap the other ranks' receive areas once every rank has finished
+        with them (collective: every rank calls it)."""
         import torch.distributed as dist
         from . import _kernels as K
         torch.cuda.synchronize(self.device)

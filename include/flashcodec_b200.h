@@ -453,43 +453,44 @@ FC_API int fc_selftest_noalloc_wait(int epoch, void *stream);
  *
  * When a batch row's KV heads are split over ranks (one process per GPU), every
  * rank needs the full (B, Hq, D) output.  Instead of a collective after the
- * kernel, fc_decode_attn_peers stores each output row into every rank's output
- * buffer over NVLink (plain peer stores; no multicast), and the CTA that stores
- * the launch's last rows publishes `epoch` in slot `rank` of every rank's flag
- * array (a system-scope release).  fc_peers_wait, queued on the consumer's
- * stream, returns once every rank's epoch has arrived.  Buffers of other ranks
- * are opened with fc_ipc_open_handle from the handles fc_ipc_get_handle gives.
- * The reference runs on one device; the collective this replaces is the one
- * all-gather of (B, Hq_local, D) outputs per layer a head-split step needs. */
+ * kernel, fc_decode_attn_peers stores this rank's output rows into its own
+ * buffer and, as self-validating 8-byte words {4 bytes of output, epoch}, into
+ * a receive area of every other rank over NVLink (plain peer stores, no
+ * multicast, no fences: a word is valid once its epoch half matches).
+ * fc_peers_wait, queued on the consumer's stream, waits for every word of the
+ * other ranks' pieces and unpacks them into the local output.  Receive areas
+ * of other ranks are opened with fc_ipc_open_handle from the handles
+ * fc_ipc_get_handle gives.  The reference runs on one device; this replaces
+ * the one all-gather of (B, Hq_local, D) outputs per layer a head-split step
+ * needs. */
 #define FC_MAX_PEERS 8
 #define FC_IPC_HANDLE_BYTES 64
 
 typedef struct fc_peer_out {
-    void *out[FC_MAX_PEERS];   /* rank p's output buffer, pre-offset to this rank's piece:
-                                  the element (b, h, d) of this call lands at
-                                  out[p] + b * o_sb + h * o_sh + d, as `out` of
-                                  fc_decode_attn; out[rank] is this rank's own buffer */
-    int *flags[FC_MAX_PEERS];  /* rank p's flag array (FC_MAX_PEERS ints, zeroed once) */
+    void *out;                 /* this rank's piece of its own output: element (b, h, d)
+                                  of the call at out + (b * o_sb + h * o_sh + d) elements */
+    void *recv[FC_MAX_PEERS];  /* rank p's receive area for this rank's piece, 8-byte
+                                  aligned: word w holds bytes 4w .. 4w+3 of the piece laid
+                                  out contiguously as (B, Hq, D) of the call, and the epoch;
+                                  recv[rank] is unused */
     int world;                 /* ranks, 1 .. FC_MAX_PEERS */
     int rank;                  /* this rank, 0 .. world - 1 */
-    int epoch;                 /* > 0, larger than every earlier epoch on these flags;
-                                  ignored when `counter` is set */
+    int epoch;                 /* > 0, larger than every earlier epoch of these receive
+                                  areas; ignored when `counter` is set */
     int *counter;              /* optional device int of this rank (zeroed once): the launch
-                                  publishes *counter + 1, read on the device, and the
+                                  uses *counter + 1, read on the device, and the
                                   fc_peers_wait given the same counter advances it -- so a
-                                  captured CUDA graph of the calls publishes a new epoch on
-                                  every replay */
+                                  captured CUDA graph of the calls uses a new epoch on every
+                                  replay */
 } fc_peer_out;
 
-/* fc_decode_attn with the outputs placed as above (`out` of fc_decode_attn is
- * peers->out[peers->rank]).  The tensor-core kernel's layouts only; others
- * return FC_ENOTSUP.  The workspace's header holds the launch's completion
- * counter, so calls on one workspace are ordered by its stream as usual.
+/* fc_decode_attn with the outputs placed as above.  The tensor-core kernel's
+ * layouts only (others return FC_ENOTSUP); D * element size must be a
+ * multiple of 4 bytes.  Receive areas must be zeroed once before first use.
  * A rank's buffers must not be read by their owner while another rank's call
  * may still store into them: give each layer (or each step in flight) its
- * own output buffer.  If any CTA's bounded wait gives up, the launch stores
- * no output and publishes nothing; the peers' fc_peers_wait then gives up
- * too and records its epoch. */
+ * own slot.  If any CTA's bounded wait gives up, the launch stores no output
+ * and the peers' fc_peers_wait gives up too and records its epoch. */
 FC_API int fc_decode_attn_peers(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
                                 int64_t q_sb, int64_t q_sh,
                                 int64_t Hk, int64_t n_blocks, int s, int r, int rows_dtype,
@@ -508,18 +509,20 @@ FC_API int fc_decode_attn_peers(const void *q, int q_dtype, int64_t B, int64_t H
                                 const fc_peer_out *peers,
                                 void *workspace, size_t workspace_bytes, void *stream);
 
-/* Wait, on `stream`, until flags[p] has reached the epoch for every
- * p < world (the local flag array of fc_peer_out).  The epoch is `epoch`, or,
- * when `counter` (the fc_peer_out counter) is non-NULL, *counter + 1 read on
- * the device, and the kernel stores it back into *counter before it returns.
- * One small kernel: each of `world` threads polls one flag with system-scope
- * acquire loads, sleeping between polls, and gives up after 100 ms of
- * %globaltimer time, recording the epoch in the device int *status (for
- * instance the workspace status word) and returning; kernels queued after it
- * see every output stored before the flags it observed.  No counterpart in
- * the reference. */
-FC_API int fc_peers_wait(const int *flags, int world, int epoch, int *counter, int *status,
-                         void *stream);
+/* Wait, on `stream`, for the other ranks' pieces of one slot and unpack them:
+ * `recv` is this rank's receive area of the slot (world pieces of
+ * piece_words 8-byte words, rank p's piece at word p * piece_words), `out`
+ * the slot's full output, which holds rank p's piece at byte
+ * 4 * p * piece_words (ranks own consecutive pieces of the output, as the
+ * split of KV heads orders them).  The epoch is `epoch`, or, when `counter`
+ * is non-NULL, *counter + 1 read on the device, stored back into *counter
+ * before the kernel returns.  One CTA polls the words with volatile loads,
+ * sleeping between polls, and gives up after 100 ms of %globaltimer time,
+ * recording the epoch in the device int *status (for instance the workspace
+ * status word) and returning; kernels queued after it read the full output.
+ * No counterpart in the reference. */
+FC_API int fc_peers_wait(const void *recv, void *out, int world, int rank, int64_t piece_words,
+                         int epoch, int *counter, int *status, void *stream);
 
 /* CUDA IPC for the peer buffers (no counterpart in the reference).
  * fc_ipc_get_handle: the FC_IPC_HANDLE_BYTES handle of the allocation that

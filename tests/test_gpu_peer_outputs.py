@@ -1,6 +1,7 @@
-"""Split KV heads without a collective: fc_decode_attn_peers stores every
-output row into each rank's buffer and publishes an epoch flag, fc_peers_wait
-waits (bounded) for every rank's epoch.
+"""Split KV heads without a collective: fc_decode_attn_peers stores this
+rank's output piece into its own buffer and sends it to every other rank's
+receive area as {4 bytes, epoch} words; fc_peers_wait waits (bounded) for the
+other ranks' words and unpacks them into the output.
 
 On one GPU two ranks are emulated in one process: both ranks' launches run
 (in stream order) before either wait is queued, so every wait finds its flags
@@ -47,91 +48,93 @@ def _peer_call(q, ks, vs, table, o_sb, o_sh):
                         q.shape[-1] ** -0.5, q.dtype, o_sb, o_sh, table)
 
 
+def _emulated_ranks(k, v, q, world, dev, quant=8, counters=None):
+    """Per emulated rank: its full output buffer, its receive area, and the
+    (query, K stream, V stream, fc_peer_out) of its call."""
+    from flashcodec_b200 import _lib
+    B, Hq, _, D = q.shape
+    Hk = k.shape[1]
+    G = Hq // Hk
+    bufs = [torch.zeros(B, Hq, 1, D, dtype=torch.bfloat16, device=dev) for _ in range(world)]
+    piece_bytes = Hq // world * D * bufs[0].element_size()
+    words = piece_bytes // 4
+    recv = [torch.zeros(world, words, dtype=torch.int64, device=dev) for _ in range(world)]
+    calls = []
+    for rank in range(world):
+        h0, h1 = rank * Hk // world, (rank + 1) * Hk // world
+        lks, lvs = _streams(k[:, h0:h1], v[:, h0:h1], dev, quant)
+        t = _lib.PeerOut()
+        t.out = bufs[rank].data_ptr() + rank * piece_bytes
+        for p in range(world):
+            t.recv[p] = recv[p].data_ptr() + rank * words * 8
+        t.world, t.rank = world, rank
+        if counters is not None:
+            t.counter = counters[rank].data_ptr()
+        calls.append((q[:, h0 * G:h1 * G].to(dev).contiguous(), lks, lvs, t))
+    return bufs, recv, words, calls
+
+
 @pytest.mark.parametrize("S,quant", [(8 * 3000 + 5, 8), (8 * 40 + 3, 8), (8 * 500 + 1, 0)])
 def test_two_ranks_emulated_on_one_gpu(S, quant):
-    """Ranks 0 and 1 each hold 4 of 8 KV heads of one sequence.  After both
-    peer launches and both waits, each rank's buffer holds the full output,
-    the two buffers are bit-identical, each rank's piece equals the plain
-    kernel on its heads bit for bit, and the whole matches the 1-GPU call
-    within the attention bar."""
+    """Ranks 0 and 1 each hold 4 of 8 KV heads of one sequence (one split per
+    unit, and many).  After both peer launches and both waits, each rank's
+    buffer holds the full output, the two buffers are bit-identical, each
+    rank's piece equals the plain kernel on its heads bit for bit, and the
+    whole matches the 1-GPU call within the attention bar -- on two calls in a
+    row with explicit epochs."""
     import flashcodec_b200 as fc
     from flashcodec_b200 import _kernels as K
-    from flashcodec_b200 import _lib
     dev = torch.device(DEV, 0)
-    B, Hq, Hk, D = 1, 32, 8, 128
+    B, Hq, Hk, D, world = 1, 32, 8, 128, 2
     k, v, q = bench.synth_case(B, Hq, Hk, S, D, 0.95, 41, dtype=torch.bfloat16)
     ks, vs = _streams(k, v, dev, quant)
     ref = fc.codec_decode_attention(q.to(dev), ks, vs)
-    world, G = 2, Hq // Hk
-    bufs = [torch.zeros(B, Hq, 1, D, dtype=torch.bfloat16, device=dev) for _ in range(world)]
-    flags = [torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=dev) for _ in range(world)]
-    es = bufs[0].element_size()
+    bufs, recv, words, calls = _emulated_ranks(k, v, q, world, dev, quant)
     local = []
-    for epoch in (1, 2):                       # two calls in a row on the same flags
+    for epoch in (1, 2):
         for b in bufs:
             b.zero_()
         pieces = []
-        for rank in range(world):
-            h0, h1 = rank * Hk // world, (rank + 1) * Hk // world
-            lks, lvs = _streams(k[:, h0:h1], v[:, h0:h1], dev, quant)
-            ql = q[:, h0 * G:h1 * G].to(dev).contiguous()
-            t = _lib.PeerOut()
-            for p in range(world):
-                t.out[p] = bufs[p].data_ptr() + h0 * G * D * es
-                t.flags[p] = flags[p].data_ptr()
-            t.world, t.rank, t.epoch = world, rank, epoch
+        for ql, lks, lvs, t in calls:
+            t.epoch = epoch
             _peer_call(ql, lks, lvs, t, bufs[0].stride(0), bufs[0].stride(1))
             pieces.append(fc.codec_decode_attention(ql, lks, lvs))
         status = torch.zeros(1, dtype=torch.int32, device=dev)
         for rank in range(world):
-            K.peers_wait(flags[rank], world, epoch, status)
+            K.peers_wait(recv[rank], bufs[rank], world, rank, words, epoch, status)
         torch.cuda.synchronize()
         assert status.item() == 0
         assert torch.equal(bufs[0], bufs[1])
         for rank in range(world):
-            h0 = rank * Hk // world * G
+            h0 = rank * Hq // world
             assert torch.equal(bufs[0][:, h0:h0 + pieces[rank].shape[1]], pieces[rank])
         r = ref.float().cpu()
         err = (bufs[0].float().cpu() - r).abs()
         assert bool((err <= 2e-3 + 2.0 ** -8 * r.abs()).all()), float(err.max())
-        assert flags[0][:world].tolist() == [epoch] * world
+        assert int(recv[0][1, 0].item()) >> 32 == epoch
         local.append(bufs[0].clone())
     assert torch.equal(local[0], local[1])
 
 
 def test_two_ranks_emulated_replay_in_a_cuda_graph():
     """Device-counter epochs: both ranks' peer launches and both waits are
-    captured once in a CUDA graph and replayed three times; every replay
-    publishes a new epoch (flags and counters end at 4 after the eager call
-    and three replays), no wait gives up, and both buffers hold the output of
-    the eager call."""
+    captured once in a CUDA graph and replayed three times; every replay uses
+    a new epoch (the counters end at 4 after the eager call and three
+    replays), no wait gives up, and both buffers hold the eager output."""
     from flashcodec_b200 import _kernels as K
-    from flashcodec_b200 import _lib
     dev = torch.device(DEV, 0)
     B, Hq, Hk, D, world = 1, 32, 8, 128, 2
-    G = Hq // Hk
     k, v, q = bench.synth_case(B, Hq, Hk, 8 * 700 + 2, D, 0.95, 43, dtype=torch.bfloat16)
-    bufs = [torch.zeros(B, Hq, 1, D, dtype=torch.bfloat16, device=dev) for _ in range(world)]
-    flags = [torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=dev) for _ in range(world)]
     ctrs = [torch.zeros(1, dtype=torch.int32, device=dev) for _ in range(world)]
+    bufs, recv, words, calls = _emulated_ranks(k, v, q, world, dev, counters=ctrs)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    es = bufs[0].element_size()
-    ranks = []
-    for rank in range(world):
-        h0, h1 = rank * Hk // world, (rank + 1) * Hk // world
-        lks, lvs = _streams(k[:, h0:h1], v[:, h0:h1], dev)
-        t = _lib.PeerOut()
-        for p in range(world):
-            t.out[p] = bufs[p].data_ptr() + h0 * G * D * es
-            t.flags[p] = flags[p].data_ptr()
-        t.world, t.rank, t.epoch, t.counter = world, rank, 0, ctrs[rank].data_ptr()
-        ranks.append((q[:, h0 * G:h1 * G].to(dev).contiguous(), lks, lvs, t))
 
     def step():
-        for ql, lks, lvs, t in ranks:
+        for ql, lks, lvs, t in calls:
             _peer_call(ql, lks, lvs, t, bufs[0].stride(0), bufs[0].stride(1))
         for rank in range(world):
-            K.peers_wait(flags[rank], world, 0, status, counter=ctrs[rank])
+            K.peers_wait(recv[rank], bufs[rank], world, rank, words, 0, status,
+                         counter=ctrs[rank])
 
     step()                     # eager: the kernels' one-time set-up happens here
     torch.cuda.synchronize()
@@ -148,47 +151,51 @@ def test_two_ranks_emulated_replay_in_a_cuda_graph():
     assert torch.equal(bufs[0], eager) and torch.equal(bufs[1], eager)
     # the eager call and three replays (capturing runs nothing)
     assert [c.item() for c in ctrs] == [4, 4]
-    assert flags[0][:world].tolist() == [4, 4] and flags[1][:world].tolist() == [4, 4]
+    assert int(recv[0][1, -1].item()) >> 32 == 4 and int(recv[1][0, -1].item()) >> 32 == 4
 
 
 def test_peer_outputs_refuse_cuda_core_layouts():
     """Peer outputs need the tensor-core kernel: head dim 64 is refused
-    loudly, before anything is stored or published."""
+    loudly, before anything is stored or sent."""
     from flashcodec_b200 import _lib
     dev = torch.device(DEV, 0)
     k, v, q = bench.synth_case(1, 8, 2, 8 * 20, 64, 0.95, 3, dtype=torch.bfloat16)
     ks, vs = _streams(k, v, dev)
     out = torch.zeros(1, 8, 1, 64, dtype=torch.bfloat16, device=dev)
-    flags = torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=dev)
+    recv = torch.zeros(2, 8 * 64 // 4, dtype=torch.int64, device=dev)
     t = _lib.PeerOut()
-    t.out[0], t.flags[0], t.world, t.rank, t.epoch = out.data_ptr(), flags.data_ptr(), 1, 0, 1
+    t.out, t.world, t.rank, t.epoch = out.data_ptr(), 2, 0, 1
+    t.recv[1] = recv.data_ptr()
     with pytest.raises(NotImplementedError):
         _peer_call(q.to(dev), ks, vs, t, out.stride(0), out.stride(1))
     torch.cuda.synchronize()
-    assert flags.abs().sum().item() == 0
+    assert recv.abs().sum().item() == 0 and out.abs().sum().item() == 0
 
 
-def test_peers_wait_gives_up_on_a_flag_nobody_sets():
-    """Failure detection without a GPU fault: waiting for an epoch no rank
-    publishes gives up after the 100 ms limit, records the epoch in the
-    status word, and the context stays usable."""
+def test_peers_wait_gives_up_on_a_piece_nobody_sends():
+    """Failure detection without a GPU fault: waiting for a piece no rank
+    sends gives up after the 100 ms limit, records the epoch in the status
+    word, and the context stays usable; once the words carry the epoch the
+    wait unpacks them into the output."""
     from flashcodec_b200 import _kernels as K
-    from flashcodec_b200 import _lib
-    flags = torch.zeros(_lib.FC_MAX_PEERS, dtype=torch.int32, device=DEV)
-    flags[0] = 7
+    words = 64
+    recv = torch.zeros(2, words, dtype=torch.int64, device=DEV)
+    out = torch.zeros(2 * words, dtype=torch.int32, device=DEV)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    K.peers_wait(flags, 2, 7, status)        # rank 1's flag never arrives
+    K.peers_wait(recv, out, 2, 0, words, 7, status)     # rank 1 never sends
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
     assert status.item() == 7
     assert 0.09 <= dt < 5.0, dt
-    flags[1] = 7
+    payload = torch.arange(1000, 1000 + words, dtype=torch.int64, device=DEV)
+    recv[1] = (7 << 32) | payload
     status.zero_()
-    K.peers_wait(flags, 2, 7, status)
+    K.peers_wait(recv, out, 2, 0, words, 7, status)
     torch.cuda.synchronize()
     assert status.item() == 0
+    assert torch.equal(out[words:].long(), payload) and out[:words].abs().sum().item() == 0
 
 
 def _worker(rank, world, port, q, k, v, ref, qo):
