@@ -197,3 +197,52 @@ def test_masked_attention_validates_on_the_host(lib):
     assert b"visibility" in lib.fc_last_error_string()
     assert call(kanc=d) == _lib.FC_EINVAL
     assert call() == _lib.FC_ERANGE          # valid so far; no workspace given
+
+
+def test_peer_entry_points_validate_on_the_host(lib):
+    """fc_decode_attn_peers, fc_peers_wait and the IPC calls refuse bad
+    tables and pointers before any launch; a valid table on a layout the
+    tensor-core kernel does not take (head dim 64) is refused as unsupported."""
+    from flashcodec_b200 import _lib
+    P = ctypes.c_void_p
+    d = P(0x1000)
+
+    def table(world=2, rank=0, epoch=1, out=0x7000, recv1=0x8000, counter=None):
+        t = _lib.PeerOut()
+        t.out, t.world, t.rank, t.epoch = out, world, rank, epoch
+        t.recv[1] = recv1
+        t.counter = counter
+        return t
+
+    def attn(t, D=64):
+        return lib.fc_decode_attn_peers(
+            d, _lib.FC_F32, 1, 4, D, 4 * D, D, 2, 4, 2, 8, _lib.FC_I8,
+            d, 0, 0, 0, 0, d, 0, 0, 0, 0, d, 0, 0, 0, d, 0, 0, 0, _lib.FC_F32,
+            None, 0, 0, 0, None, 0, 0, 0, _lib.FC_F32, 0,
+            d, 0.125, _lib.FC_F32, 4 * D, D, None if t is None else ctypes.byref(t),
+            None, 0, None)
+
+    assert attn(None) == _lib.FC_EINVAL
+    assert attn(table(world=0)) == _lib.FC_EINVAL
+    assert attn(table(world=9)) == _lib.FC_EINVAL
+    assert attn(table(rank=2)) == _lib.FC_EINVAL
+    assert attn(table(epoch=0)) == _lib.FC_EINVAL               # no epoch and no counter
+    assert attn(table(out=0)) == _lib.FC_EINVAL
+    assert attn(table(recv1=0)) == _lib.FC_EINVAL
+    assert attn(table(recv1=0x8004)) == _lib.FC_EINVAL          # receive words are 8 bytes
+    assert attn(table(epoch=0, counter=0x9000)) == _lib.FC_ENOTSUP   # valid, head dim 64
+    assert b"tensor-core" in lib.fc_last_error_string()
+    assert attn(table()) == _lib.FC_ENOTSUP
+
+    w = lib.fc_peers_wait
+    assert w(None, d, 2, 0, 16, 1, None, None, None) == _lib.FC_EINVAL
+    assert w(d, None, 2, 0, 16, 1, None, None, None) == _lib.FC_EINVAL
+    assert w(d, d, 9, 0, 16, 1, None, None, None) == _lib.FC_EINVAL
+    assert w(d, d, 2, 2, 16, 1, None, None, None) == _lib.FC_EINVAL
+    assert w(d, d, 2, 0, 16, 0, None, None, None) == _lib.FC_EINVAL
+    assert w(P(0x1004), d, 2, 0, 16, 1, None, None, None) == _lib.FC_EINVAL
+    h = ctypes.create_string_buffer(_lib.FC_IPC_HANDLE_BYTES)
+    off = ctypes.c_int64(0)
+    assert lib.fc_ipc_get_handle(None, h, ctypes.byref(off)) == _lib.FC_EINVAL
+    assert lib.fc_ipc_open_handle(None, ctypes.byref(P())) == _lib.FC_EINVAL
+    assert lib.fc_ipc_close_handle(None) == _lib.FC_EINVAL
