@@ -302,16 +302,24 @@ jpeg_encode_d128_kernel(EncArgs a) {
         advance(cb, ch, cblk);
         // coefficients of every kept frequency: sequential fp32 FMA chain
         // over the R samples, rounded to the input dtype (jpeg.py:66-67)
+        // (channel pairs in paired fp32 FMAs: each half is the same fma.rn)
         float c[KM][4];
 #pragma unroll
         for (int j = 0; j < KM; j++) {
 #pragma unroll
             for (int v = 0; v < 4; v++) c[j][v] = 0.0f;
             if (j >= kk) continue;
+            float2 c01 = make_float2(0.0f, 0.0f), c23 = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int i = 0; i < R; i++)
-#pragma unroll
-                for (int v = 0; v < 4; v++) c[j][v] = __fmaf_rn(xv[i][v], mb[j][i], c[j][v]);
+            for (int i = 0; i < R; i++) {
+                const float2 m2 = make_float2(mb[j][i], mb[j][i]);
+                c01 = __ffma2_rn(make_float2(xv[i][0], xv[i][1]), m2, c01);
+                c23 = __ffma2_rn(make_float2(xv[i][2], xv[i][3]), m2, c23);
+            }
+            c[j][0] = c01.x;
+            c[j][1] = c01.y;
+            c[j][2] = c23.x;
+            c[j][3] = c23.y;
             round_pair<T>(c[j][0], c[j][1]);
             round_pair<T>(c[j][2], c[j][3]);
         }
