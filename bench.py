@@ -135,13 +135,18 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic(per_launch):
+def ncu_traffic(per_launch, codec="jpeg-int8"):
     """Per-launch DRAM bytes (read + write) of the attention kernel at this
-    workload, from the committed one-kernel ncu capture of a small case
-    (profiles/attn_decode_cfg2.json): its measured bytes per algorithmic byte
-    times this launch's algorithmic bytes (the kernel streams each archive
-    byte once, so traffic grows in proportion), or None."""
-    p = ROOT / "profiles" / "attn_decode_cfg2.json"
+    workload, from the committed one-kernel ncu capture of a small case of
+    the same codec (profiles/attn_decode_cfg2.json, int8 codes;
+    profiles/attn_decode_cfg2_fp.json, bf16 coefficients): its measured bytes
+    per algorithmic byte times this launch's algorithmic bytes (the kernel
+    streams each archive byte once, so traffic grows in proportion), or
+    None."""
+    name = {"jpeg-int8": "attn_decode_cfg2.json", "jpeg-fp": "attn_decode_cfg2_fp.json"}.get(codec)
+    if name is None:
+        return None
+    p = ROOT / "profiles" / name
     if not p.exists():
         return None
     try:
@@ -1012,8 +1017,8 @@ def main():
     if rank == 0:
         peak, kind = measured_peaks()
         achieved = per_launch / (kern_max * 1e-3) / 1e9
-        traffic = (ncu_traffic(per_launch) if cfg["config"] == 2 and plan is None
-                   and cfg["B"] == CFG2["B"] and cfg["codec"] == "jpeg-int8" else None)
+        traffic = (ncu_traffic(per_launch, cfg["codec"]) if cfg["config"] == 2 and plan is None
+                   and cfg["B"] == CFG2["B"] else None)
         tokens = Bg if plan is not None else world * cfg["B"]
         line = {
             "metric": METRIC if cfg["codec"] == "jpeg-int8" else
