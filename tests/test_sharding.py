@@ -75,3 +75,24 @@ def test_gloo_world2_gather_matches_single_device(B):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert all(err == 0.0 for _, err in res), res
+
+
+@pytest.mark.parametrize("B,Hk,Hq,world", [(1, 8, 32, 2), (1, 8, 32, 8), (2, 8, 32, 8),
+                                           (4, 8, 32, 8), (1, 4, 28, 4), (3, 2, 16, 6)])
+def test_head_split_pieces_are_rank_ordered(B, Hk, Hq, world):
+    """The peer exchange (PeerOutputs, fc_peers_wait) places rank p's piece
+    at p * piece in the (B, Hq) output: in every KV-head plan the ranks' query
+    head ranges, batch row first, tile the output in rank order with equal
+    pieces."""
+    from flashcodec_b200.sharding import plan_shards
+    plan = plan_shards(B, Hk, Hq, world)
+    assert plan.mode == "heads"
+    piece = None
+    for r in range(world):
+        b0, b1 = plan.batch_range(r)
+        h0, h1 = plan.q_head_range(r)
+        assert b1 - b0 == 1
+        piece = piece or (h1 - h0)
+        assert h1 - h0 == piece
+        assert b0 * Hq + h0 == r * piece
+    assert world * piece == B * Hq
