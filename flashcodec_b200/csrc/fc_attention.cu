@@ -37,7 +37,7 @@ namespace fc {
 
 void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk);
 bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled);
-int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, bool bf,
+int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, int rows_dtype,
                    cudaStream_t st);
 
 namespace {
@@ -1048,7 +1048,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
                 t.pepoch = peers->epoch;
                 t.pctr = peers->counter;
             }
-            return launch_attn_tc(t, B, k_rows, v_rows, rows_dtype == FC_BF16,
+            return launch_attn_tc(t, B, k_rows, v_rows, rows_dtype,
                                   static_cast<cudaStream_t>(stream));
         }
         if (sel == FC_ATTN_TENSOR_CORE || peers) {

@@ -101,9 +101,10 @@ __host__ __device__ constexpr uint32_t i8_idesc(int n, int a_mn_major) {
            ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
-// Instruction descriptor: bf16 x bf16 -> fp32, M = 128, N, A K- or MN-major.
-__host__ __device__ constexpr uint32_t bf16_idesc(int n, int a_mn_major) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) |
+// Instruction descriptor: bf16 x bf16 (or fp16 x fp16 when f16) -> fp32,
+// M = 128, N, A K- or MN-major.
+__host__ __device__ constexpr uint32_t bf16_idesc(int n, int a_mn_major, bool f16 = false) {
+    return (1u << 4) | (f16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)a_mn_major << 15) |
            ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
 }
 
@@ -163,14 +164,23 @@ __device__ __forceinline__ int sw128_off_bf(int row, int c, int rows) {
     return (c >> 6) * rows * 128 + sw128_off(row, (c & 63) * 2);
 }
 
-// x -> three bf16 limbs h0 + h1 + h2 (each the round-to-nearest of what the
-// previous ones left), which carry x to about 2^-24 of |x|: the tensor core's
-// bf16 products then reproduce fp32 dot products.
-__device__ __forceinline__ void bf_limbs3(float x, __nv_bfloat16 h[3]) {
+// x -> three 16-bit float limbs h0 + h1 + h2, as raw bits (bf16, or fp16 when
+// F16), each the round-to-nearest of what the previous ones left: they carry x
+// to about 2^-24 of |x| (bf16; fp16 limbs carry more, while they stay normal),
+// so the tensor core's 16-bit products reproduce fp32 dot products.
+template <bool F16>
+__device__ __forceinline__ void limbs3_16(float x, uint16_t h[3]) {
 #pragma unroll
     for (int i = 0; i < 3; i++) {
-        h[i] = __float2bfloat16_rn(x);
-        x -= __bfloat162float(h[i]);
+        if constexpr (F16) {
+            const __half t = __float2half_rn(x);
+            h[i] = __half_as_ushort(t);
+            x -= __half2float(t);
+        } else {
+            const __nv_bfloat16 t = __float2bfloat16_rn(x);
+            h[i] = __bfloat16_as_ushort(t);
+            x -= __bfloat162float(t);
+        }
     }
 }
 
@@ -240,7 +250,13 @@ __host__ __device__ constexpr int tc_stages() { return (BF && GT == 8) ? 2 : kTc
 template <bool BF, int GT>
 __host__ __device__ constexpr int tc_min_ctas() { return BF ? 2 : (GT <= 4 ? 4 : 3); }
 
-template <int GT, int S, bool BF>
+//
+// F16 (with BF): fp16 coefficient rows through the same kind::f16 MMAs with
+// fp16 limbs.  fp16's exponent range is narrow, so q is scaled per head by a
+// power of two that puts its largest |q| in [2^13, 2^14) (folded back through
+// the logit factor) and the weights by 2^12 (folded back with the output), which
+// keeps the limbs of every value that matters normal.
+template <int GT, int S, bool BF, bool F16 = false>
 __global__ void __launch_bounds__(kTcThreads, tc_min_ctas<BF, GT>())
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                const __grid_constant__ TcArgs a) {
@@ -298,8 +314,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     // rows at or past the archive's n blocks read as zeros
     const int y0 = (int)(n0 * S);
     const int slab = (int)(b * a.Hk + hk);
-    const uint32_t idesc_s = BF ? bf16_idesc(N, 0) : i8_idesc(N, 0);
-    const uint32_t idesc_o = BF ? bf16_idesc(N, 1) : i8_idesc(N, 1);
+    const uint32_t idesc_s = BF ? bf16_idesc(N, 0, F16) : i8_idesc(N, 0);
+    const uint32_t idesc_o = BF ? bf16_idesc(N, 1, F16) : i8_idesc(N, 1);
     constexpr int kAlloc = N * 4 <= 64 ? 64 : 128;  // TMEM columns: 2 score + 2 output buffers
 
     // ---------------------------------------------------------------- setup
@@ -345,27 +361,47 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         asm volatile("griddepcontrol.wait;" ::: "memory");
         const int d = tid;  // head_dim == 128 == epilogue threads
         if constexpr (BF) {
-            // q of the group's heads as three bf16 limbs (K-major B tile), no scale
-            __nv_bfloat16 *bq16 = reinterpret_cast<__nv_bfloat16 *>(bq);
-            const __nv_bfloat16 zero = __float2bfloat16_rn(0.0f);
+            // q of the group's heads as three 16-bit limbs (K-major B tile):
+            // bf16 unscaled; fp16 scaled per head by 2^(13 - floor(log2 max|q|))
+            uint16_t *bq16 = reinterpret_cast<uint16_t *>(bq);
 #pragma unroll
             for (int g = 0; g < GT; g++) {
                 float v = 0.0f;
                 if (g < G) v = load_as_f32(a.q, b * a.q_sb + (hq0 + g) * a.q_sh + d, a.q_dtype);
-                __nv_bfloat16 h[3];
-                bf_limbs3(v, h);
+                qv[g] = v;
+                if constexpr (F16) {
+                    float m = fabsf(v);
+                    for (int off = 16; off > 0; off >>= 1)
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+                    if (lane == 0) red[warp * 8 + g] = m;
+                }
+            }
+            if constexpr (F16) {
+                epi_bar();
+                if (tid < GT) {
+                    const float m = fmaxf(fmaxf(red[tid], red[8 + tid]), fmaxf(red[16 + tid], red[24 + tid]));
+                    const int e = m > 0.0f ? min(max((int)((__float_as_uint(m) >> 23) & 0xff) - 127, -100), 100) : 0;
+                    s_sq[tid] = pow2_biased(127 + e - 13);
+                }
+            } else {
+                if (tid < GT) s_sq[tid] = 1.0f;
+            }
+            epi_bar();
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                uint16_t h[3];
+                // q / s_sq: a power-of-two factor, exact
+                limbs3_16<F16>(F16 ? qv[g] * __frcp_rn(s_sq[g]) : qv[g], h);
 #pragma unroll
                 for (int l = 0; l < 3; l++) bq16[sw128_off_bf(3 * g + l, d, N) / 2] = h[l];
             }
-            if (tid < GT) s_sq[tid] = 1.0f;
-            __nv_bfloat16 *bw16 = reinterpret_cast<__nv_bfloat16 *>(bw);
+            uint16_t *bw16 = reinterpret_cast<uint16_t *>(bw);
 #pragma unroll
             for (int row = 0; row < N; row++) {
-                if (row >= 3 * GT) bq16[sw128_off_bf(row, d, N) / 2] = zero;
-                bw16[sw128_off_bf(row, d, N) / 2] = zero;
-                bw16[(BQ + sw128_off_bf(row, d, N)) / 2] = zero;
+                if (row >= 3 * GT) bq16[sw128_off_bf(row, d, N) / 2] = 0;
+                bw16[sw128_off_bf(row, d, N) / 2] = 0;
+                bw16[(BQ + sw128_off_bf(row, d, N)) / 2] = 0;
             }
-            epi_bar();
         } else {
             // q of the group's heads: per-head scale, int8 limbs (K-major B tile)
 #pragma unroll
@@ -519,9 +555,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             if (lane == 0) mbar_arrive(vfree + (u & 1));
 #pragma unroll
             for (int g = 0; g < GT; g++) {
-                if constexpr (BF)  // tile output in 2^m_u units (AXp = m_u)
+                if constexpr (BF)  // tile output in 2^m_u units (AXp = m_u; fp16 weights x 2^12)
                     acc[g] = fmaf(bits_f(o[3 * g]) + (bits_f(o[3 * g + 1]) + bits_f(o[3 * g + 2])),
-                                  pow2_biased(127 + AXp[g] - Mref[g]), acc[g]);
+                                  pow2_biased(127 + AXp[g] - Mref[g] - (F16 ? 12 : 0)), acc[g]);
                 else
                     acc[g] = fmaf(limb_value(o, g), pow2_biased(AXp[g] - 5 - Mref[g]), acc[g]);
             }
@@ -645,12 +681,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             // weight limbs of this row (column lrow of the B tile)
             unsigned char *bwt = bw + par * BQ;
             if constexpr (BF) {
-                // w relative to the tile max 2^m (an exact power-of-two factor)
-                __nv_bfloat16 *bw16 = reinterpret_cast<__nv_bfloat16 *>(bwt);
+                // w relative to the tile max 2^m (an exact power-of-two factor;
+                // fp16 weights also times 2^12)
+                uint16_t *bw16 = reinterpret_cast<uint16_t *>(bwt);
 #pragma unroll
                 for (int g = 0; g < GT; g++) {
-                    __nv_bfloat16 h[3];
-                    bf_limbs3(w[g] * pow2_biased(127 + mw[g] - m[g]), h);
+                    uint16_t h[3];
+                    limbs3_16<F16>(w[g] * pow2_biased(127 + (F16 ? 12 : 0) + mw[g] - m[g]), h);
 #pragma unroll
                     for (int l = 0; l < 3; l++) bw16[sw128_off_bf(3 * g + l, lrow, N) / 2] = h[l];
                 }
@@ -833,7 +870,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 // Boxes are 128 int8 codes x 128 rows, or 64 bf16 channels x 128 rows (two
 // per tile), with the 128-byte swizzle the MMA descriptors expect.
 bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows, int64_t slabs,
-                     int64_t slab_rows, bool bf) {
+                     int64_t slab_rows, bool bf, bool f16) {
     auto fn = get_encode();
     if (!fn) return false;
     const int64_t rb = bf ? 256 : 128;
@@ -841,7 +878,10 @@ bool encode_rows_map(CUtensorMap *m, const void *base, int64_t rows, int64_t sla
     cuuint64_t strides[2] = {(cuuint64_t)rb, (cuuint64_t)(slab_rows * rb)};
     cuuint32_t box[3] = {(cuuint32_t)(bf ? 64 : 128), (cuuint32_t)kTileRows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    return fn(m, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+    const CUtensorMapDataType ty = !bf ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    return fn(m, ty, 3,
               const_cast<void *>(base), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -862,7 +902,7 @@ bool pdl_enabled() {
 
 // Dynamic shared memory already opted in, per kernel variant (rows x GT x s) and device.
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_smem_opted[32][kMaxDevices];
+std::atomic<int> g_smem_opted[48][kMaxDevices];
 
 // Tiles per split forced by FLASHCODEC_TC_CHUNK_TILES (tuning), 0 when unset.
 int chunk_tiles_override() {
@@ -910,15 +950,17 @@ void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int 
     chunk = (int)std::min<int64_t>(blocks, n);
 }
 
-// int8 codes with one scale per row, or bf16 coefficients without scales
+// int8 codes with one scale per row, or bf16 / fp16 coefficients without scales
 bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled) {
-    const bool rows_ok = (rows_dtype == FC_I8 && scaled) || (rows_dtype == FC_BF16 && !scaled);
+    const bool rows_ok = (rows_dtype == FC_I8 && scaled) ||
+                         ((rows_dtype == FC_BF16 || rows_dtype == FC_F16) && !scaled);
     return D == 128 && rows_ok && r == kR && (s == 1 || s == 2 || s == 4 || s == 8) &&
            G >= 1 && G <= 8 && get_encode() != nullptr;
 }
 
-int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, bool bf,
+int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, int rows_dtype,
                    cudaStream_t st) {
+    const bool bf = rows_dtype != FC_I8, f16 = rows_dtype == FC_F16;
     CUtensorMap mk, mv;
     const int64_t rows = a.n * a.s, slabs = B * a.Hk;
     if (rows >= (int64_t)1 << 31 || slabs >= (int64_t)1 << 31) {
@@ -926,8 +968,8 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, b
                   "kernel's 32-bit tile coordinates", (long long)rows, (long long)slabs);
         return FC_ENOTSUP;
     }
-    if (!encode_rows_map(&mk, krows, rows, slabs, a.k_cap * a.s, bf) ||
-        !encode_rows_map(&mv, vrows, rows, slabs, a.v_cap * a.s, bf)) {
+    if (!encode_rows_map(&mk, krows, rows, slabs, a.k_cap * a.s, bf, f16) ||
+        !encode_rows_map(&mv, vrows, rows, slabs, a.v_cap * a.s, bf, f16)) {
         set_error("decode_attn: tensor map encoding failed");
         return FC_ECUDA;
     }
@@ -973,6 +1015,15 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, b
     };
     auto by_s = [&](auto gt, int gi) {
         constexpr int GT = decltype(gt)::value;
+        if (f16) {
+            switch (a.s) {
+                case 1: go(attn_tc_kernel<GT, 1, true, true>, 32 + gi * 4 + 0); break;
+                case 2: go(attn_tc_kernel<GT, 2, true, true>, 32 + gi * 4 + 1); break;
+                case 4: go(attn_tc_kernel<GT, 4, true, true>, 32 + gi * 4 + 2); break;
+                default: go(attn_tc_kernel<GT, 8, true, true>, 32 + gi * 4 + 3); break;
+            }
+            return;
+        }
         if (bf) {
             switch (a.s) {
                 case 1: go(attn_tc_kernel<GT, 1, true>, 16 + gi * 4 + 0); break;

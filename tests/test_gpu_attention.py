@@ -219,6 +219,7 @@ def test_tensor_core_and_cuda_core_kernels_vs_oracle(kernel_choice, G, K, dt, S,
     assert Kn.attn_status(q.to(DEV).device) == 0
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("G,K,S,tail,B,Hk", [
     (4, 4, 8 * 2000, 5, 2, 4),      # config-2 layer shape (jpeg-fp line)
     (8, 2, 8 * 300, 3, 2, 4),       # N = 32 columns, 2 ring stages
@@ -227,21 +228,21 @@ def test_tensor_core_and_cuda_core_kernels_vs_oracle(kernel_choice, G, K, dt, S,
     (2, 4, 8 * 20, 4, 2, 4),        # one split, partial tile
     (4, 4, 8 * 9000, 1, 1, 1),      # one unit, many splits merged
 ])
-def test_tensor_core_bf16_coefficients_vs_oracle(kernel_choice, G, K, S, tail, B, Hk):
-    """Unquantized jpeg archives (bf16 coefficients, no scales): the
-    tensor-core kernel's bf16 path and the CUDA-core kernel against the
-    oracle, within the bf16 output tolerance."""
+def test_tensor_core_16bit_coefficients_vs_oracle(kernel_choice, G, K, S, tail, B, Hk, dt):
+    """Unquantized jpeg archives (bf16 or fp16 coefficients, no scales): the
+    tensor-core kernel's 16-bit paths and the CUDA-core kernel against the
+    oracle, within the 16-bit output tolerance."""
     import flashcodec_b200 as fc
     from flashcodec_b200 import _kernels as Kn
-    k, v, q = bench.synth_case(B, Hk * G, Hk, S + tail, 128, 0.95, 29, dtype=torch.bfloat16)
+    k, v, q = bench.synth_case(B, Hk * G, Hk, S + tail, 128, 0.95, 29, dtype=dt)
     ks, vs = build("jpeg", dict(keep_freqs=K, quant_bits=0), k.to(DEV), v.to(DEV))
-    assert ks._coeffs.dtype == torch.bfloat16
+    assert ks._coeffs.dtype == dt
     ref = oracle_attention(q, ks, vs)
     outs = {}
     for which in ("tensor-core", "cuda-core"):
         kernel_choice(which)
         outs[which] = fc.codec_decode_attention(q.to(DEV), ks, vs)
-        check_close(outs[which], ref, torch.bfloat16)
+        check_close(outs[which], ref, dt)
     kernel_choice("auto")
     auto = fc.codec_decode_attention(q.to(DEV), ks, vs)
     assert torch.equal(auto, outs["tensor-core"])
@@ -274,11 +275,11 @@ def test_unwritten_capacity_is_never_read(kernel_choice, quant):
         check_close(fc.codec_decode_attention(q.to(DEV), ks, vs), ref, torch.bfloat16)
 
 
-def test_tensor_core_refuses_fp16_coefficients(kernel_choice):
-    """fp16 coefficient rows stay on the CUDA-core kernel: forcing the
+def test_tensor_core_refuses_fp32_coefficients(kernel_choice):
+    """fp32 coefficient rows stay on the CUDA-core kernel: forcing the
     tensor-core kernel on them fails loudly."""
     import flashcodec_b200 as fc
-    k, v, q = bench.synth_case(1, 8, 2, 8 * 40, 128, 0.95, 3, dtype=torch.float16)
+    k, v, q = bench.synth_case(1, 8, 2, 8 * 40, 128, 0.95, 3, dtype=torch.float32)
     ks, vs = build("jpeg", dict(keep_freqs=4, quant_bits=0), k.to(DEV), v.to(DEV))
     kernel_choice("tensor-core")
     with pytest.raises(NotImplementedError):
