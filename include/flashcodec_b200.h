@@ -423,7 +423,7 @@ FC_API int fc_decode_attn_masked(const void *q, int q_dtype, int64_t B, int64_t 
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
  * AUTO uses the tcgen05 tensor-core kernel whenever the archive allows it
  * (contiguous (B, Hk, cap, s, 128) rows of int8 codes with one scale per row,
- * or of bf16 coefficients without scales; block size 8 with s in
+ * or of bf16 or fp16 coefficients without scales; block size 8 with s in
  * {1, 2, 4, 8} stored rows per block, Hq/Hk <= 8) and the CUDA-core kernel
  * otherwise.  CUDA_CORE forces the CUDA-core kernel;
  * TENSOR_CORE makes unsupported layouts fail with FC_ENOTSUP instead of
