@@ -53,6 +53,9 @@ constexpr int kMaxD = 256;
 constexpr int kTargetChunk = 128;     // blocks per split (upper target)
 constexpr int kMinChunk = 16;
 constexpr size_t kSmemBudget = 96 * 1024;  // per-CTA shared-memory plan budget
+constexpr int kAringSlotBytes = 8 * 128 * 4;            // one block: 8 rows of 128 fp32
+constexpr int kAringBytes = kWarps * 2 * kAringSlotBytes; // two slots per warp
+constexpr size_t kAringBudget = 55 * 1024;              // 4 CTAs per SM with the ring
 
 struct AttnArgs {
     const void *q;
@@ -94,6 +97,7 @@ struct AttnArgs {
     int chunk;       // blocks per split
     int tb;          // blocks per bulk tile
     int lprl;        // log2(lanes per row)
+    int aring;       // per-warp cp.async ring of fp32 row blocks (see make_plan)
     int *status;     // workspace header: epoch of the last launch whose wait gave up
     int epoch;       // this launch's epoch (> 0, increasing)
     int *cnt;        // per (unit, group) arrival counters
@@ -337,6 +341,61 @@ attn_kernel(AttnArgs a) {
         }
         return off;
     };
+    // ---- per-warp cp.async ring (a.aring; make_plan): fp32 rows, 8 stored
+    // rows per block, head dim 128, so a warp's 32 lanes cover one row (4
+    // channels each) and a warp takes whole blocks (warp, warp + 4, ...).  Slot
+    // k & 1 of the warp's two holds block k of the warp: row j at byte 512 j,
+    // lane li's 16 bytes at 16 li (a png anchor row: its own dtype, 4 elements
+    // per lane).  Each lane copies only the bytes it reads back, so completion
+    // is the lane's own cp.async group -- no barrier.  Blocks k + 1 and k + 2
+    // are in flight while block k is computed.
+    constexpr bool kRing = sizeof(RT) == 4 && VEC == 4 && NCH == 1 && !BULK && U == 8;
+    unsigned char *wring = ring + warp * (2 * kAringSlotBytes);
+    const int aes = a.kanc ? (a.anc_dtype == FC_F32 ? 4 : 2) : 4;
+    auto ring_issue = [&](const RT *base, const void *anc, int64_t sn, int64_t sj, int k) {
+        const int blk = warp + k * kWarps;
+        if (blk < nb) {
+            unsigned char *slot = wring + (k & 1) * kAringSlotBytes;
+            const RT *rb = base + (int64_t)blk * sn - (anc ? sj : 0);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (j == 0 && anc) {
+                    const unsigned char *src = static_cast<const unsigned char *>(anc) +
+                        ((b * a.a_sb + hk * a.a_sh + (n0 + blk) * a.a_sn) + li * 4) * aes;
+                    if (aes == 4) cp_async16(slot + li * 16, src);
+                    else cp_async8(slot + li * 16, src);
+                } else {
+                    cp_async16(slot + j * 512 + li * 16, rb + (int64_t)j * sj + li * 4);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    auto ring_rows = [&](const void *anc, int k, float x[U][NCH][VEC]) {
+        const unsigned char *slot = wring + (k & 1) * kAringSlotBytes;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const unsigned char *p = slot + j * 512 + li * 16;
+            if (j == 0 && anc && aes == 2) {
+                const uint2 h = *reinterpret_cast<const uint2 *>(p);
+                if (a.anc_dtype == FC_BF16) {
+                    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&h.x));
+                    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&h.y));
+                    x[j][0][0] = lo.x; x[j][0][1] = lo.y; x[j][0][2] = hi.x; x[j][0][3] = hi.y;
+                } else {
+                    const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+                    const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&h.y));
+                    x[j][0][0] = lo.x; x[j][0][1] = lo.y; x[j][0][2] = hi.x; x[j][0][3] = hi.y;
+                }
+            } else {
+                const float4 v4 = *reinterpret_cast<const float4 *>(p);
+                x[j][0][0] = v4.x; x[j][0][1] = v4.y; x[j][0][2] = v4.z; x[j][0][3] = v4.w;
+            }
+        }
+    };
+    // blocks of this warp in the split
+    const int nmine = nb > warp ? (nb - warp + kWarps - 1) / kWarps : 0;
+
     // entries a lane holds after the butterfly, and whether it writes them
     // (when the row has more lanes than entries, lanes repeat; the first writes)
     const int held = max(M >> a.lprl, 1);
@@ -409,6 +468,36 @@ attn_kernel(AttnArgs a) {
             __syncthreads();
             if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
+    } else if (kRing && a.aring) {
+        ring_issue(kbase, a.kanc, a.k_sn, a.k_sj, 0);
+        ring_issue(kbase, a.kanc, a.k_sn, a.k_sj, 1);
+        for (int k = 0; k < nmine; k++) {
+            cp_async_wait<1>();  // block k has landed (k + 1 may be in flight)
+            const int blk = warp + k * kWarps;
+            float x[U][NCH][VEC];
+            ring_rows(a.kanc, k, x);
+#pragma unroll
+            for (int u = (a.kanc ? 1 : 0); u < U; u++) kgs(blk * s + u, x[u]);
+            float v[M];
+            dots(x, v);
+            const int off = butterfly(v);
+            // the slot is read: refill it with block k + 2
+            ring_issue(kbase, a.kanc, a.k_sn, a.k_sj, k + 2);
+            if (writer) {
+#pragma unroll
+                for (int i = 0; i < M; i++) {
+                    if (i < held) {
+                        const int e = off + i;
+                        const int row = blk * s + e / GT;
+                        ssc[row * GT + e % GT] = v[i] * sks[row];
+                    }
+                }
+            }
+        }
+        cp_async_wait<0>();
+        // the V pass's first two blocks start now, under the softmax step
+        ring_issue(vbase, a.vanc, a.v_sn, a.v_sj, 0);
+        ring_issue(vbase, a.vanc, a.v_sn, a.v_sj, 1);
     } else if (s % U == 0) {
         // block-major: each lane group takes whole blocks, U of its rows at a
         // time (a png block's anchor is row 0 of its first batch)
@@ -589,6 +678,30 @@ attn_kernel(AttnArgs a) {
             __syncthreads();
             if (tid == 0 && t + kStages < ttot) issue(issued++);
         }
+    } else if (kRing && a.aring) {
+        // the first two blocks were issued at the end of pass 1
+        for (int k = 0; k < nmine; k++) {
+            cp_async_wait<1>();
+            const int blk = warp + k * kWarps;
+            float x[U][NCH][VEC];
+            ring_rows(a.vanc, k, x);
+            float w[U][GT];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int row = blk * s + u;
+                vgs(row, x[u]);
+#pragma unroll
+                for (int g = 0; g < GT; g++) w[u][g] = ssc[row * GT + g];
+            }
+            ring_issue(vbase, a.vanc, a.v_sn, a.v_sj, k + 2);
+#pragma unroll
+            for (int u = 0; u < U; u++)
+#pragma unroll
+                for (int g = 0; g < GT; g++)
+#pragma unroll
+                    for (int c = 0; c < NCH; c++) axpy(w[u][g], x[u][c], acc[g][c]);
+        }
+        cp_async_wait<0>();
     } else if (s % U == 0) {
         // block-major, as in pass 1
         for (int blk0 = 0; blk0 < nb; blk0 += rows_per_pass) {
@@ -766,6 +879,7 @@ size_t workspace_for(int64_t units, int n_split, int GT, int64_t D) {
 struct Plan {
     int GT = 1, n_groups = 1, n_split = 1, chunk = 0, tb = 1, lprl = 5;
     int vec_mode = 0;  // 0 = generic scalar, 1 = 16-byte vectors, direct; 2 = bulk ring
+    int aring = 0;     // direct fp32 rows through a per-warp cp.async ring
     size_t smem = 0, ws = 0;
     int off_A, off_ksc, off_vsc, off_sc, off_lg, off_red, off_stat, off_ring, off_bar;
 };
@@ -814,14 +928,22 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
         p.n_split = (int)ns;
         p.chunk = (int)chunk;
     }
+    // Direct fp32 rows with 8 stored rows per block and head dim 128 (png
+    // archives: bf16/fp16/fp32 anchors + fp32 deltas) stream through a
+    // two-slot cp.async ring per warp, so a warp has its next blocks in flight
+    // while it computes one; the ring's 32 KB come out of the per-block arrays
+    // (smaller chunks) so that 4 CTAs still fit an SM.
+    p.aring = (vec_mode == 1 && es == 4 && D == 128 && s == 8 && p.GT <= 4 && n > 0) ? 1 : 0;
     // cap the chunk so the per-block shared-memory arrays fit the budget
     {
         const size_t fixed = (size_t)r * s * 4 + (size_t)kWarps * p.GT * D * 4 +
                              (size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4 +
                              (vec_mode == 2 ? (size_t)kStages * (kStageBytes + 8) : 0) +
+                             (p.aring ? (size_t)kAringBytes : 0) +
                              (size_t)2 * (n_raw + 1) * p.GT * 4 + 8 * 128;
         const size_t per_block = ((size_t)2 * s + (size_t)(s + r) * p.GT) * 4;
-        const size_t cap = fixed < kSmemBudget ? (kSmemBudget - fixed) / per_block : 1;
+        const size_t budget = p.aring ? kAringBudget : kSmemBudget;
+        const size_t cap = fixed < budget ? (budget - fixed) / per_block : 1;
         if (n > 0 && (size_t)p.chunk > cap) {
             const int64_t chunk = std::max<int64_t>(1, (int64_t)cap);
             p.n_split = (int)((n + chunk - 1) / chunk);
@@ -842,7 +964,8 @@ Plan make_plan(int64_t B, int64_t Hq, int64_t Hk, int64_t D, int64_t n, int s, i
     p.off_red = take(std::max((size_t)kWarps * p.GT * D * 4,
                               (size_t)merge_scratch_floats(p.n_split, p.GT, kThreads) * 4));
     p.off_stat = take((size_t)(2 * kWarps * p.GT + 2 * p.GT) * 4);
-    p.off_ring = take(vec_mode == 2 ? (size_t)kStages * kStageBytes : 0);
+    p.off_ring = take(vec_mode == 2 ? (size_t)kStages * kStageBytes
+                                    : (p.aring ? (size_t)kAringBytes : 0));
     p.off_bar = take(vec_mode == 2 ? (size_t)kStages * 8 : 0);
     p.smem = off;
     // workspace: header | counters | pm | pl | pacc
@@ -872,8 +995,11 @@ int pick_vec_mode(int64_t D, int es, const void *k, const void *v, int64_t k_sb,
 template <typename RT, int GT>
 int launch_gt(const Plan &p, AttnArgs &args, dim3 grid, cudaStream_t st) {
     auto setup = [&](auto kern) {
-        if (p.smem > 48 * 1024)
+        if (p.smem > 48 * 1024) {
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+            cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+        }
         kern<<<grid, kThreads, p.smem, st>>>(args);
     };
     constexpr int V16 = 16 / (int)sizeof(RT);
@@ -1104,7 +1230,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
     a.A = A;
     a.scale_log2 = softmax_scale * 1.4426950408889634f;
     a.out = out; a.out_dtype = out_dtype; a.o_sb = o_sb; a.o_sh = o_sh;
-    a.n_split = p.n_split; a.chunk = p.chunk; a.tb = p.tb; a.lprl = p.lprl;
+    a.n_split = p.n_split; a.chunk = p.chunk; a.tb = p.tb; a.lprl = p.lprl; a.aring = p.aring;
     unsigned char *ws = static_cast<unsigned char *>(workspace);
     a.status = reinterpret_cast<int *>(ws);
     a.epoch = next_epoch();

@@ -102,6 +102,24 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         : "memory");
 }
 
+// Per-thread async copies global -> shared (cp.async, completion by
+// commit/wait groups of the issuing thread; no barrier, no mbarrier).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Arguments of the tensor-core decode-attention kernel (fc_attention_tc.cu).
 struct TcArgs {
     const void *q;
