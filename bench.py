@@ -114,13 +114,17 @@ def attn_bytes(B, Hq, Hk, D, n, K, tail, code_b=1, scale_b=4, io_b=2):
 
 def codec_attn_bytes(cfg, n):
     """Algorithmic bytes of one launch for the archive format in cfg:
-    jpeg-int8 (codes + scales), jpeg-fp (bf16 coefficients, quant_bits=0) or
-    png (bf16 anchor + fp32 deltas per block)."""
+    jpeg-int8 (codes + scales), jpeg-int8-g32 (codes + one scale per 32
+    channels), jpeg-fp (bf16 coefficients, quant_bits=0) or png (bf16 anchor
+    + fp32 deltas per block)."""
     codec = cfg.get("codec", "jpeg-int8")
     B, Hq, Hk, D, tail = cfg["B"], cfg["Hq"], cfg["Hk"], cfg["D"], cfg["tail"]
     if codec == "jpeg-int8":
         return attn_bytes(B, Hq, Hk, D, n, cfg["K"], tail,
                           scale_b=2 if cfg["scale_dtype"] == "fp16" else 4)
+    if codec == "jpeg-int8-g32":   # one scale per 32 channels of a kept frequency row
+        return attn_bytes(B, Hq, Hk, D, n, cfg["K"], tail,
+                          scale_b=(D // 32) * (2 if cfg["scale_dtype"] == "fp16" else 4))
     if codec == "jpeg-fp":
         return attn_bytes(B, Hq, Hk, D, n, cfg["K"], tail, code_b=2, scale_b=0)
     per_block = D * 2 + (cfg["r"] - 1) * D * 4
@@ -244,9 +248,10 @@ def make_bench_codec(cfg):
     if codec == "png":
         return fc.make_codec("png", block_size=cfg["r"], keep_ratio=1.0)
     return fc.make_codec("jpeg", block_size=cfg["r"], keep_freqs=cfg["K"],
-                         quant_bits=8 if codec == "jpeg-int8" else 0,
+                         quant_bits=0 if codec == "jpeg-fp" else 8,
                          scale_dtype=torch.float16 if cfg["scale_dtype"] == "fp16"
-                         else torch.float32)
+                         else torch.float32,
+                         group_size=32 if codec == "jpeg-int8-g32" else None)
 
 
 def _fill_rows(st, b0, x):
@@ -260,8 +265,12 @@ def _fill_rows(st, b0, x):
     if st.codec.name == "jpeg":
         k = st.codec.keep_freqs
         basis = device_basis(r, k, x.device)
-        K.jpeg_encode(x[:, :, :n * r], basis, r, k, st._coeffs[rows, :, :n],
-                      st._scales[rows, :, :n] if st.codec.quantized else None)
+        if getattr(st.codec, "group_size", None) is not None:
+            K.jpeg_encode_grouped(x[:, :, :n * r], basis, r, k, st._coeffs[rows, :, :n],
+                                  st._scales[rows, :, :n], st.codec.group_size)
+        else:
+            K.jpeg_encode(x[:, :, :n * r], basis, r, k, st._coeffs[rows, :, :n],
+                          st._scales[rows, :, :n] if st.codec.quantized else None)
     else:
         K.png_encode(x[:, :, :n * r], r, st.codec.keep_m, st._deltas[rows, :, :n],
                      st._anchors[rows, :, :n])
@@ -336,6 +345,9 @@ def check_outputs(layers, outs, which, b=0):
             if st.codec.name == "png":
                 rows[nm] = orc.stored_rows("png", anchors=f(st._anchors[sel, :, :n]),
                                            deltas=f(st._deltas[sel, :, :n]))
+            elif getattr(st.codec, "group_size", None) is not None:
+                rows[nm] = orc.dequantize_grouped(st._coeffs[sel, :, :n].cpu().numpy(),
+                                                  f(st._scales[sel, :, :n]))
             elif st.codec.quantized:
                 rows[nm] = orc.stored_rows("jpeg", codes=f(st._coeffs[sel, :, :n]),
                                            scales=f(st._scales[sel, :, :n]))
@@ -740,6 +752,9 @@ def workload_config(cfg, world, plan=None, Bg=None):
     if codec == "jpeg-fp":
         name = name.replace("int8 DCT archive", "unquantized DCT archive (bf16 coefficients)")
         desc = f"jpeg r={cfg['r']} K={cfg['K']} quant_bits=0, bf16 coefficients"
+    elif codec == "jpeg-int8-g32":
+        name = name.replace("int8 DCT archive", "int8 DCT archive with one scale per 32 channels")
+        desc = f"jpeg r={cfg['r']} K={cfg['K']} int8, {cfg['scale_dtype']} scales per 32 channels"
     elif codec == "png":
         name = name.replace("int8 DCT archive", "png archive (bf16 anchors + fp32 deltas)")
         name = name.replace("36 layers", f"{cfg['layers']} layers")
@@ -784,9 +799,11 @@ def main():
                     help="strong scaling: this many sequences in total, sharded over the GPUs "
                          "by batch (>= GPUs) or by KV head (< GPUs; one NCCL all_gather of "
                          "outputs per layer)")
-    ap.add_argument("--codec", default="jpeg-int8", choices=("jpeg-int8", "jpeg-fp", "png"),
+    ap.add_argument("--codec", default="jpeg-int8",
+                    choices=("jpeg-int8", "jpeg-int8-g32", "jpeg-fp", "png"),
                     help="archive format of the attention workload: jpeg-int8 (default, the "
-                         "headline), jpeg-fp (quant_bits=0, bf16 coefficients) or png "
+                         "headline), jpeg-int8-g32 (one scale per 32 channels), jpeg-fp "
+                         "(quant_bits=0, bf16 coefficients) or png "
                          "(r=8, lossless; 4 layers by default)")
     ap.add_argument("--gather", default="peer", choices=("peer", "nccl"),
                     help="with split KV heads: peer (default) -- the attention kernel stores "
