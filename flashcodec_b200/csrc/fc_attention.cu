@@ -35,8 +35,10 @@
 
 namespace fc {
 
-void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk);
-bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled);
+void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk,
+             bool pg = false);
+bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled, int sgrp,
+                  int scale_dtype);
 int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, int rows_dtype,
                    cudaStream_t st);
 
@@ -1054,9 +1056,11 @@ extern "C" size_t fc_decode_attn_workspace_size(int64_t B, int64_t Hq, int64_t H
             w = std::max(w, make_plan(B, Hq, Hk, D, n_blocks, s, r, n_raw, es, vm).ws);
     if (n_blocks > 0 && r == 8 && s <= 8 && (8 % s) == 0 && Hq / Hk <= 8) {
         for (int es : {1, 2}) {  // int8 codes, bf16 coefficients
-            int ns, chunk;
-            tc_plan(n_blocks, s, B * Hk, pick_gt(Hq / Hk), es, ns, chunk);
-            w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
+            for (bool pg : {false, true}) {  // per-row or per-32-channel scales
+                int ns, chunk;
+                tc_plan(n_blocks, s, B * Hk, pick_gt(Hq / Hk), es, ns, chunk, pg);
+                w = std::max(w, workspace_for(B * Hk, ns, pick_gt(Hq / Hk), D));
+            }
         }
     }
     return w;
@@ -1115,19 +1119,29 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
 
     // png rows come from two tensors (the CUDA-core kernel's direct-load path);
     // a visibility mask is applied by the CUDA-core kernel
-    const int sel = (png || vis || sgrp) ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
+    // one fp32 scale per 32 channels of int8 codes at head dim 128 may take the
+    // tensor-core kernel's per-group form; other per-group layouts cannot
+    const bool pg_cand = sgrp == 32 && D == 128 && rows_dtype == FC_I8 && scale_dtype == FC_F32;
+    const int sel = (png || vis || (sgrp && !pg_cand)) ? FC_ATTN_CUDA_CORE : g_attn_kernel.load();
     if (peers && (sel == FC_ATTN_CUDA_CORE || n_blocks == 0)) {
         set_error("decode_attn_peers: peer outputs need the tensor-core kernel (an archive of "
                   "at least one block in one of its layouts)");
         return FC_ENOTSUP;
     }
-    if (sgrp && g_attn_kernel.load() == FC_ATTN_TENSOR_CORE) {
-        set_error("decode_attn: the tensor-core kernel takes one scale per row only");
+    if (sgrp && !pg_cand && g_attn_kernel.load() == FC_ATTN_TENSOR_CORE) {
+        set_error("decode_attn: the tensor-core kernel takes one scale per row, or one fp32 "
+                  "scale per 32 channels of int8 codes at head dim 128");
         return FC_ENOTSUP;
     }
     if (n_blocks > 0 && sel != FC_ATTN_CUDA_CORE) {
         const int64_t G = Hq / Hk, row = (int64_t)s * D;
-        const bool contig = tc_supported(D, s, r, G, rows_dtype, k_scales || v_scales) &&
+        // per-group scales: 4 contiguous fp32 per stored row, 16-byte aligned
+        const bool pg_layout = !sgrp || (ks_sj == 4 && vs_sj == 4 && aligned(k_scales, 16) &&
+                                         aligned(v_scales, 16) && ks_sb % 4 == 0 &&
+                                         ks_sh % 4 == 0 && ks_sn % 4 == 0 && vs_sb % 4 == 0 &&
+                                         vs_sh % 4 == 0 && vs_sn % 4 == 0);
+        const bool contig = tc_supported(D, s, r, G, rows_dtype, k_scales || v_scales, sgrp,
+                                         scale_dtype) && pg_layout &&
                             (rows_dtype != FC_I8 || (k_scales && v_scales)) && k_sj == D && k_sn == row &&
                             v_sj == D && v_sn == row && k_sh % row == 0 && v_sh % row == 0 &&
                             k_sb == Hk * k_sh && v_sb == Hk * v_sh && aligned(k_rows, 16) &&
@@ -1135,7 +1149,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
         if (contig) {
             const int GT = pick_gt(G);
             int ns, chunk;
-            tc_plan(n_blocks, s, B * Hk, GT, dtype_size(rows_dtype), ns, chunk);
+            tc_plan(n_blocks, s, B * Hk, GT, dtype_size(rows_dtype), ns, chunk, sgrp != 0);
             const size_t need = workspace_for(B * Hk, ns, GT, D);
             if (!workspace || workspace_bytes < need) {
                 set_error("decode_attn: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
@@ -1149,6 +1163,7 @@ static int decode_attn_impl(const void *q, int q_dtype, int64_t B, int64_t Hq, i
             t.ksc = k_scales; t.vsc = v_scales; t.sc_dtype = scale_dtype;
             t.ks_sb = ks_sb; t.ks_sh = ks_sh; t.ks_sn = ks_sn;
             t.vs_sb = vs_sb; t.vs_sh = vs_sh; t.vs_sn = vs_sn;
+            t.ks_sj = ks_sj; t.vs_sj = vs_sj; t.pg = sgrp != 0;
             t.kraw = k_raw; t.vraw = v_raw; t.raw_dtype = raw_dtype;
             t.kr_sb = kr_sb; t.kr_sh = kr_sh; t.kr_st = kr_st;
             t.vr_sb = vr_sb; t.vr_sh = vr_sh; t.vr_st = vr_st;

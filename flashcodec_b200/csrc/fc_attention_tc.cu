@@ -245,10 +245,19 @@ constexpr int kMaxLog = 1 << 29;  // clamp of the integer logit maxima
 // (columns 3g..3g+2), the score and output columns are fp32 sums of the limbs,
 // and the weights of a tile are taken relative to the tile max 2^m, so the
 // output of tile t folds into acc with the factor 2^(m_t - Mref).
-template <bool BF, int GT>
-__host__ __device__ constexpr int tc_stages() { return (BF && GT == 8) ? 2 : kTcStages; }
-template <bool BF, int GT>
-__host__ __device__ constexpr int tc_min_ctas() { return BF ? 2 : (GT <= 4 ? 4 : 3); }
+//
+// PG: int8 codes with one fp32 scale per 32 channels (the per-32 format,
+// head dim 128 = 4 groups; GT <= 4).  Each 32-channel K step of the score MMA
+// accumulates into its own column range, and a row's score is the sum of the
+// four ranges weighted by its group scales.  The output needs each group's V
+// scale inside the weights: one weight-limb B tile per group (w times that
+// group's V scale, with its own common exponent), four output accumulators,
+// and epilogue warp w -- whose TMEM lanes are the channels of group w -- folds
+// only accumulator w.  256 TMEM columns and a 5-stage ring: 2 CTAs per SM.
+template <bool BF, int GT, bool PG = false>
+__host__ __device__ constexpr int tc_stages() { return PG ? 5 : (BF && GT == 8) ? 2 : kTcStages; }
+template <bool BF, int GT, bool PG = false>
+__host__ __device__ constexpr int tc_min_ctas() { return (BF || PG) ? 2 : (GT <= 4 ? 4 : 3); }
 
 //
 // F16 (with BF): fp16 coefficient rows through the same kind::f16 MMAs with
@@ -256,17 +265,21 @@ __host__ __device__ constexpr int tc_min_ctas() { return BF ? 2 : (GT <= 4 ? 4 :
 // power of two that puts its largest |q| in [2^13, 2^14) (folded back through
 // the logit factor) and the weights by 2^12 (folded back with the output), which
 // keeps the limbs of every value that matters normal.
-template <int GT, int S, bool BF, bool F16 = false>
-__global__ void __launch_bounds__(kTcThreads, tc_min_ctas<BF, GT>())
+template <int GT, int S, bool BF, bool F16 = false, bool PG = false>
+__global__ void __launch_bounds__(kTcThreads, tc_min_ctas<BF, GT, PG>())
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                const __grid_constant__ TcArgs a) {
+    static_assert(!PG || (!BF && GT <= 4), "per-group scales: int8 codes, at most 4 heads");
     constexpr int NL = BF ? 3 : kLimbs;           // limbs per head
     constexpr int N = NL * GT <= 16 ? 16 : 32;    // B columns: NL limbs x GT heads, padded
     constexpr int PP = kR / S;                    // positions of a block per lane
-    constexpr int XF = 2 * GT + 1;                // exchange fields per tile (x 4 warps)
+    constexpr int NG = PG ? 4 : 1;                // scale groups per row
+    constexpr int XF = GT + NG * GT + 1;          // exchange fields per tile (x 4 warps)
     constexpr int TB = BF ? 2 * kTileBytes : kTileBytes;  // bytes per ring stage
-    constexpr int NST = tc_stages<BF, GT>();      // ring stages
+    constexpr int NST = tc_stages<BF, GT, PG>();  // ring stages
     constexpr int BQ = N * 128 * (BF ? 2 : 1);    // bytes of one B tile (q or weight limbs)
+    constexpr int SB = NG * N;                    // TMEM columns of one score / output buffer
+    constexpr int BW = NG * BQ;                   // bytes of one weight-limb buffer
     // Programmatic dependent launch: the next launch in the stream (when it
     // is launched as a dependent) may be scheduled once every CTA of this one
     // has started; it reads nothing before its griddepcontrol.wait.
@@ -276,7 +289,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *ring = smem;
     unsigned char *bq = smem + a.off_bq;                       // BQ bytes of q limbs (K-major B)
-    unsigned char *bw = smem + a.off_bw;                       // 2 x BQ weight limbs
+    unsigned char *bw = smem + a.off_bw;                       // 2 x BW weight limbs
     int *xch = reinterpret_cast<int *>(smem + a.off_xch);      // [2][XF][4 warps] exchange, [4] flags
     float *red = reinterpret_cast<float *>(smem + a.off_red);  // small reductions
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bar);
@@ -316,7 +329,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     const int slab = (int)(b * a.Hk + hk);
     const uint32_t idesc_s = BF ? bf16_idesc(N, 0, F16) : i8_idesc(N, 0);
     const uint32_t idesc_o = BF ? bf16_idesc(N, 1, F16) : i8_idesc(N, 1);
-    constexpr int kAlloc = N * 4 <= 64 ? 64 : 128;  // TMEM columns: 2 score + 2 output buffers
+    // TMEM columns: 2 score buffers at [0, 2 SB), 2 output buffers after them
+    constexpr int kAlloc = PG ? 256 : (N * 4 <= 64 ? 64 : 128);
 
     // ---------------------------------------------------------------- setup
     int issued = 0, consumed = 0;  // producer bookkeeping (lane 0 of warp 4)
@@ -429,8 +443,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 #pragma unroll
             for (int row = 0; row < N; row++) {
                 if (row >= kLimbs * GT) bq[sw128_off(row, d)] = 0;
-                bw[sw128_off(row, d)] = 0;
-                bw[N * 128 + sw128_off(row, d)] = 0;
+#pragma unroll
+                for (int t2 = 0; t2 < 2 * NG; t2++) bw[t2 * BQ + sw128_off(row, d)] = 0;
             }
         }
         fence_async_smem();
@@ -462,15 +476,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                         // each row, in atom k / 4 at byte (k % 4) * 32
 #pragma unroll
                         for (int k = 0; k < 8; k++)
-                            mma_bf16(tmem + (t & 1) * N,
+                            mma_bf16(tmem + (t & 1) * SB,
                                      sw128_desc(at + (k >> 2) * kTileBytes + (k & 3) * 32),
                                      sw128_desc(bt + (k >> 2) * (N * 128) + (k & 3) * 32), idesc_s,
                                      k > 0);
                     } else {
 #pragma unroll
-                        for (int k = 0; k < 4; k++)
-                            mma_i8(tmem + (t & 1) * N, sw128_desc(at + k * 32), sw128_desc(bt + k * 32),
-                                   idesc_s, k > 0);
+                        for (int k = 0; k < 4; k++)  // PG: K step k = group k, own columns
+                            mma_i8(tmem + (t & 1) * SB + (PG ? k * N : 0), sw128_desc(at + k * 32),
+                                   sw128_desc(bt + k * 32), idesc_s, PG ? 0 : k > 0);
                     }
                     mma_commit(sdone + (t & 1));
                     if (!mbar_wait_bounded(sdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
@@ -479,20 +493,22 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     if (t >= 2 && !mbar_wait_bounded(vfree + (t & 1), ((t - 2) >> 1) & 1, a.status, a.epoch))
                         return false;
                     tc_fence_after();
-                    const uint32_t bt = smem_addr(bw + (t & 1) * BQ);
+                    const uint32_t bt = smem_addr(bw + (t & 1) * BW);
                     if constexpr (BF) {
                         // K = 128 rows in 8 steps of 16 (2 KB of the tile each); the
                         // tile's channels 64-127 lie one box (LBO) further on
 #pragma unroll
                         for (int k = 0; k < 8; k++)
-                            mma_bf16(tmem + (2 + (t & 1)) * N, sw128_desc(at + k * 2048, kTileBytes),
+                            mma_bf16(tmem + 2 * SB + (t & 1) * SB, sw128_desc(at + k * 2048, kTileBytes),
                                      sw128_desc(bt + (k >> 2) * (N * 128) + (k & 3) * 32), idesc_o,
                                      k > 0);
                     } else {
 #pragma unroll
-                        for (int k = 0; k < 4; k++)
-                            mma_i8(tmem + (2 + (t & 1)) * N, sw128_desc(at + k * 4096),
-                                   sw128_desc(bt + k * 32), idesc_o, k > 0);
+                        for (int gi = 0; gi < NG; gi++)  // PG: one weight tile per group
+#pragma unroll
+                            for (int k = 0; k < 4; k++)
+                                mma_i8(tmem + 2 * SB + (t & 1) * SB + gi * N, sw128_desc(at + k * 4096),
+                                       sw128_desc(bt + gi * BQ + k * 32), idesc_o, k > 0);
                     }
                     mma_commit(vdone + (t & 1));
                     if (!mbar_wait_bounded(vdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
@@ -531,8 +547,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         // row scales: split base (uniform) + this thread's offset, one tile per step
         const int64_t kb0 = b * a.ks_sb + hk * a.ks_sh + n0 * a.ks_sn;
         const int64_t vb0 = b * a.vs_sb + hk * a.vs_sh + n0 * a.vs_sn;
-        int kidx = (lrow / S) * (int)a.ks_sn + (lrow & (S - 1));
-        int vidx = (lrow / S) * (int)a.vs_sn + (lrow & (S - 1));
+        int kidx = (lrow / S) * (int)a.ks_sn + (lrow & (S - 1)) * (PG ? (int)a.ks_sj : 1);
+        int vidx = (lrow / S) * (int)a.vs_sn + (lrow & (S - 1)) * (PG ? (int)a.vs_sj : 1);
         const int kstep = (kTileRows / S) * (int)a.ks_sn;
         const int vstep = (kTileRows / S) * (int)a.vs_sn;
         const bool sc16 = a.sc_dtype == FC_F16;
@@ -540,15 +556,21 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             return sc16 ? __half2float(static_cast<const __half *>(p)[base + i])
                         : static_cast<const float *>(p)[base + i];
         };
+        // per-group scales of this row: 4 fp32 (a 16-byte load)
+        auto group_scales = [&](const void *p, int64_t base, int i) -> float4 {
+            return *reinterpret_cast<const float4 *>(static_cast<const float *>(p) + base + i);
+        };
         // fold the output of tile u (limbs relative to 2^(AXp - 132)) into acc
+        // (PG: this warp's channels are group `warp`, its own accumulator)
         auto fold = [&](int u) -> bool {
             const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(vdone + (u & 1), (u >> 1) & 1,
                                                                       a.status, a.epoch));
             if (!ok) return false;
             tc_fence_after();
             int32_t o[N];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N, o);
-            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (2 + (u & 1)) * N + 16, o + 16);
+            const uint32_t oc = 2 * SB + (u & 1) * SB + (PG ? warp * N : 0);
+            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + oc, o);
+            if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + oc + 16, o + 16);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
@@ -565,15 +587,31 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
         };
         int pend_bad = 0;
         float ks_next = 0.0f, vs_next = 0.0f;
-        if (!BF && T > 0 && lrow < R) {
+        float4 kg_next = make_float4(0.f, 0.f, 0.f, 0.f), vg_next = kg_next;
+        if (!BF && !PG && T > 0 && lrow < R) {
             ks_next = scale_at(a.ksc, kb0, kidx);
             vs_next = scale_at(a.vsc, vb0, vidx);
+        }
+        if (PG && T > 0 && lrow < R) {
+            kg_next = group_scales(a.ksc, kb0, kidx);
+            vg_next = group_scales(a.vsc, vb0, vidx);
         }
         for (int t = 0; t < T; t++) {
             const int par = t & 1;
             const int row = t * kTileRows + lrow;
-            const float ks = BF ? 1.0f : ks_next, vsr = BF ? 1.0f : vs_next;
-            if constexpr (!BF) {
+            const float ks = (BF || PG) ? 1.0f : ks_next, vsr = (BF || PG) ? 1.0f : vs_next;
+            const float4 kg = kg_next, vg = vg_next;
+            if constexpr (PG) {
+                kidx += kstep;
+                vidx += vstep;
+                if (row + kTileRows < R) {  // the next tile's group scales
+                    kg_next = group_scales(a.ksc, kb0, kidx);
+                    vg_next = group_scales(a.vsc, vb0, vidx);
+                } else {
+                    kg_next = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vg_next = kg_next;
+                }
+            } else if constexpr (!BF) {
                 kidx += kstep;
                 vidx += vstep;
                 if (row + kTileRows < R) {  // the next tile's row scales
@@ -584,15 +622,19 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     vs_next = 0.0f;
                 }
             }
-            int mw[GT], wx[GT];
+            int mw[GT], wx[GT][NG];
             float w[GT], lsum[GT];
             const bool okS = __all_sync(0xffffffffu, mbar_wait_bounded(sdone + par, (t >> 1) & 1,
                                                                        a.status, a.epoch));
             if (okS) {
                 tc_fence_after();
-                int32_t v[N];
-                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N, v);
-                if (N == 32) tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * N + 16, v + 16);
+                int32_t v[NG][N];
+#pragma unroll
+                for (int gi = 0; gi < NG; gi++) {
+                    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * SB + gi * N, v[gi]);
+                    if (N == 32)
+                        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + par * SB + gi * N + 16, v[gi] + 16);
+                }
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
@@ -600,9 +642,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 const float nb = row >= R ? -INFINITY : 0.0f;  // rows past the split
 #pragma unroll
                 for (int g = 0; g < GT; g++) {
-                    const float sg =
-                        BF ? (bits_f(v[3 * g]) + (bits_f(v[3 * g + 1]) + bits_f(v[3 * g + 2]))) * cq[g]
-                           : limb_value(v, g) * (cq[g] * ks);
+                    float sg;
+                    if constexpr (PG)  // the four group sums, each times its group scale
+                        sg = fmaf(limb_value(v[0], g), kg.x,
+                                  fmaf(limb_value(v[1], g), kg.y,
+                                       fmaf(limb_value(v[2], g), kg.z, limb_value(v[3], g) * kg.w))) *
+                             cq[g];
+                    else if constexpr (BF)
+                        sg = (bits_f(v[0][3 * g]) + (bits_f(v[0][3 * g + 1]) + bits_f(v[0][3 * g + 2]))) * cq[g];
+                    else
+                        sg = limb_value(v[0], g) * (cq[g] * ks);
                     float lg[PP];
 #pragma unroll
                     for (int k = 0; k < PP; k++) lg[k] = fmaf(Ar[k][0], sg, nb);
@@ -638,11 +687,18 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     w[g] = c[0] * vsr;
                     mw[g] = mi;
                     if constexpr (BF) {
-                        wx[g] = 0;  // bf16 limbs need no common exponent
+                        wx[g][0] = 0;  // bf16 limbs need no common exponent
                     } else {
-                        const unsigned wb =
-                            __reduce_max_sync(0xffffffffu, __float_as_uint(w[g]) & 0x7fffffffu);
-                        wx[g] = (int)(wb >> 23) + mi;
+                        // PG: the weight of group gi is w times the row's V scale of gi
+#pragma unroll
+                        for (int gi = 0; gi < NG; gi++) {
+                            const float wg = PG ? w[g] * (gi == 0 ? vg.x : gi == 1 ? vg.y
+                                                          : gi == 2 ? vg.z : vg.w)
+                                                : w[g];
+                            const unsigned wb =
+                                __reduce_max_sync(0xffffffffu, __float_as_uint(wg) & 0x7fffffffu);
+                            wx[g][gi] = (int)(wb >> 23) + mi;
+                        }
                     }
                     lsum[g] = ls;
                 }
@@ -654,9 +710,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             if (lane == 0) {
                 if (okS) {
 #pragma unroll
-                    for (int g = 0; g < GT; g++) { xw[4 * g] = mw[g]; xw[4 * (GT + g)] = wx[g]; }
+                    for (int g = 0; g < GT; g++) {
+                        xw[4 * g] = mw[g];
+#pragma unroll
+                        for (int gi = 0; gi < NG; gi++) xw[4 * (GT + g * NG + gi)] = wx[g][gi];
+                    }
                 }
-                xw[4 * 2 * GT] = (okS ? 0 : 1) | pend_bad;
+                xw[4 * (XF - 1)] = (okS ? 0 : 1) | pend_bad;
                 mbar_arrive(xbar + par);
             }
             // the previous tile's output (in the reference before this tile's max)
@@ -672,14 +732,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 ab = true;
                 break;
             }
-            int m[GT], AX[GT];
+            int m[GT], AX[GT][NG];
 #pragma unroll
             for (int g = 0; g < GT; g++) {
                 m[g] = __shfl_sync(0xffffffffu, fmx, g);
-                AX[g] = __shfl_sync(0xffffffffu, fmx, GT + g);
+#pragma unroll
+                for (int gi = 0; gi < NG; gi++) AX[g][gi] = __shfl_sync(0xffffffffu, fmx, GT + g * NG + gi);
             }
             // weight limbs of this row (column lrow of the B tile)
-            unsigned char *bwt = bw + par * BQ;
+            unsigned char *bwt = bw + par * BW;
             if constexpr (BF) {
                 // w relative to the tile max 2^m (an exact power-of-two factor;
                 // fp16 weights also times 2^12)
@@ -694,10 +755,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
             } else {
 #pragma unroll
             for (int g = 0; g < GT; g++) {
+#pragma unroll
+              for (int gi = 0; gi < NG; gi++) {
                 // x = w * 2^(132 + m_w - AX), |x| < 64.  The factor's exponent is
                 // clamped at 127, reached only when every weight of this warp is
                 // below 2^-121 (contributions under 2^-114 of the output scale).
-                const float x = w[g] * pow2_biased(259 + mw[g] - AX[g]);
+                // PG: w times the row's V scale of group gi, in that group's tile.
+                const float wg = PG ? w[g] * (gi == 0 ? vg.x : gi == 1 ? vg.y : gi == 2 ? vg.z : vg.w)
+                                    : w[g];
+                const float x = wg * pow2_biased(259 + mw[g] - AX[g][gi]);
                 const float y0 = x + kRoundMagic;
                 const float d0 = x - (y0 - kRoundMagic);
                 const float y1 = fmaf(d0, 128.0f, kRoundMagic);
@@ -705,10 +771,12 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 const float y2 = fmaf(d1, 128.0f, kRoundMagic);
                 const float d2 = fmaf(d1, 128.0f, -(y2 - kRoundMagic));
                 const float y3 = fmaf(d2, 128.0f, kRoundMagic);
-                bwt[sw128_off(4 * g + 0, lrow)] = (unsigned char)__float_as_uint(y0);
-                bwt[sw128_off(4 * g + 1, lrow)] = (unsigned char)__float_as_uint(y1);
-                bwt[sw128_off(4 * g + 2, lrow)] = (unsigned char)__float_as_uint(y2);
-                bwt[sw128_off(4 * g + 3, lrow)] = (unsigned char)__float_as_uint(y3);
+                unsigned char *bt8 = bwt + gi * BQ;
+                bt8[sw128_off(4 * g + 0, lrow)] = (unsigned char)__float_as_uint(y0);
+                bt8[sw128_off(4 * g + 1, lrow)] = (unsigned char)__float_as_uint(y1);
+                bt8[sw128_off(4 * g + 2, lrow)] = (unsigned char)__float_as_uint(y2);
+                bt8[sw128_off(4 * g + 3, lrow)] = (unsigned char)__float_as_uint(y3);
+              }
             }
             }
             fence_async_smem();
@@ -724,7 +792,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                     Mref[g] = m[g];
                 }
                 Ls[g] = fmaf(lsum[g], pow2_biased(127 + mw[g] - Mref[g]), Ls[g]);
-                AXp[g] = BF ? m[g] : AX[g];
+                // PG: this warp folds group `warp`'s accumulator (selects, so
+                // that AX stays in registers)
+                if constexpr (BF) AXp[g] = m[g];
+                else if constexpr (PG)
+                    AXp[g] = warp == 0 ? AX[g][0] : warp == 1 ? AX[g][NG > 1 ? 1 : 0]
+                           : warp == 2 ? AX[g][NG > 2 ? 2 : 0] : AX[g][NG > 3 ? 3 : 0];
+                else AXp[g] = AX[g][0];
             }
         }
         float M[GT], L[GT];
@@ -902,7 +976,7 @@ bool pdl_enabled() {
 
 // Dynamic shared memory already opted in, per kernel variant (rows x GT x s) and device.
 constexpr int kMaxDevices = 64;
-std::atomic<int> g_smem_opted[48][kMaxDevices];
+std::atomic<int> g_smem_opted[64][kMaxDevices];
 
 // Tiles per split forced by FLASHCODEC_TC_CHUNK_TILES (tuning), 0 when unset.
 int chunk_tiles_override() {
@@ -919,7 +993,9 @@ int chunk_tiles_override() {
 // Resident CTAs per SM of the tensor-core kernel (its launch bounds and
 // shared-memory footprint): int8 rows 4 for GT <= 4, 3 for GT = 8; bf16 rows
 // (32 KB tiles) 2.
-int tc_ctas_per_sm(int GT, int es) { return es == 2 ? 2 : (GT <= 4 ? 4 : 3); }
+int tc_ctas_per_sm(int GT, int es, bool pg = false) {
+    return (es == 2 || pg) ? 2 : (GT <= 4 ? 4 : 3);
+}
 
 // Split plan of the tensor-core kernel.  Every CTA pays a pipeline fill and
 // drain, and CTAs of a second wave run behind an idle tail, so the plan takes
@@ -932,11 +1008,14 @@ static_assert(merge_scratch_floats(1024, 8, kTcThreads) * 4 + 1024 <= kTcStages 
 static_assert(merge_scratch_floats(1024, 8, kTcThreads) * 4 + 1024 <=
                   tc_stages<true, 8>() * 2 * kTileBytes,
               "merge scratch must fit the bf16 tile ring");
-void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk) {
+static_assert(merge_scratch_floats(1024, 8, kTcThreads) * 4 + 1024 <=
+                  tc_stages<false, 4, true>() * kTileBytes,
+              "merge scratch must fit the per-group tile ring");
+void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int &chunk, bool pg) {
     const int64_t tiles = std::max<int64_t>(1, (n * s + kTileRows - 1) / kTileRows);
     int64_t ct = chunk_tiles_override();
     if (ct == 0) {
-        const int64_t slots = (int64_t)num_sms() * tc_ctas_per_sm(GT, es);
+        const int64_t slots = (int64_t)num_sms() * tc_ctas_per_sm(GT, es, pg);
         const int64_t want = std::max<int64_t>(1, slots / std::max<int64_t>(units, 1));
         ct = (tiles + want - 1) / want;
         // at least 4 tiles per split: in launches smaller than a wave of such
@@ -950,10 +1029,15 @@ void tc_plan(int64_t n, int s, int64_t units, int GT, int es, int &n_split, int 
     chunk = (int)std::min<int64_t>(blocks, n);
 }
 
-// int8 codes with one scale per row, or bf16 / fp16 coefficients without scales
-bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled) {
-    const bool rows_ok = (rows_dtype == FC_I8 && scaled) ||
-                         ((rows_dtype == FC_BF16 || rows_dtype == FC_F16) && !scaled);
+// int8 codes with one scale per row (sgrp 0) or one fp32 scale per 32
+// channels (sgrp 32, at most 4 query heads per KV head), or bf16 / fp16
+// coefficients without scales
+bool tc_supported(int64_t D, int s, int r, int64_t G, int rows_dtype, bool scaled, int sgrp,
+                  int scale_dtype) {
+    const bool rows_ok = (rows_dtype == FC_I8 && scaled && sgrp == 0) ||
+                         (rows_dtype == FC_I8 && scaled && sgrp == 32 && scale_dtype == FC_F32 &&
+                          G <= 4) ||
+                         ((rows_dtype == FC_BF16 || rows_dtype == FC_F16) && !scaled && sgrp == 0);
     return D == 128 && rows_ok && r == kR && (s == 1 || s == 2 || s == 4 || s == 8) &&
            G >= 1 && G <= 8 && get_encode() != nullptr;
 }
@@ -974,15 +1058,18 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
         return FC_ECUDA;
     }
     const int N = a.GT <= 4 ? 16 : 32;  // 4 int8 or 3 bf16 limbs x GT heads, padded
-    const int stages = bf ? (a.GT == 8 ? tc_stages<true, 8>() : tc_stages<true, 4>()) : kTcStages;
+    const bool pg = a.pg != 0;
+    const int ng = pg ? 4 : 1;          // weight-limb tiles per buffer (scale groups)
+    const int stages = pg ? tc_stages<false, 4, true>()
+                     : bf ? (a.GT == 8 ? tc_stages<true, 8>() : tc_stages<true, 4>()) : kTcStages;
     const size_t bq_bytes = (size_t)N * 128 * (bf ? 2 : 1);
     size_t off = (size_t)stages * kTileBytes * (bf ? 2 : 1);
     a.off_bq = (int)off;
     off = align_to(off + bq_bytes, 1024);
     a.off_bw = (int)off;
-    off += 2 * bq_bytes;
+    off += 2 * ng * bq_bytes;
     a.off_xch = (int)off;
-    off = align_to(off + (size_t)(2 * 4 * (2 * a.GT + 1) + 4) * 4, 16);
+    off = align_to(off + (size_t)(2 * 4 * (a.GT + ng * a.GT + 1) + 4) * 4, 16);
     a.off_red = (int)off;
     off = align_to(off + (size_t)40 * 4, 16);
     a.off_scr = 0;  // merge scratch lives in the ring after the last tile
@@ -1015,6 +1102,17 @@ int launch_attn_tc(TcArgs &a, int64_t B, const void *krows, const void *vrows, i
     };
     auto by_s = [&](auto gt, int gi) {
         constexpr int GT = decltype(gt)::value;
+        if (pg) {
+            if constexpr (GT <= 4) {
+                switch (a.s) {
+                    case 1: go(attn_tc_kernel<GT, 1, false, false, true>, 48 + gi * 4 + 0); break;
+                    case 2: go(attn_tc_kernel<GT, 2, false, false, true>, 48 + gi * 4 + 1); break;
+                    case 4: go(attn_tc_kernel<GT, 4, false, false, true>, 48 + gi * 4 + 2); break;
+                    default: go(attn_tc_kernel<GT, 8, false, false, true>, 48 + gi * 4 + 3); break;
+                }
+            }
+            return;
+        }
         if (f16) {
             switch (a.s) {
                 case 1: go(attn_tc_kernel<GT, 1, true, true>, 32 + gi * 4 + 0); break;

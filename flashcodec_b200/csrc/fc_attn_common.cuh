@@ -131,6 +131,8 @@ struct TcArgs {
     const void *ksc, *vsc;
     int sc_dtype;
     int64_t ks_sb, ks_sh, ks_sn, vs_sb, vs_sh, vs_sn;
+    int64_t ks_sj, vs_sj;  // frequency stride of per-group scales (pg)
+    int pg;                // one fp32 scale per 32 channels (4 per row)
     const void *kraw, *vraw;
     int raw_dtype;
     int64_t kr_sb, kr_sh, kr_st, vr_sb, vr_sh, vr_st;

@@ -89,31 +89,75 @@ def test_grouped_stream_archive_read_and_attention(dt, D, r, k, group, sdt, S):
     check_close(out, ref, dt)
 
 
-def test_grouped_config2_shape_and_kernel_choice():
-    """A config-2 layer shape (bf16, r=8, K=4) in the per-32 format: attention
-    within the bar; forcing the tensor-core kernel (one scale per row only)
-    is refused."""
-    import bench
+def _grouped_streams(k, v, group, K=4, r=8):
     import flashcodec_b200 as fc
-    from flashcodec_b200 import _kernels as Kn
-    from test_gpu_attention import check_close, oracle_rows  # noqa: F401
-    k, v, q = bench.synth_case(2, 32, 8, 8 * 700 + 5, 128, 0.95, 44, device=DEV,
-                               dtype=torch.bfloat16)
-    kw = dict(block_size=8, keep_freqs=4, quant_bits=8, group_size=32)
+    kw = dict(block_size=r, keep_freqs=K, quant_bits=8, group_size=group)
     ks = fc._CodecStream(fc.make_codec("jpeg", **kw))
     vs = fc._CodecStream(fc.make_codec("jpeg", **kw))
     ks.append(k)
     vs.append(v)
-    out = fc.codec_decode_attention(q, ks, vs)
+    return ks, vs
+
+
+def _grouped_oracle(q, ks, vs):
+    import flashcodec_b200 as fc
     n = ks.n_blocks
     rows = {nm: orc.dequantize_grouped(st._coeffs[:, :, :n].cpu().numpy(), f32(st._scales[:, :, :n]))
             for nm, st in (("k", ks), ("v", vs))}
-    A = f32(fc.block_basis(ks.codec, 8))
-    ref = orc.decode_attention(f32(q), rows["k"], rows["v"], f32(ks.raw), f32(vs.raw), A)
-    check_close(out, ref, torch.bfloat16)
+    A = f32(fc.block_basis(ks.codec, ks.block_size))
+    raw = lambda st: f32(st.raw) if st.raw is not None else None  # noqa: E731
+    return orc.decode_attention(f32(q), rows["k"], rows["v"], raw(ks), raw(vs), A)
+
+
+def test_grouped_config2_shape_and_kernel_choice():
+    """A config-2 layer shape (bf16, r=8, K=4) in the per-32 format: the
+    default kernel, and the tensor-core kernel forced (its per-group form:
+    one fp32 scale per 32 channels at head dim 128), within the bar; forcing
+    the tensor-core kernel on a per-16 archive is refused."""
+    import bench
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as Kn
+    from test_gpu_attention import check_close
+    k, v, q = bench.synth_case(2, 32, 8, 8 * 700 + 5, 128, 0.95, 44, device=DEV,
+                               dtype=torch.bfloat16)
+    ks, vs = _grouped_streams(k, v, 32)
+    ref = _grouped_oracle(q, ks, vs)
+    check_close(fc.codec_decode_attention(q, ks, vs), ref, torch.bfloat16)
     prev = Kn.set_attn_kernel("tensor-core")
     try:
+        check_close(fc.codec_decode_attention(q, ks, vs), ref, torch.bfloat16)
+        ks16, vs16 = _grouped_streams(k, v, 16)
         with pytest.raises(NotImplementedError):
-            fc.codec_decode_attention(q, ks, vs)
+            fc.codec_decode_attention(q, ks16, vs16)
     finally:
         Kn.set_attn_kernel(prev)
+    assert Kn.attn_status(q.device) == 0
+
+
+@pytest.mark.parametrize("G,K,S,tail,B,Hk", [
+    (4, 4, 8 * 2000, 5, 2, 4),      # config-2 layer shape
+    (2, 2, 8 * 300, 3, 2, 4),       # s = 2
+    (1, 1, 8 * 70, 0, 2, 4),        # s = 1
+    (3, 8, 8 * 90, 7, 2, 4),        # s = 8, G not a power of 2
+    (4, 4, 8 * 20, 4, 2, 4),        # one split, partial tile
+    (4, 4, 8 * 9000, 1, 1, 1),      # one unit, many splits merged
+])
+def test_grouped_tensor_core_vs_cuda_core_vs_oracle(G, K, S, tail, B, Hk):
+    """Per-32 archives on the tensor-core kernel's per-group form and on the
+    CUDA-core kernel, both against the fp64 oracle of the dequantized rows."""
+    import bench
+    import flashcodec_b200 as fc
+    from flashcodec_b200 import _kernels as Kn
+    from test_gpu_attention import check_close
+    k, v, q = bench.synth_case(B, Hk * G, Hk, S + tail, 128, 0.95, 45, device=DEV,
+                               dtype=torch.bfloat16)
+    ks, vs = _grouped_streams(k, v, 32, K=K)
+    ref = _grouped_oracle(q, ks, vs)
+    prev = Kn.set_attn_kernel("auto")
+    try:
+        for which in ("tensor-core", "cuda-core"):
+            Kn.set_attn_kernel(which)
+            check_close(fc.codec_decode_attention(q, ks, vs), ref, torch.bfloat16)
+    finally:
+        Kn.set_attn_kernel(prev)
+    assert Kn.attn_status(q.device) == 0
