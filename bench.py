@@ -1052,7 +1052,8 @@ def main():
                          "frac": achieved / peak, "peak_kind": kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": per_launch,
                          "kernel_ms": kern_max,
-                         "kernel": "attn_tc_kernel" if cfg["codec"] in ("jpeg-int8", "jpeg-fp")
+                         "kernel": "attn_tc_kernel"
+                         if cfg["codec"] in ("jpeg-int8", "jpeg-int8-g32", "jpeg-fp")
                          else "attn_kernel"},
             "cpu_baseline": cpu,
             "e2e": {"value": tokens / (e_ms * 1e-3), "unit": "tokens/s",
