@@ -96,9 +96,23 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
 }
 
 // Instruction descriptor: int8 x int8 -> int32, M = 128, N, A K- or MN-major.
-__host__ __device__ constexpr uint32_t i8_idesc(int n, int a_mn_major) {
+__host__ __device__ constexpr uint32_t i8_idesc(int n, int a_mn_major, int b_mn_major = 0) {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn_major << 15) |
-           ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+           ((uint32_t)b_mn_major << 16) | ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor without swizzle for an N-major operand of
+// 16 int8 columns: row k of the tile is 16 contiguous bytes at 16 k, so core
+// matrices (8 rows x 16 bytes) follow each other every 128 bytes along K.
+// With 16 columns a single core matrix spans N and the N-direction stride is
+// never used; both stride fields are 128 bytes.
+__device__ __forceinline__ uint64_t mn16_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)(128 >> 4) << 16;
+    d |= (uint64_t)(128 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;
 }
 
 // Instruction descriptor: bf16 x bf16 (or fp16 x fp16 when f16) -> fp32,
@@ -328,7 +342,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
     const int y0 = (int)(n0 * S);
     const int slab = (int)(b * a.Hk + hk);
     const uint32_t idesc_s = BF ? bf16_idesc(N, 0, F16) : i8_idesc(N, 0);
-    const uint32_t idesc_o = BF ? bf16_idesc(N, 1, F16) : i8_idesc(N, 1);
+    // int8 weight limbs with N = 16 sit N-major (one 16-byte row per thread)
+    constexpr bool kWN = !BF && N == 16;
+    const uint32_t idesc_o = BF ? bf16_idesc(N, 1, F16) : i8_idesc(N, 1, kWN ? 1 : 0);
     // TMEM columns: 2 score buffers at [0, 2 SB), 2 output buffers after them
     constexpr int kAlloc = PG ? 256 : (N * 4 <= 64 ? 64 : 128);
 
@@ -508,7 +524,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 #pragma unroll
                             for (int k = 0; k < 4; k++)
                                 mma_i8(tmem + 2 * SB + (t & 1) * SB + gi * N, sw128_desc(at + k * 4096),
-                                       sw128_desc(bt + gi * BQ + k * 32), idesc_o, k > 0);
+                                       kWN ? mn16_desc(bt + gi * BQ + k * 512)
+                                           : sw128_desc(bt + gi * BQ + k * 32),
+                                       idesc_o, k > 0);
                     }
                     mma_commit(vdone + (t & 1));
                     if (!mbar_wait_bounded(vdone + (t & 1), (t >> 1) & 1, a.status, a.epoch)) return false;
@@ -752,11 +770,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
 #pragma unroll
                     for (int l = 0; l < 3; l++) bw16[sw128_off_bf(3 * g + l, lrow, N) / 2] = h[l];
                 }
-            } else {
+            } else if constexpr (kWN) {
+            // N-major weight tile: this row's 16 limb bytes (4 heads x 4 limbs,
+            // column 4 g + l = byte 4 g + l) as one 16-byte store per group
 #pragma unroll
-            for (int g = 0; g < GT; g++) {
+            for (int gi = 0; gi < NG; gi++) {
+              uint32_t pk[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-              for (int gi = 0; gi < NG; gi++) {
+              for (int g = 0; g < GT; g++) {
                 // x = w * 2^(132 + m_w - AX), |x| < 64.  The factor's exponent is
                 // clamped at 127, reached only when every weight of this warp is
                 // below 2^-121 (contributions under 2^-114 of the output scale).
@@ -771,12 +792,30 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ 
                 const float y2 = fmaf(d1, 128.0f, kRoundMagic);
                 const float d2 = fmaf(d1, 128.0f, -(y2 - kRoundMagic));
                 const float y3 = fmaf(d2, 128.0f, kRoundMagic);
-                unsigned char *bt8 = bwt + gi * BQ;
-                bt8[sw128_off(4 * g + 0, lrow)] = (unsigned char)__float_as_uint(y0);
-                bt8[sw128_off(4 * g + 1, lrow)] = (unsigned char)__float_as_uint(y1);
-                bt8[sw128_off(4 * g + 2, lrow)] = (unsigned char)__float_as_uint(y2);
-                bt8[sw128_off(4 * g + 3, lrow)] = (unsigned char)__float_as_uint(y3);
+                pk[g] = __byte_perm(__byte_perm(__float_as_uint(y0), __float_as_uint(y1), 0x0040),
+                                    __byte_perm(__float_as_uint(y2), __float_as_uint(y3), 0x0040),
+                                    0x5410);
               }
+              *reinterpret_cast<uint4 *>(bwt + gi * BQ + lrow * 16) =
+                  make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+            } else {
+#pragma unroll
+            for (int g = 0; g < GT; g++) {
+                // x = w * 2^(132 + m_w - AX), |x| < 64 (as above), K-major
+                // swizzled tile: one byte per limb row
+                const float x = w[g] * pow2_biased(259 + mw[g] - AX[g][0]);
+                const float y0 = x + kRoundMagic;
+                const float d0 = x - (y0 - kRoundMagic);
+                const float y1 = fmaf(d0, 128.0f, kRoundMagic);
+                const float d1 = fmaf(d0, 128.0f, -(y1 - kRoundMagic));
+                const float y2 = fmaf(d1, 128.0f, kRoundMagic);
+                const float d2 = fmaf(d1, 128.0f, -(y2 - kRoundMagic));
+                const float y3 = fmaf(d2, 128.0f, kRoundMagic);
+                bwt[sw128_off(4 * g + 0, lrow)] = (unsigned char)__float_as_uint(y0);
+                bwt[sw128_off(4 * g + 1, lrow)] = (unsigned char)__float_as_uint(y1);
+                bwt[sw128_off(4 * g + 2, lrow)] = (unsigned char)__float_as_uint(y2);
+                bwt[sw128_off(4 * g + 3, lrow)] = (unsigned char)__float_as_uint(y3);
             }
             }
             fence_async_smem();
