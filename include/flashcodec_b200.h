@@ -233,8 +233,10 @@ FC_API int fc_decode_attn(const void *q, int q_dtype, int64_t B, int64_t Hq, int
  * the reference).  k_scales / v_scales are (B, Hk, n_blocks, s, D /
  * scale_group) with strides *_sb, *_sh, *_sn, *_sj (frequency) and group
  * stride 1; scale_group must divide D.  The workspace is the one
- * fc_decode_attn_workspace_size reports for the same sizes.  Runs the
- * CUDA-core kernel (the tensor-core kernel takes one scale per row).
+ * fc_decode_attn_workspace_size reports for the same sizes.  With
+ * scale_group 32, fp32 scales, head dim 128, Hq/Hk <= 4, 16-byte aligned
+ * scales with frequency stride 4 and the tensor-core archive layout, it runs
+ * the tensor-core kernel's per-group form; otherwise the CUDA-core kernel.
  */
 FC_API int fc_decode_attn_grouped(const void *q, int q_dtype, int64_t B, int64_t Hq, int64_t D,
                    int64_t q_sb, int64_t q_sh, int64_t Hk, int64_t n_blocks, int s, int r,
@@ -422,8 +424,9 @@ FC_API int fc_decode_attn_masked(const void *q, int q_dtype, int64_t B, int64_t 
 
 /* Decode-attention kernel selection (process-wide; for tests and benchmarks).
  * AUTO uses the tcgen05 tensor-core kernel whenever the archive allows it
- * (contiguous (B, Hk, cap, s, 128) rows of int8 codes with one scale per row,
- * or of bf16 or fp16 coefficients without scales; block size 8 with s in
+ * (contiguous (B, Hk, cap, s, 128) rows of int8 codes with one scale per row
+ * or one fp32 scale per 32 channels (Hq/Hk <= 4), or of bf16 or fp16
+ * coefficients without scales; block size 8 with s in
  * {1, 2, 4, 8} stored rows per block, Hq/Hk <= 8) and the CUDA-core kernel
  * otherwise.  CUDA_CORE forces the CUDA-core kernel;
  * TENSOR_CORE makes unsupported layouts fail with FC_ENOTSUP instead of
